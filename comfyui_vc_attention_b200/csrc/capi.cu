@@ -1,0 +1,295 @@
+// extern "C" entry points of libvcattn.so (declared in include/vcattn.h).
+//
+// Each entry point validates its arguments on the host, honours host-side
+// fault injection, enqueues kernels on the caller's stream and returns a
+// status code.  No entry point allocates device memory.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "kernels.cuh"
+
+namespace vcattn {
+
+// ---------------------------------------------------------------------------
+// Standalone codec kernels (bit-exact tests of the in-kernel encoders).
+// ---------------------------------------------------------------------------
+__global__ void e4m3_encode_kernel(const float* __restrict__ x, int64_t n, uint8_t* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = static_cast<uint8_t>(e4m3x2(x[i], 0.f) & 0xff);
+}
+
+__global__ void fp4_encode_kernel(const float* __restrict__ x, int64_t n, uint8_t* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = static_cast<uint8_t>(e2m1x2(x[i], 0.f) & 0xf);
+}
+
+// mode 1: the operation sequence of expcast.py:67-69; mode 0: one FMA per
+// element with the per-row bias folded, c = fma(s, 8*log2e, 64 + 56 + beta -
+// 8*log2e*m), which is the form the attention kernel evaluates.
+__global__ void expcast_kernel(const float* __restrict__ s, const float* __restrict__ m, int rows, int cols,
+                               float c0, float c120, int mode, uint8_t* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(rows) * cols) return;
+  const int r = static_cast<int>(i / cols);
+  const float sv = s[i], mv = m[r];
+  float c;
+  if (mode == 1) {
+    const float u = __fadd_rn(__fmul_rn(__fsub_rn(sv, mv), kLog2e), 8.0f);
+    c = __fmaf_rn(u, 8.0f, c0);
+  } else {
+    const float k8 = 8.0f * kLog2e;
+    c = __fmaf_rn(sv, k8, __fmaf_rn(-k8, mv, c120));
+  }
+  c = fminf(fmaxf(rintf(c), 0.0f), 120.0f);
+  out[i] = static_cast<uint8_t>(c);
+}
+
+cudaError_t launch_codecs_e4m3(const float* x, int64_t n, uint8_t* out, cudaStream_t st) {
+  if (n > 0) e4m3_encode_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(x, n, out);
+  return cudaGetLastError();
+}
+cudaError_t launch_codecs_fp4(const float* x, int64_t n, uint8_t* out, cudaStream_t st) {
+  if (n > 0) fp4_encode_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(x, n, out);
+  return cudaGetLastError();
+}
+cudaError_t launch_expcast(const float* s, const float* m, int rows, int cols, double beta, int mode,
+                           uint8_t* out, cudaStream_t st) {
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  const float c0 = static_cast<float>(56.0 + beta);
+  const float c120 = static_cast<float>(64.0 + 56.0 + beta);
+  if (n > 0) expcast_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(s, m, rows, cols, c0, c120, mode, out);
+  return cudaGetLastError();
+}
+
+}  // namespace vcattn
+
+using namespace vcattn;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::mutex g_inject_mu;
+std::string g_inject;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return VCATTN_OK;
+  return fail(VCATTN_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+bool injected(const char* name) {
+  std::lock_guard<std::mutex> lk(g_inject_mu);
+  return !g_inject.empty() && g_inject == name;
+}
+
+int elem_size(int dtype) { return dtype == VCATTN_DTYPE_F32 ? 4 : 2; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Views are read with 16-byte (kmeans rows) or 8/16-byte (prepare) vector
+// loads: base 16-byte aligned and every stride a multiple of 16 bytes.
+bool view_ok(const vcattn_bhnd* v, int dtype) {
+  if (v == nullptr || v->data == nullptr || !aligned16(v->data)) return false;
+  const int64_t q = 16 / elem_size(dtype);
+  return (v->sb % q) == 0 && (v->sh % q) == 0 && (v->sn % q) == 0;
+}
+
+bool dtype_ok(int dtype) {
+  return dtype == VCATTN_DTYPE_BF16 || dtype == VCATTN_DTYPE_F16 || dtype == VCATTN_DTYPE_F32;
+}
+
+#define VC_CHECK(cond, msg) \
+  do {                      \
+    if (!(cond)) return fail(VCATTN_ERR_ARG, msg); \
+  } while (0)
+
+}  // namespace
+
+extern "C" {
+
+int vcattn_abi_version(void) { return 1; }
+
+const char* vcattn_last_error(void) { return g_last_error.c_str(); }
+
+void vcattn_inject_fault(const char* entry_point) {
+  std::lock_guard<std::mutex> lk(g_inject_mu);
+  g_inject = entry_point ? entry_point : "";
+}
+
+size_t vcattn_kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys) {
+  if (G <= 0 || N <= 0 || D <= 0 || k <= 0) return 0;
+  return kmeans_workspace_bytes(G, N, D, k, nkeys);
+}
+
+int vcattn_kmeans(const vcattn_bhnd* v, int dtype, int B, int H, int N, int D, int k, int iters,
+                  const uint16_t* warm_centroids, const int32_t* key_offset, int nkeys,
+                  uint16_t* centroids_out, int32_t* perm_out, int32_t* labels_out, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_kmeans")) return fail(VCATTN_ERR_INJECTED, "vcattn_kmeans: injected fault");
+  VC_CHECK(dtype_ok(dtype), "vcattn_kmeans: unsupported dtype");
+  VC_CHECK(D == 64 || D == 128, "vcattn_kmeans: D must be 64 or 128");
+  VC_CHECK(B > 0 && H > 0 && N > 0, "vcattn_kmeans: empty shape");
+  VC_CHECK(k >= 1 && k <= N && k <= 4096, "vcattn_kmeans: need 1 <= k <= min(N, 4096)");
+  VC_CHECK(iters >= 0 && iters <= 1000, "vcattn_kmeans: iters out of range");
+  VC_CHECK(view_ok(v, dtype), "vcattn_kmeans: v must be 16-byte aligned with 16-byte multiple strides");
+  VC_CHECK(centroids_out && perm_out, "vcattn_kmeans: null output");
+  VC_CHECK(key_offset == nullptr || nkeys >= k, "vcattn_kmeans: nkeys must be >= k");
+  const int G = B * H;
+  const size_t need = kmeans_workspace_bytes(G, N, D, k, key_offset ? nkeys : k);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(VCATTN_ERR_WORKSPACE, "vcattn_kmeans: workspace too small (need " + std::to_string(need) + " bytes)");
+  VC_CHECK(aligned16(workspace), "vcattn_kmeans: workspace must be 16-byte aligned");
+  KMeansParams p{};
+  p.v = v; p.dtype = dtype; p.B = B; p.H = H; p.N = N; p.D = D; p.k = k; p.iters = iters;
+  p.warm = warm_centroids; p.key_offset = key_offset; p.nkeys = key_offset ? nkeys : k;
+  p.centroids_out = centroids_out; p.perm_out = perm_out; p.labels_out = labels_out;
+  p.workspace = workspace;
+  return cuda_status(launch_kmeans(p, static_cast<cudaStream_t>(stream)), "vcattn_kmeans");
+}
+
+size_t vcattn_prepare_workspace_bytes(int G, int N, int D) {
+  if (G <= 0 || N <= 0 || D <= 0) return 0;
+  return prepare_workspace_bytes(G, N, D);
+}
+
+int vcattn_prepare_fp8(const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_bhnd* v, int dtype, int B,
+                       int H, int N, int D, const int32_t* perm, int perm_rows, int block_rows, int flags,
+                       uint8_t* q8, float* q_scale, uint8_t* k8, float* k_scale, uint8_t* v8,
+                       float* v_scale, float* mu, uint8_t* v8t, const vcattn_route_stats* route,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_prepare_fp8")) return fail(VCATTN_ERR_INJECTED, "vcattn_prepare_fp8: injected fault");
+  VC_CHECK(dtype_ok(dtype), "vcattn_prepare_fp8: unsupported dtype");
+  VC_CHECK(D == 64 || D == 128, "vcattn_prepare_fp8: D must be 64 or 128");
+  VC_CHECK(B > 0 && H > 0 && N > 0, "vcattn_prepare_fp8: empty shape");
+  VC_CHECK(block_rows == 64 || block_rows == 128, "vcattn_prepare_fp8: block_rows must be 64 or 128");
+  VC_CHECK(view_ok(q, dtype) && view_ok(k, dtype) && view_ok(v, dtype),
+           "vcattn_prepare_fp8: q/k/v must be 16-byte aligned with 16-byte multiple strides");
+  VC_CHECK(perm == nullptr || perm_rows == 1 || perm_rows == B * H, "vcattn_prepare_fp8: perm_rows must be 1 or G");
+  VC_CHECK(q8 && q_scale && k8 && k_scale && v_scale && mu && (v8 || v8t), "vcattn_prepare_fp8: null output");
+  VC_CHECK(aligned16(q8) && aligned16(k8) && (v8 == nullptr || aligned16(v8)) && (v8t == nullptr || aligned16(v8t)),
+           "vcattn_prepare_fp8: code buffers must be 16-byte aligned");
+  const int G = B * H;
+  const int n_pad = (N + block_rows - 1) / block_rows * block_rows;
+  if (route) {
+    VC_CHECK(route->q_block == 64 || route->q_block == 128, "vcattn_prepare_fp8: route q_block must be 64 or 128");
+    VC_CHECK(n_pad % route->q_block == 0, "vcattn_prepare_fp8: n_pad must be a multiple of q_block");
+  }
+  const size_t need = prepare_workspace_bytes(G, N, D);
+  if ((flags & VCATTN_SMOOTH_K) && (workspace == nullptr || workspace_bytes < need))
+    return fail(VCATTN_ERR_WORKSPACE, "vcattn_prepare_fp8: workspace too small (need " + std::to_string(need) + " bytes)");
+  PrepareParams p{};
+  p.q = q; p.k = k; p.v = v; p.dtype = dtype; p.B = B; p.H = H; p.N = N; p.D = D; p.n_pad = n_pad;
+  p.block_rows = block_rows; p.flags = flags; p.perm = perm; p.perm_rows = perm ? perm_rows : 0;
+  p.q8 = q8; p.k8 = k8; p.v8 = v8; p.v8t = v8t;
+  p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
+  p.v_mean = route ? route->v_mean : nullptr;
+  p.route = route; p.workspace = workspace;
+  return cuda_status(launch_prepare(p, static_cast<cudaStream_t>(stream)), "vcattn_prepare_fp8");
+}
+
+int vcattn_route_mask(const vcattn_route_stats* route, int G, int N, int n_pad, int D, int block_rows, float tau,
+                      int local_blocks, int sink_blocks, float sm_scale, uint8_t* keep, float* thresh,
+                      void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_route_mask")) return fail(VCATTN_ERR_INJECTED, "vcattn_route_mask: injected fault");
+  VC_CHECK(route && route->k_mean && route->q_cent && route->q_bar, "vcattn_route_mask: missing statistics");
+  VC_CHECK(D == 64 || D == 128, "vcattn_route_mask: D must be 64 or 128");
+  VC_CHECK(block_rows == 64 || block_rows == 128, "vcattn_route_mask: block_rows must be 64 or 128");
+  VC_CHECK(route->q_block > 0 && n_pad % route->q_block == 0 && n_pad % block_rows == 0,
+           "vcattn_route_mask: inconsistent padding");
+  VC_CHECK(keep != nullptr, "vcattn_route_mask: null keep");
+  RouteParams p{};
+  p.k_mean = route->k_mean; p.q_cent = route->q_cent; p.q_bar = route->q_bar;
+  p.G = G; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows; p.q_block = route->q_block;
+  p.tau = tau; p.sm_scale = sm_scale; p.local_blocks = local_blocks; p.sink_blocks = sink_blocks;
+  p.keep = keep; p.thresh = thresh;
+  return cuda_status(launch_route_mask(p, static_cast<cudaStream_t>(stream)), "vcattn_route_mask");
+}
+
+static int attn_common_checks(const char* name, const uint8_t* q8, const float* q_scale, const uint8_t* k8,
+                              const float* k_scale, const uint8_t* v8t, const float* v_scale, const float* mu,
+                              int B, int H, int N, int n_pad, int D, int block_rows, void* out, int out_dtype) {
+  const std::string n(name);
+  VC_CHECK(q8 && q_scale && k8 && k_scale && v8t && v_scale && mu && out, n + ": null pointer");
+  VC_CHECK(D == 64 || D == 128, n + ": D must be 64 or 128");
+  VC_CHECK(block_rows == 64 || block_rows == 128, n + ": block_rows must be 64 or 128");
+  VC_CHECK(B > 0 && H > 0 && N > 0, n + ": empty shape");
+  VC_CHECK(n_pad >= N && n_pad % block_rows == 0 && n_pad - N < block_rows, n + ": n_pad inconsistent with N");
+  VC_CHECK(dtype_ok(out_dtype), n + ": unsupported output dtype");
+  VC_CHECK(aligned16(q8) && aligned16(k8) && aligned16(v8t) && aligned16(k_scale) && aligned16(v_scale) &&
+               aligned16(mu),
+           n + ": operand buffers must be 16-byte aligned");
+  return VCATTN_OK;
+}
+
+int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
+                    const uint8_t* v8t, const float* v_scale, const float* mu, int B, int H, int N, int n_pad,
+                    int D, int block_rows, float sm_scale, int flags, double expcast_beta, void* out,
+                    int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn, void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_attn_fp8")) return fail(VCATTN_ERR_INJECTED, "vcattn_attn_fp8: injected fault");
+  const int rc = attn_common_checks("vcattn_attn_fp8", q8, q_scale, k8, k_scale, v8t, v_scale, mu, B, H, N, n_pad,
+                                    D, block_rows, out, out_dtype);
+  if (rc != VCATTN_OK) return rc;
+  AttnParams p{};
+  p.q8 = q8; p.k8 = k8; p.v8t = v8t; p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
+  p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
+  p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
+  p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
+  return cuda_status(launch_attn_mma(p, static_cast<cudaStream_t>(stream)), "vcattn_attn_fp8");
+}
+
+int vcattn_attn_fp8_sparse(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
+                           const uint8_t* v8t, const float* v_scale, const float* mu, const float* k_mean,
+                           const float* v_mean, const uint8_t* keep, int q_block, int group, int B, int H,
+                           int N, int n_pad, int D, int block_rows, float sm_scale, int flags,
+                           double expcast_beta, void* out, int out_dtype, int64_t out_sb, int64_t out_sh,
+                           int64_t out_sn, void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_attn_fp8_sparse")) return fail(VCATTN_ERR_INJECTED, "vcattn_attn_fp8_sparse: injected fault");
+  const int rc = attn_common_checks("vcattn_attn_fp8_sparse", q8, q_scale, k8, k_scale, v8t, v_scale, mu, B, H, N,
+                                    n_pad, D, block_rows, out, out_dtype);
+  if (rc != VCATTN_OK) return rc;
+  VC_CHECK(k_mean && v_mean && keep, "vcattn_attn_fp8_sparse: missing routing inputs");
+  VC_CHECK(q_block == 64 && n_pad % q_block == 0, "vcattn_attn_fp8_sparse: q_block must be 64");
+  VC_CHECK(group >= 1 && group <= 64, "vcattn_attn_fp8_sparse: group out of range");
+  AttnParams p{};
+  p.q8 = q8; p.k8 = k8; p.v8t = v8t; p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
+  p.k_mean = k_mean; p.v_mean = v_mean; p.keep = keep; p.q_block = q_block; p.group = group;
+  p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
+  p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
+  p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
+  return cuda_status(launch_attn_sparse_mma(p, static_cast<cudaStream_t>(stream)), "vcattn_attn_fp8_sparse");
+}
+
+int vcattn_e4m3_encode(const float* x, int64_t n, uint8_t* out, void* stream) {
+  g_last_error.clear();
+  VC_CHECK(n >= 0 && (n == 0 || (x && out)), "vcattn_e4m3_encode: bad arguments");
+  return cuda_status(launch_codecs_e4m3(x, n, out, static_cast<cudaStream_t>(stream)), "vcattn_e4m3_encode");
+}
+
+int vcattn_fp4_encode(const float* x, int64_t n, uint8_t* out, void* stream) {
+  g_last_error.clear();
+  VC_CHECK(n >= 0 && (n == 0 || (x && out)), "vcattn_fp4_encode: bad arguments");
+  return cuda_status(launch_codecs_fp4(x, n, out, static_cast<cudaStream_t>(stream)), "vcattn_fp4_encode");
+}
+
+int vcattn_expcast_codes(const float* s, const float* m, int rows, int cols, double beta, int mode, uint8_t* out,
+                         void* stream) {
+  g_last_error.clear();
+  VC_CHECK(rows >= 0 && cols >= 0 && (rows * static_cast<int64_t>(cols) == 0 || (s && m && out)),
+           "vcattn_expcast_codes: bad arguments");
+  VC_CHECK(mode == 0 || mode == 1, "vcattn_expcast_codes: mode must be 0 or 1");
+  return cuda_status(launch_expcast(s, m, rows, cols, beta, mode, out, static_cast<cudaStream_t>(stream)),
+                     "vcattn_expcast_codes");
+}
+
+}  // extern "C"

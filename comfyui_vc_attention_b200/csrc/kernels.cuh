@@ -1,0 +1,69 @@
+// Internal launcher interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace vcattn {
+
+struct PrepareParams {
+  const vcattn_bhnd *q, *k, *v;
+  int dtype, B, H, N, D, n_pad, block_rows, flags;
+  const int32_t* perm;
+  int perm_rows;
+  uint8_t *q8, *k8, *v8, *v8t;
+  float *q_scale, *k_scale, *v_scale, *mu, *v_mean;
+  const vcattn_route_stats* route;
+  void* workspace;
+};
+
+struct RouteParams {
+  const float *k_mean, *q_cent, *q_bar;
+  int G, N, n_pad, D, block_rows, q_block;
+  float tau, sm_scale;
+  int local_blocks, sink_blocks;
+  uint8_t* keep;
+  float* thresh;
+};
+
+struct KMeansParams {
+  const vcattn_bhnd* v;
+  int dtype, B, H, N, D, k, iters;
+  const uint16_t* warm;
+  const int32_t* key_offset;
+  int nkeys;
+  uint16_t* centroids_out;
+  int32_t* perm_out;
+  int32_t* labels_out;
+  void* workspace;
+};
+
+struct AttnParams {
+  const uint8_t *q8, *k8, *v8, *v8t;
+  const float *q_scale, *k_scale, *v_scale, *mu;
+  // block-sparse extras (nullptr for the dense kernel)
+  const float *k_mean, *v_mean;
+  const uint8_t* keep;
+  int q_block, group;
+  int B, H, N, n_pad, D, block_rows;
+  float sm_scale;
+  double beta;
+  int flags;
+  void* out;
+  int out_dtype;
+  int64_t osb, osh, osn;
+};
+
+size_t prepare_workspace_bytes(int G, int N, int D);
+size_t kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys);
+
+cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t st);
+cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st);
+cudaError_t launch_kmeans(const KMeansParams& p, cudaStream_t st);
+cudaError_t launch_attn_mma(const AttnParams& p, cudaStream_t st);
+cudaError_t launch_attn_sparse_mma(const AttnParams& p, cudaStream_t st);
+cudaError_t launch_codecs_e4m3(const float* x, int64_t n, uint8_t* out, cudaStream_t st);
+cudaError_t launch_codecs_fp4(const float* x, int64_t n, uint8_t* out, cudaStream_t st);
+cudaError_t launch_expcast(const float* s, const float* m, int rows, int cols, double beta, int mode,
+                           uint8_t* out, cudaStream_t st);
+
+}  // namespace vcattn

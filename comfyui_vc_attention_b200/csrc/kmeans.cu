@@ -1,0 +1,332 @@
+// V-Smooth k-means grouping and the stable label sort that yields the
+// permutation (grouping.py:71-186).
+//
+// Arithmetic is fixed so that labels, centroids and the permutation are bit
+// exact against the CPU restatement:
+//   * assignment: the bf16 GEMM of grouping.py:98 is a per-(token, centroid)
+//     fp32 FMA chain over channels in increasing order (bf16 products are
+//     exact, so this equals a sequential fp32 sum), rounded to bf16, times 2,
+//     minus |c|^2 (sequential fp32), first argmax;
+//   * update: fp32 sums in token order, which is what index_add_ does
+//     (grouping.py:277-278), then / count and bf16 rounding;
+//   * sort: a stable counting sort over (key, 32-token chunk) pairs.
+#include "kernels.cuh"
+
+namespace vcattn {
+
+namespace {
+
+constexpr int kChunk = 32;        // tokens per counting-sort chunk (one warp)
+constexpr int kAssignThreads = 128;
+constexpr int kCentTile = 64;     // centroids staged in shared memory per pass
+
+struct KmWs {
+  int32_t* labels;
+  int32_t* counts;
+  int32_t* offsets;
+  float* cent;
+  float* seeds;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+KmWs carve(void* base, int G, int N, int D, int k, int nkeys) {
+  const size_t nchunks = (N + kChunk - 1) / kChunk;
+  const size_t nk = static_cast<size_t>(nkeys > k ? nkeys : k);
+  char* p = static_cast<char*>(base);
+  KmWs w;
+  w.labels = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * G * static_cast<size_t>(N));
+  w.counts = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * G * nk * nchunks);
+  w.offsets = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * G * nk * nchunks);
+  w.cent = reinterpret_cast<float*>(p); p += align256(sizeof(float) * G * static_cast<size_t>(k) * D);
+  w.seeds = reinterpret_cast<float*>(p);
+  return w;
+}
+
+template <int DT>
+__device__ __forceinline__ float load_bf16_value(const vcattn_bhnd& v, int b, int h, int t, int d) {
+  const int64_t off = b * v.sb + h * v.sh + static_cast<int64_t>(t) * v.sn + d;
+  if constexpr (DT == VCATTN_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(v.data)[off]);
+  else if constexpr (DT == VCATTN_DTYPE_F16) return bf16_round(__half2float(static_cast<const __half*>(v.data)[off]));
+  else return bf16_round(static_cast<const float*>(v.data)[off]);
+}
+
+// grouping.py:71-83: centroid c = bf16(mean of the samples at
+// round(linspace(0, N-1, m))[c*m_per : (c+1)*m_per]).
+template <int DT>
+__global__ void seed_kernel(vcattn_bhnd v, int H, int N, int D, int k, int m, int m_per,
+                            float* seeds, float* cent, const uint16_t* warm) {
+  const int g = blockIdx.y, c = blockIdx.x, d = threadIdx.x;
+  if (d >= D) return;
+  const int b = g / H, h = g % H;
+  float step = 0.f;
+  if (m > 1) step = __fdiv_rn(static_cast<float>(N - 1), static_cast<float>(m - 1));
+  double s = 0.0;
+  for (int i = 0; i < m_per; ++i) {
+    const int pos = c * m_per + i;
+    int idx = 0;
+    if (m > 1) {
+      const float f = (pos < m / 2) ? __fmaf_rn(step, static_cast<float>(pos), 0.0f)
+                                    : __fmaf_rn(-step, static_cast<float>(m - 1 - pos), static_cast<float>(N - 1));
+      idx = static_cast<int>(rintf(f));
+    }
+    s += static_cast<double>(load_bf16_value<DT>(v, b, h, idx, d));
+  }
+  const float mean = bf16_round(__fdiv_rn(__double2float_rn(s), static_cast<float>(m_per)));
+  const int64_t o = (static_cast<int64_t>(g) * k + c) * D + d;
+  seeds[o] = mean;
+  cent[o] = warm ? bf16_bits_to_float(warm[o]) : mean;
+}
+
+// Row of D bf16 values packed two per register.
+template <int DT, int D>
+__device__ __forceinline__ void load_row_bf16x2(const vcattn_bhnd& v, int b, int h, int t, uint32_t (&r)[D / 2]) {
+  const int64_t off = b * v.sb + h * v.sh + static_cast<int64_t>(t) * v.sn;
+  if constexpr (DT == VCATTN_DTYPE_BF16) {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(v.data) + off);
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      const uint4 x = p[i];
+      r[4 * i + 0] = x.x; r[4 * i + 1] = x.y; r[4 * i + 2] = x.z; r[4 * i + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < D / 2; ++i) {
+      float lo, hi;
+      if constexpr (DT == VCATTN_DTYPE_F16) {
+        const __half* p = static_cast<const __half*>(v.data) + off;
+        lo = __half2float(p[2 * i]); hi = __half2float(p[2 * i + 1]);
+      } else {
+        const float* p = static_cast<const float*>(v.data) + off;
+        lo = p[2 * i]; hi = p[2 * i + 1];
+      }
+      const uint32_t bl = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+      const uint32_t bh = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+      r[i] = bl | (bh << 16);
+    }
+  }
+}
+
+// grouping.py:86-100: nearest centroid per token (one thread per token), then
+// per-warp counts of the sort key for the stable counting sort.
+template <int DT, int D>
+__global__ void __launch_bounds__(kAssignThreads) assign_kernel(
+    vcattn_bhnd v, int H, int N, int k, const float* __restrict__ cent,
+    int32_t* __restrict__ labels, const int32_t* __restrict__ key_offset, int nkeys, int nchunks,
+    int32_t* __restrict__ counts) {
+  __shared__ __align__(16) float cT[D][kCentTile];   // channel-major centroid tile
+  __shared__ float c2[kCentTile];
+  const int g = blockIdx.y;
+  const int b = g / H, h = g % H;
+  const int t = blockIdx.x * kAssignThreads + threadIdx.x;
+  const bool live = t < N;
+  uint32_t row[D / 2];
+  if (live) load_row_bf16x2<DT, D>(v, b, h, t, row);
+  else {
+#pragma unroll
+    for (int i = 0; i < D / 2; ++i) row[i] = 0u;
+  }
+  float best = -INFINITY;
+  int label = 0;
+  for (int c0 = 0; c0 < k; c0 += kCentTile) {
+    const int nc = min(kCentTile, k - c0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kCentTile * D; i += kAssignThreads) {
+      const int c = i / D, d = i % D;
+      cT[d][c] = (c < nc) ? cent[(static_cast<int64_t>(g) * k + c0 + c) * D + d] : 0.f;
+    }
+    __syncthreads();
+    if (threadIdx.x < kCentTile) {
+      float acc = 0.f;
+      for (int d = 0; d < D; ++d) acc = __fmaf_rn(cT[d][threadIdx.x], cT[d][threadIdx.x], acc);
+      c2[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    for (int cc = 0; cc < nc; cc += 8) {
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < D / 2; ++i) {
+        const float v0 = __uint_as_float(row[i] << 16);
+        const float v1 = __uint_as_float(row[i] & 0xffff0000u);
+        const float4 a0 = *reinterpret_cast<const float4*>(&cT[2 * i][cc]);
+        const float4 a1 = *reinterpret_cast<const float4*>(&cT[2 * i][cc + 4]);
+        const float4 b0 = *reinterpret_cast<const float4*>(&cT[2 * i + 1][cc]);
+        const float4 b1 = *reinterpret_cast<const float4*>(&cT[2 * i + 1][cc + 4]);
+        acc[0] = __fmaf_rn(v0, a0.x, acc[0]); acc[1] = __fmaf_rn(v0, a0.y, acc[1]);
+        acc[2] = __fmaf_rn(v0, a0.z, acc[2]); acc[3] = __fmaf_rn(v0, a0.w, acc[3]);
+        acc[4] = __fmaf_rn(v0, a1.x, acc[4]); acc[5] = __fmaf_rn(v0, a1.y, acc[5]);
+        acc[6] = __fmaf_rn(v0, a1.z, acc[6]); acc[7] = __fmaf_rn(v0, a1.w, acc[7]);
+        acc[0] = __fmaf_rn(v1, b0.x, acc[0]); acc[1] = __fmaf_rn(v1, b0.y, acc[1]);
+        acc[2] = __fmaf_rn(v1, b0.z, acc[2]); acc[3] = __fmaf_rn(v1, b0.w, acc[3]);
+        acc[4] = __fmaf_rn(v1, b1.x, acc[4]); acc[5] = __fmaf_rn(v1, b1.y, acc[5]);
+        acc[6] = __fmaf_rn(v1, b1.z, acc[6]); acc[7] = __fmaf_rn(v1, b1.w, acc[7]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (cc + j < nc) {
+          const float sim = __fsub_rn(__fmul_rn(bf16_round(acc[j]), 2.0f), c2[cc + j]);
+          if (sim > best) { best = sim; label = c0 + cc + j; }
+        }
+      }
+    }
+  }
+  // Counting-sort histogram: one chunk per warp.
+  const unsigned live_mask = __ballot_sync(0xffffffffu, live);
+  if (live) {
+    labels[static_cast<int64_t>(g) * N + t] = label;
+    const int key = label + (key_offset ? key_offset[t] : 0);
+    const unsigned same = __match_any_sync(live_mask, key);
+    const int lane = threadIdx.x & 31;
+    // Keys outside [0, nkeys) (a malformed key_offset) are dropped, never written.
+    if ((same & ((1u << lane) - 1u)) == 0u && key >= 0 && key < nkeys) {
+      const int chunk = t / kChunk;
+      counts[(static_cast<int64_t>(g) * nkeys + key) * nchunks + chunk] = __popc(same);
+    }
+  }
+}
+
+// Exclusive scan of counts[g] in (key, chunk) order: one CTA per head.
+__global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ counts,
+                                                    int32_t* __restrict__ offsets, int64_t len) {
+  __shared__ int32_t part[1024];
+  const int g = blockIdx.x;
+  const int32_t* c = counts + static_cast<int64_t>(g) * len;
+  int32_t* o = offsets + static_cast<int64_t>(g) * len;
+  const int64_t per = (len + blockDim.x - 1) / blockDim.x;
+  const int64_t s = threadIdx.x * per;
+  const int64_t e = min(len, s + per);
+  int32_t local = 0;
+  for (int64_t i = s; i < e; ++i) local += c[i];
+  part[threadIdx.x] = local;
+  __syncthreads();
+  // Hillis-Steele inclusive scan over the 1024 partial sums.
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int32_t x = (threadIdx.x >= off) ? part[threadIdx.x - off] : 0;
+    __syncthreads();
+    part[threadIdx.x] += x;
+    __syncthreads();
+  }
+  int32_t run = part[threadIdx.x] - local;
+  for (int64_t i = s; i < e; ++i) {
+    o[i] = run;
+    run += c[i];
+  }
+}
+
+// Stable scatter: position = offset(key, chunk) + rank among equal keys in the warp.
+__global__ void __launch_bounds__(kAssignThreads) scatter_kernel(
+    const int32_t* __restrict__ labels, const int32_t* __restrict__ key_offset, int N, int nkeys,
+    int nchunks, const int32_t* __restrict__ offsets, int32_t* __restrict__ sorted) {
+  const int g = blockIdx.y;
+  const int t = blockIdx.x * kAssignThreads + threadIdx.x;
+  const bool live = t < N;
+  const unsigned live_mask = __ballot_sync(0xffffffffu, live);
+  if (!live) return;
+  const int key = labels[static_cast<int64_t>(g) * N + t] + (key_offset ? key_offset[t] : 0);
+  const unsigned same = __match_any_sync(live_mask, key);
+  const int lane = threadIdx.x & 31;
+  const int rank = __popc(same & ((1u << lane) - 1u));
+  if (key < 0 || key >= nkeys) return;
+  const int pos = offsets[(static_cast<int64_t>(g) * nkeys + key) * nchunks + t / kChunk] + rank;
+  if (pos >= 0 && pos < N) sorted[static_cast<int64_t>(g) * N + pos] = t;
+}
+
+// grouping.py:103-124: fp32 sums in token order, / max(count, 1), re-seed
+// clusters with count <= 1, bf16.  One CTA per (cluster, head), thread = channel.
+template <int DT>
+__global__ void update_kernel(vcattn_bhnd v, int H, int N, int D, int k, int nchunks,
+                              const int32_t* __restrict__ offsets, const int32_t* __restrict__ sorted,
+                              const float* __restrict__ seeds, float* __restrict__ cent,
+                              uint16_t* __restrict__ cent_out) {
+  const int g = blockIdx.y, c = blockIdx.x, d = threadIdx.x;
+  if (d >= D) return;
+  const int b = g / H, h = g % H;
+  const int64_t base = static_cast<int64_t>(g) * k * nchunks;
+  const int start = offsets[base + static_cast<int64_t>(c) * nchunks];
+  const int end = (c + 1 < k) ? offsets[base + static_cast<int64_t>(c + 1) * nchunks] : N;
+  const int32_t* mem = sorted + static_cast<int64_t>(g) * N;
+  float acc = 0.f;
+  int i = start;
+  for (; i + 4 <= end; i += 4) {
+    const float x0 = load_bf16_value<DT>(v, b, h, mem[i], d);
+    const float x1 = load_bf16_value<DT>(v, b, h, mem[i + 1], d);
+    const float x2 = load_bf16_value<DT>(v, b, h, mem[i + 2], d);
+    const float x3 = load_bf16_value<DT>(v, b, h, mem[i + 3], d);
+    acc = __fadd_rn(acc, x0); acc = __fadd_rn(acc, x1);
+    acc = __fadd_rn(acc, x2); acc = __fadd_rn(acc, x3);
+  }
+  for (; i < end; ++i) acc = __fadd_rn(acc, load_bf16_value<DT>(v, b, h, mem[i], d));
+  const int cnt = end - start;
+  const int64_t o = (static_cast<int64_t>(g) * k + c) * D + d;
+  const float cntc = static_cast<float>(cnt > 1 ? cnt : 1);
+  const float nv = (cnt <= 1) ? seeds[o] : bf16_round(__fdiv_rn(acc, cntc));
+  cent[o] = nv;
+  if (cent_out) cent_out[o] = __bfloat16_as_ushort(__float2bfloat16_rn(nv));
+}
+
+__global__ void copy_centroids_kernel(const float* __restrict__ cent, uint16_t* __restrict__ out, int64_t n) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(cent[i]));
+}
+
+template <int DT, int D>
+cudaError_t kmeans_impl(const KMeansParams& p, cudaStream_t st) {
+  const int G = p.B * p.H;
+  const int k = p.k;
+  const int nkeys = p.key_offset ? p.nkeys : k;
+  const int nchunks = (p.N + kChunk - 1) / kChunk;
+  KmWs w = carve(p.workspace, G, p.N, D, k, nkeys);
+  int32_t* labels = p.labels_out ? p.labels_out : w.labels;
+  const int m = (p.N < 4 * k) ? p.N : 4 * k;          // init_samples_per_centroid = 4
+  const int m_per = (m / k) > 1 ? (m / k) : 1;
+  seed_kernel<DT><<<dim3(k, G), D, 0, st>>>(*p.v, p.H, p.N, D, k, m, m_per, w.seeds, w.cent, p.warm);
+  const dim3 agrid((p.N + kAssignThreads - 1) / kAssignThreads, G, 1);
+  auto sort_pass = [&](const int32_t* koff, int nkey, int32_t* out_sorted) {
+    const size_t cnt_bytes = sizeof(int32_t) * static_cast<size_t>(G) * nkey * nchunks;
+    cudaMemsetAsync(w.counts, 0, cnt_bytes, st);
+    assign_kernel<DT, D><<<agrid, kAssignThreads, 0, st>>>(
+        *p.v, p.H, p.N, k, w.cent, labels, koff, nkey, nchunks, w.counts);
+    scan_kernel<<<G, 1024, 0, st>>>(w.counts, w.offsets, static_cast<int64_t>(nkey) * nchunks);
+    scatter_kernel<<<dim3(agrid.x, G), kAssignThreads, 0, st>>>(labels, koff, p.N, nkey, nchunks,
+                                                              w.offsets, out_sorted);
+  };
+  const int iters = p.iters;
+  for (int it = 0; it < iters; ++it) {
+    sort_pass(nullptr, k, p.perm_out);
+    update_kernel<DT><<<dim3(k, G), D, 0, st>>>(*p.v, p.H, p.N, D, k, nchunks, w.offsets, p.perm_out,
+                                               w.seeds, w.cent, nullptr);
+  }
+  copy_centroids_kernel<<<static_cast<unsigned>((static_cast<int64_t>(G) * k * D + 255) / 256), 256, 0, st>>>(
+      w.cent, p.centroids_out, static_cast<int64_t>(G) * k * D);
+  sort_pass(p.key_offset, nkeys, p.perm_out);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys) {
+  const size_t nchunks = (N + kChunk - 1) / kChunk;
+  const size_t nk = static_cast<size_t>(nkeys > k ? nkeys : k);
+  return align256(sizeof(int32_t) * G * static_cast<size_t>(N)) +
+         2 * align256(sizeof(int32_t) * G * nk * nchunks) +
+         2 * align256(sizeof(float) * G * static_cast<size_t>(k) * D) + 256;
+}
+
+cudaError_t launch_kmeans(const KMeansParams& p, cudaStream_t st) {
+  if (p.D == 128) {
+    switch (p.dtype) {
+      case VCATTN_DTYPE_BF16: return kmeans_impl<VCATTN_DTYPE_BF16, 128>(p, st);
+      case VCATTN_DTYPE_F16: return kmeans_impl<VCATTN_DTYPE_F16, 128>(p, st);
+      default: return kmeans_impl<VCATTN_DTYPE_F32, 128>(p, st);
+    }
+  }
+  switch (p.dtype) {
+    case VCATTN_DTYPE_BF16: return kmeans_impl<VCATTN_DTYPE_BF16, 64>(p, st);
+    case VCATTN_DTYPE_F16: return kmeans_impl<VCATTN_DTYPE_F16, 64>(p, st);
+    default: return kmeans_impl<VCATTN_DTYPE_F32, 64>(p, st);
+  }
+}
+
+}  // namespace vcattn

@@ -1,0 +1,441 @@
+// Prepare kernels: permute, Hadamard-rotate, smooth and quantise Q/K/V into
+// the Prepared layout of triton_attn.py:504-579, plus the routing statistics
+// of triton_attn.py:716-735.
+//
+// All kernels are HBM-bound.  One warp owns one token row (D = 128: four
+// elements per lane; D = 64: sixteen lanes per row), so every load and store
+// of a row is a single coalesced transaction and the Hadamard butterfly runs
+// in registers with warp shuffles.  Means are accumulated in float64 and
+// rounded once, which makes them independent of the reduction order.
+#include "kernels.cuh"
+
+namespace vcattn {
+
+// ---------------------------------------------------------------------------
+// Row access helpers.  A warp handles one row; lane l owns 4 consecutive
+// elements (D = 128) or, for D = 64, lanes 0..15 own row r and lanes 16..31
+// row r+1 of a row pair.
+// ---------------------------------------------------------------------------
+template <int D> struct RowMap;
+template <> struct RowMap<128> {
+  static constexpr int kRowsPerWarp = 1;
+  static __device__ __forceinline__ int sub(int lane) { return 0; }
+  static __device__ __forceinline__ int col(int lane) { return lane * 4; }
+  static __device__ __forceinline__ float amax(float v) { return warp_max(v); }
+  static __device__ __forceinline__ void fwht(float v[4], int lane) { fwht128_warp(v, lane); }
+};
+template <> struct RowMap<64> {
+  static constexpr int kRowsPerWarp = 2;
+  static __device__ __forceinline__ int sub(int lane) { return lane >> 4; }
+  static __device__ __forceinline__ int col(int lane) { return (lane & 15) * 4; }
+  static __device__ __forceinline__ float amax(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+  }
+  static __device__ __forceinline__ void fwht(float v[4], int lane) { fwht64_halfwarp(v, lane); }
+};
+
+__device__ __forceinline__ int source_row(const int32_t* perm, int perm_rows, int g, int n, int t) {
+  if (perm == nullptr) return t;
+  const int pr = (perm_rows == 1) ? 0 : g;
+  return perm[static_cast<int64_t>(pr) * n + t];
+}
+
+// ---------------------------------------------------------------------------
+// K token mean (smooth_k, triton_attn.py:545-546): partial float64 sums of the
+// rotated K per (head, chunk of kChunkRows tokens).  The mean is permutation
+// invariant, so it is taken over the unpermuted rows.
+// ---------------------------------------------------------------------------
+constexpr int kChunkRows = 256;
+
+// Fixed-order reduction of per-lane float64 accumulators: lane l of warp w
+// holds channels col(l)..col(l)+3; thread d < D sums warps 0..7 and, for
+// D = 64, both half-warps, always in the same order.
+template <int D>
+__device__ __forceinline__ double reduce_lanes(double (*red)[32][4], int nwarps, int d) {
+  const int l = d / 4, i = d % 4;
+  double tot = 0.0;
+  for (int w = 0; w < nwarps; ++w) {
+    tot += red[w][l][i];
+    if (D == 64) tot += red[w][l + 16][i];
+  }
+  return tot;
+}
+
+template <int DT, int D>
+__global__ void __launch_bounds__(256) kmean_partial_kernel(
+    vcattn_bhnd k, int H, int N, int flags, double* __restrict__ partial) {
+  using RM = RowMap<D>;
+  __shared__ double red[8][32][4];
+  const int g = blockIdx.y, chunk = blockIdx.x;
+  const int b = g / H, h = g % H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  const int t0 = chunk * kChunkRows;
+  const int t1 = min(N, t0 + kChunkRows);
+  // Rows advance in warp-uniform steps so every lane reaches the shuffles.
+  for (int base = t0 + warp * RM::kRowsPerWarp; base < t1; base += 8 * RM::kRowsPerWarp) {
+    const int t = base + RM::sub(lane);
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool live = t < t1;
+    if (live) {
+      const int64_t off = b * k.sb + h * k.sh + static_cast<int64_t>(t) * k.sn + RM::col(lane);
+      const float4 x = load4<DT>(k.data, off);
+      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    }
+    if (flags & VCATTN_HADAMARD) RM::fwht(v, lane);
+    if (live) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] += static_cast<double>(v[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) red[warp][lane][i] = acc[i];
+  __syncthreads();
+  if (threadIdx.x < D)
+    partial[(static_cast<int64_t>(g) * gridDim.x + chunk) * D + threadIdx.x] =
+        reduce_lanes<D>(red, 8, threadIdx.x);
+}
+
+template <int D>
+__global__ void kmean_final_kernel(const double* __restrict__ partial, int nchunks, int N,
+                                   float* __restrict__ kmean) {
+  const int g = blockIdx.x, d = threadIdx.x;
+  if (d >= D) return;
+  double tot = 0.0;
+  for (int c = 0; c < nchunks; ++c) tot += partial[(static_cast<int64_t>(g) * nchunks + c) * D + d];
+  kmean[g * D + d] = __fdiv_rn(__double2float_rn(tot), static_cast<float>(N));
+}
+
+// ---------------------------------------------------------------------------
+// Q / K rows: rotate, (K) subtract the token mean, per-row E4M3.
+// One CTA covers `rows` consecutive output rows (a routing block when
+// statistics are requested) so that block sums reduce in a fixed order.
+// ---------------------------------------------------------------------------
+struct QKArgs {
+  vcattn_bhnd x;
+  int H, N, n_pad, flags;
+  const int32_t* perm;   // K only
+  int perm_rows;
+  const float* kmean;    // (G, D) or nullptr
+  uint8_t* codes;        // (G, NP, D)
+  float* scale;          // (G, NP)
+  int rows;              // rows per CTA
+  float* blk_mean;       // (G, NP/rows, D) mean of the rotated rows, or nullptr
+  float* blk_qbar;       // (G, NP/rows, D) sum of fp32(q8 * fp32(qs*sm)), or nullptr
+  float sm_scale;
+};
+
+template <int DT, int D>
+__global__ void __launch_bounds__(256) quant_rows_kernel(QKArgs a) {
+  using RM = RowMap<D>;
+  const int g = blockIdx.y;
+  const int b = g / a.H, h = g % a.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * a.rows;
+  const bool want_mean = a.blk_mean != nullptr;
+  const bool want_qbar = a.blk_qbar != nullptr;
+  double msum[4] = {0.0, 0.0, 0.0, 0.0};
+  double qsum[4] = {0.0, 0.0, 0.0, 0.0};
+  float km[4] = {0.f, 0.f, 0.f, 0.f};
+  if (a.kmean != nullptr) {
+    const float4 t = *reinterpret_cast<const float4*>(a.kmean + g * D + RM::col(lane));
+    km[0] = t.x; km[1] = t.y; km[2] = t.z; km[3] = t.w;
+  }
+  const int nwarps = blockDim.x >> 5;
+  for (int base = warp * RM::kRowsPerWarp; base < a.rows; base += nwarps * RM::kRowsPerWarp) {
+    const int t = r0 + base + RM::sub(lane);
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool real = t < a.N;
+    if (real) {
+      const int src = source_row(a.perm, a.perm_rows, g, a.N, t);
+      const int64_t off = b * a.x.sb + h * a.x.sh + static_cast<int64_t>(src) * a.x.sn + RM::col(lane);
+      const float4 x = load4<DT>(a.x.data, off);
+      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    }
+    if (a.flags & VCATTN_HADAMARD) RM::fwht(v, lane);
+    if (real && a.kmean != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __fsub_rn(v[i], km[i]);
+    }
+    if (!real) { v[0] = v[1] = v[2] = v[3] = 0.f; }
+    float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    am = RM::amax(am);
+    uint32_t packed = 0;
+    float sc = 0.f;
+    if (real) {
+      sc = e4m3_row_scale(am);
+      packed = e4m3x4(__fdiv_rn(v[0], sc), __fdiv_rn(v[1], sc), __fdiv_rn(v[2], sc), __fdiv_rn(v[3], sc));
+    }
+    if (t < a.n_pad) {
+      *reinterpret_cast<uint32_t*>(a.codes + (static_cast<int64_t>(g) * a.n_pad + t) * D + RM::col(lane)) = packed;
+      if ((lane & (32 / RM::kRowsPerWarp - 1)) == 0) a.scale[static_cast<int64_t>(g) * a.n_pad + t] = sc;
+      if (want_mean) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) msum[i] += static_cast<double>(v[i]);
+      }
+      if (want_qbar && real) {
+        const float w = __fmul_rn(sc, a.sm_scale);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float q8 = e4m3_to_float((packed >> (8 * i)) & 0xff);
+          qsum[i] += static_cast<double>(__fmul_rn(q8, w));
+        }
+      }
+    }
+  }
+  if (!want_mean && !want_qbar) return;
+  __shared__ double red_m[8][32][4];
+  __shared__ double red_q[8][32][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    red_m[warp][lane][i] = msum[i];
+    red_q[warp][lane][i] = qsum[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < D) {
+    const int d = threadIdx.x;
+    const int64_t o = (static_cast<int64_t>(g) * gridDim.x + blockIdx.x) * D + d;
+    if (want_mean)
+      a.blk_mean[o] = __fdiv_rn(__double2float_rn(reduce_lanes<D>(red_m, nwarps, d)),
+                                static_cast<float>(a.rows));
+    if (want_qbar) a.blk_qbar[o] = __double2float_rn(reduce_lanes<D>(red_q, nwarps, d));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// V: gather by perm, zero-pad, block demean, per-(block x channel) E4M3,
+// mu / scale (triton_attn.py:555-567, quant.py:219-237).  One CTA per
+// (head, value block); the block is staged in shared memory as fp32.
+// ---------------------------------------------------------------------------
+struct VArgs {
+  vcattn_bhnd x;
+  int H, N, n_pad, br;
+  const int32_t* perm;
+  int perm_rows;
+  uint8_t* codes;    // (G, NP, D) or nullptr
+  uint8_t* codes_t;  // (G, NB, D, br) or nullptr
+  float* scale;      // (G, NB, D)
+  float* mu;         // (G, NB, D) block mean / scale
+  float* mean;       // (G, NB, D) block mean, or nullptr
+};
+
+template <int DT, int D>
+__global__ void __launch_bounds__(D) quant_v_kernel(VArgs a) {
+  extern __shared__ float vs_smem[];   // [br][D]
+  const int g = blockIdx.y, j = blockIdx.x;
+  const int b = g / a.H, h = g % a.H;
+  const int tid = threadIdx.x;
+  const int nb = a.n_pad / a.br;
+  // Stage rows: thread tid loads channel tid of each row (coalesced per row).
+  for (int r = 0; r < a.br; ++r) {
+    const int t = j * a.br + r;
+    float x = 0.f;
+    if (t < a.N) {
+      const int src = source_row(a.perm, a.perm_rows, g, a.N, t);
+      const int64_t off = b * a.x.sb + h * a.x.sh + static_cast<int64_t>(src) * a.x.sn + tid;
+      if constexpr (DT == VCATTN_DTYPE_BF16) x = __bfloat162float(static_cast<const __nv_bfloat16*>(a.x.data)[off]);
+      else if constexpr (DT == VCATTN_DTYPE_F16) x = __half2float(static_cast<const __half*>(a.x.data)[off]);
+      else x = static_cast<const float*>(a.x.data)[off];
+    }
+    vs_smem[r * D + tid] = x;
+  }
+  double s = 0.0;
+  for (int r = 0; r < a.br; ++r) s += static_cast<double>(vs_smem[r * D + tid]);
+  const float mu = __fdiv_rn(__double2float_rn(s), static_cast<float>(a.br));
+  float am = 0.f;
+  for (int r = 0; r < a.br; ++r) {
+    const float rr = __fsub_rn(vs_smem[r * D + tid], mu);
+    vs_smem[r * D + tid] = rr;
+    am = fmaxf(am, fabsf(rr));
+  }
+  const float sc = e4m3_row_scale(am);
+  const int64_t so = (static_cast<int64_t>(g) * nb + j) * D + tid;
+  a.scale[so] = sc;
+  a.mu[so] = __fdiv_rn(mu, sc);
+  if (a.mean) a.mean[so] = mu;
+  if (a.codes_t) {
+    uint8_t* dst = a.codes_t + ((static_cast<int64_t>(g) * nb + j) * D + tid) * a.br;
+    for (int r = 0; r < a.br; r += 4) {
+      const uint32_t w = e4m3x4(__fdiv_rn(vs_smem[(r + 0) * D + tid], sc), __fdiv_rn(vs_smem[(r + 1) * D + tid], sc),
+                                __fdiv_rn(vs_smem[(r + 2) * D + tid], sc), __fdiv_rn(vs_smem[(r + 3) * D + tid], sc));
+      *reinterpret_cast<uint32_t*>(dst + r) = w;
+    }
+  }
+  if (a.codes) {
+    __shared__ float scs[D];
+    scs[tid] = sc;
+    __syncthreads();
+    // Row-major codes: warp w writes rows, lane owns 4 channels.
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nw = D / 32;
+    for (int r = warp; r < a.br; r += nw) {
+      for (int c = lane * 4; c < D; c += 128) {
+        const float* row = vs_smem + r * D + c;
+        const uint32_t w = e4m3x4(__fdiv_rn(row[0], scs[c]), __fdiv_rn(row[1], scs[c + 1]),
+                                  __fdiv_rn(row[2], scs[c + 2]), __fdiv_rn(row[3], scs[c + 3]));
+        *reinterpret_cast<uint32_t*>(a.codes + (static_cast<int64_t>(g) * a.n_pad + j * a.br + r) * D + c) = w;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Routing threshold + keep mask (triton_attn.py:449-459 and :716-735).
+// One CTA per (head, routing query block); thread j handles KV block j.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void route_mask_kernel(const float* __restrict__ k_mean, const float* __restrict__ q_cent,
+                                  const float* __restrict__ q_bar, int nqb, int nb, int q_block,
+                                  int br, float tau, int local_blocks, int sink_blocks,
+                                  float sm_scale, uint8_t* __restrict__ keep,
+                                  float* __restrict__ thresh_out) {
+  extern __shared__ float rsm[];           // proxy[nb]
+  __shared__ float qc[D], qb[D];
+  __shared__ double red[256];
+  const int g = blockIdx.y, i = blockIdx.x;
+  const int tid = threadIdx.x;
+  if (tid < D) {
+    qc[tid] = q_cent[(static_cast<int64_t>(g) * nqb + i) * D + tid];
+    qb[tid] = q_bar[(static_cast<int64_t>(g) * nqb + i) * D + tid];
+  }
+  __syncthreads();
+  // proxy_h[j] = fp32(q_cent . k_mean_j) * scale ; mean over j
+  double part = 0.0;
+  for (int j = tid; j < nb; j += blockDim.x) {
+    const float* km = k_mean + (static_cast<int64_t>(g) * nb + j) * D;
+    double dot = 0.0;
+    for (int d = 0; d < D; ++d) dot += static_cast<double>(qc[d]) * static_cast<double>(km[d]);
+    const float p = __fmul_rn(__double2float_rn(dot), sm_scale);
+    rsm[j] = p;
+    part += static_cast<double>(p);
+  }
+  red[tid] = part;
+  __syncthreads();
+  if (tid == 0) {
+    double tot = 0.0;
+    for (int t = 0; t < blockDim.x; ++t) tot += red[t];
+    red[0] = tot;
+  }
+  __syncthreads();
+  const float mean = __fdiv_rn(__double2float_rn(red[0]), static_cast<float>(nb));
+  __syncthreads();
+  part = 0.0;
+  for (int j = tid; j < nb; j += blockDim.x) {
+    const float dv = __fsub_rn(rsm[j], mean);
+    part += static_cast<double>(__fmul_rn(dv, dv));
+  }
+  red[tid] = part;
+  __syncthreads();
+  if (tid == 0) {
+    double tot = 0.0;
+    for (int t = 0; t < blockDim.x; ++t) tot += red[t];
+    red[0] = tot;
+  }
+  __syncthreads();
+  const float var = __fdiv_rn(__double2float_rn(red[0]), static_cast<float>(nb));
+  const float thr = __fadd_rn(mean, __fmul_rn(tau, __fsqrt_rn(var)));
+  if (tid == 0 && thresh_out) thresh_out[static_cast<int64_t>(g) * nqb + i] = thr;
+  // score_j = fp32(qbar . bf16(k_mean_j)) / q_block
+  const int qb_kv = (i * q_block) / br;
+  for (int j = tid; j < nb; j += blockDim.x) {
+    const float* km = k_mean + (static_cast<int64_t>(g) * nb + j) * D;
+    double dot = 0.0;
+    for (int d = 0; d < D; ++d) dot += static_cast<double>(qb[d]) * static_cast<double>(bf16_round(km[d]));
+    const float score = __fdiv_rn(__double2float_rn(dot), static_cast<float>(q_block));
+    const bool k = (score > thr) || (abs(qb_kv - j) <= local_blocks) || (j < sink_blocks);
+    keep[(static_cast<int64_t>(g) * nqb + i) * nb + j] = k ? 1 : 0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+size_t prepare_workspace_bytes(int G, int N, int D) {
+  const size_t nchunks = (N + kChunkRows - 1) / kChunkRows;
+  return static_cast<size_t>(G) * nchunks * D * sizeof(double) + static_cast<size_t>(G) * D * sizeof(float) + 256;
+}
+
+template <int DT, int D>
+static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
+  const int G = p.B * p.H;
+  const int nb = p.n_pad / p.block_rows;
+  float* kmean = nullptr;
+  if (p.flags & VCATTN_SMOOTH_K) {
+    const int nchunks = (p.N + kChunkRows - 1) / kChunkRows;
+    double* partial = reinterpret_cast<double*>(p.workspace);
+    kmean = reinterpret_cast<float*>(partial + static_cast<size_t>(G) * nchunks * D);
+    kmean_partial_kernel<DT, D><<<dim3(nchunks, G), 256, 0, st>>>(*p.k, p.H, p.N, p.flags, partial);
+    kmean_final_kernel<D><<<G, D, 0, st>>>(partial, nchunks, p.N, kmean);
+  }
+  const bool route = p.route != nullptr;
+  // Q rows
+  {
+    QKArgs a{};
+    a.x = *p.q; a.H = p.H; a.N = p.N; a.n_pad = p.n_pad; a.flags = p.flags;
+    a.perm = nullptr; a.perm_rows = 0; a.kmean = nullptr;
+    a.codes = p.q8; a.scale = p.q_scale;
+    a.rows = route ? p.route->q_block : 64;
+    a.blk_mean = route ? p.route->q_cent : nullptr;
+    a.blk_qbar = route ? p.route->q_bar : nullptr;
+    a.sm_scale = route ? p.route->sm_scale : 0.f;
+    const int grid_x = (p.n_pad + a.rows - 1) / a.rows;
+    quant_rows_kernel<DT, D><<<dim3(grid_x, G), 256, 0, st>>>(a);
+  }
+  // K rows (gathered by perm)
+  {
+    QKArgs a{};
+    a.x = *p.k; a.H = p.H; a.N = p.N; a.n_pad = p.n_pad; a.flags = p.flags;
+    a.perm = p.perm; a.perm_rows = p.perm_rows; a.kmean = kmean;
+    a.codes = p.k8; a.scale = p.k_scale;
+    a.rows = p.block_rows;
+    a.blk_mean = route ? p.route->k_mean : nullptr;
+    a.blk_qbar = nullptr;
+    quant_rows_kernel<DT, D><<<dim3(nb, G), 256, 0, st>>>(a);
+  }
+  // V blocks
+  {
+    VArgs a{};
+    a.x = *p.v; a.H = p.H; a.N = p.N; a.n_pad = p.n_pad; a.br = p.block_rows;
+    a.perm = p.perm; a.perm_rows = p.perm_rows;
+    a.codes = p.v8; a.codes_t = p.v8t; a.scale = p.v_scale; a.mu = p.mu; a.mean = p.v_mean;
+    const size_t smem = static_cast<size_t>(p.block_rows) * D * sizeof(float);
+    cudaFuncSetAttribute(quant_v_kernel<DT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    quant_v_kernel<DT, D><<<dim3(nb, G), D, smem, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t st) {
+  if (p.D == 128) {
+    switch (p.dtype) {
+      case VCATTN_DTYPE_BF16: return prepare_impl<VCATTN_DTYPE_BF16, 128>(p, st);
+      case VCATTN_DTYPE_F16: return prepare_impl<VCATTN_DTYPE_F16, 128>(p, st);
+      default: return prepare_impl<VCATTN_DTYPE_F32, 128>(p, st);
+    }
+  }
+  switch (p.dtype) {
+    case VCATTN_DTYPE_BF16: return prepare_impl<VCATTN_DTYPE_BF16, 64>(p, st);
+    case VCATTN_DTYPE_F16: return prepare_impl<VCATTN_DTYPE_F16, 64>(p, st);
+    default: return prepare_impl<VCATTN_DTYPE_F32, 64>(p, st);
+  }
+}
+
+cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st) {
+  const int nqb = p.n_pad / p.q_block;
+  const int nb = p.n_pad / p.block_rows;
+  const size_t smem = static_cast<size_t>(nb) * sizeof(float);
+  if (p.D == 128) {
+    route_mask_kernel<128><<<dim3(nqb, p.G), 256, smem, st>>>(
+        p.k_mean, p.q_cent, p.q_bar, nqb, nb, p.q_block, p.block_rows, p.tau, p.local_blocks,
+        p.sink_blocks, p.sm_scale, p.keep, p.thresh);
+  } else {
+    route_mask_kernel<64><<<dim3(nqb, p.G), 256, smem, st>>>(
+        p.k_mean, p.q_cent, p.q_bar, nqb, nb, p.q_block, p.block_rows, p.tau, p.local_blocks,
+        p.sink_blocks, p.sm_scale, p.keep, p.thresh);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace vcattn

@@ -1,0 +1,288 @@
+"""Fused VC-Attention on B200: host side of the libvcattn.so kernels.
+
+Interface of the reference's vc_attention/kernels/triton_attn.py
+(``TritonConfig`` :93-129, ``Prepared`` :140-165, ``prepare`` :504-579,
+``restore`` :582-598, ``vc_attention_triton`` :757-855).  The reference name
+``vc_attention_triton`` is kept as an alias of ``vc_attention_cuda`` so the
+router calls it unchanged; there is no Triton and no CPU fallback here: a
+failure raises, and the router (patch.py) turns that into "defer to the
+original attention".
+
+Per call (all on the current CUDA stream, no host synchronisation):
+  1. vcattn_prepare_fp8 : permute K/V, Hadamard-rotate Q/K, subtract the K
+     token mean, per-token E4M3 Q/K, V block demean + per-(block, channel)
+     E4M3, and (sparse) the routing statistics;
+  2. vcattn_route_mask  : the tau block mask (sparse only);
+  3. vcattn_attn_fp8[_sparse] : the fused attention kernel.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import NamedTuple, Optional
+
+import torch
+
+from .. import _native as N
+from ..grouping import _dtype_code, as_bhnd
+
+__all__ = ["TritonConfig", "Prepared", "has_triton", "has_kernel", "prepare", "restore",
+           "vc_attention_cuda", "vc_attention_triton", "route_mask"]
+
+LOG2E = 1.4426950408889634
+P_SCALE = 448.0
+
+
+@dataclass
+class TritonConfig:
+    """Launch configuration (field names of triton_attn.py:93-129).
+
+    block_m     rows per routing query block of the sparse path (the dense
+                kernel's own tile is fixed by the kernel).
+    block_n     KV tile == value block rows (64 or 128).
+    num_warps / num_stages  accepted for interface parity, unused.
+    pv_fp8      accepted; PV is always FP8 E4M3 here.
+    """
+    block_m: int = 64
+    block_n: int = 128
+    num_warps: int = 4
+    num_stages: int = 2
+    enable_expcast: bool = False
+    expcast_beta: float = -0.35
+    pv_fp8: Optional[bool] = None
+    qk_fp4: bool = False
+    sparse: bool = False
+    tau: float = 1.3
+    local_blocks: int = 1
+    sink_blocks: int = 0
+    group: int = 16
+
+
+class Prepared(NamedTuple):
+    """Kernel operands (layout of triton_attn.py:140-165)."""
+    q: torch.Tensor            # (B, H, NP, D) float8_e4m3fn
+    q_scale: torch.Tensor      # (B, H, NP) fp32
+    k: torch.Tensor            # (B, H, NP, D) float8_e4m3fn (permuted)
+    k_scale: torch.Tensor      # (B, H, NP) fp32
+    v: Optional[torch.Tensor]  # (B, H, NP, D) float8_e4m3fn residual codes (permuted)
+    v_scale: torch.Tensor      # (B, H, NB, D) fp32
+    mu: torch.Tensor           # (B, H, NB, D) fp32 block mean / v_scale
+    n_pad: int
+    q4: Optional[torch.Tensor] = None
+    q4_scale: Optional[torch.Tensor] = None
+    k4: Optional[torch.Tensor] = None
+    k4_scale: Optional[torch.Tensor] = None
+    k_mean: Optional[torch.Tensor] = None   # (B, H, NB, D) fp32
+    v_mean: Optional[torch.Tensor] = None   # (B, H, NB, D) fp32
+    thresh: Optional[torch.Tensor] = None   # (B, H, NQB) fp32
+    n_qblk: int = 0
+    # build-specific operands
+    v_t: Optional[torch.Tensor] = None      # (G, NB, D, block_rows) uint8 V codes, block-transposed
+    q_cent: Optional[torch.Tensor] = None   # (G, NQB, D) fp32
+    q_bar: Optional[torch.Tensor] = None    # (G, NQB, D) fp32
+    keep: Optional[torch.Tensor] = None     # (G, NQB, NB) uint8 routing mask
+    block_rows: int = 128
+
+
+def has_kernel() -> bool:
+    """True when libvcattn.so is loaded and a CUDA device is visible."""
+    return N.available() and torch.cuda.is_available()
+
+
+# The reference's name for "the fused kernel can run".
+has_triton = has_kernel
+
+
+def _stream(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _check_qkv(q, k, v):
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise RuntimeError("VC-Attention kernels need CUDA tensors (this build has no CPU path)")
+    if q.shape != k.shape or q.shape != v.shape or q.dim() != 4:
+        raise ValueError(f"q, k, v must share a (B, H, N, D) shape, got {tuple(q.shape)}, "
+                         f"{tuple(k.shape)}, {tuple(v.shape)}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k, v must share a dtype")
+    if q.shape[-1] not in (64, 128):
+        raise ValueError(f"head_dim must be 64 or 128, got {q.shape[-1]}")
+
+
+def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[torch.Tensor] = None,
+            block_rows: int = 128, hadamard: bool = True, smooth_k: bool = True, *,
+            sparse: bool = False, tau: float = 1.3, q_block: int = 64,
+            scale: Optional[float] = None, want_v: bool = True, want_v_t: bool = False,
+            local_blocks: int = 1, sink_blocks: int = 0) -> Prepared:
+    """Quantise and permute Q/K/V into the kernel layout (triton_attn.py:504-579).
+
+    Byte-identical to the reference's portable ``prepare`` on the codes; the
+    scales that depend on a token/block mean differ from it only in the last
+    bits (the mean is rounded once here).  With ``sparse=True`` the routing
+    statistics and the block mask are produced as well.
+    """
+    _check_qkv(q, k, v)
+    lib = N.lib()
+    b, h, n, d = q.shape
+    g = b * h
+    dev = q.device
+    n_pad = -(-n // block_rows) * block_rows
+    nb = n_pad // block_rows
+    qv, _, _, _, _ = as_bhnd(q)
+    kv, _, _, _, _ = as_bhnd(k)
+    vv, _, _, _, _ = as_bhnd(v)
+    dt = _dtype_code(qv._keep)
+    if _dtype_code(kv._keep) != dt or _dtype_code(vv._keep) != dt:
+        raise ValueError("q, k, v must share a dtype")
+    perm_t = None
+    perm_rows = 0
+    if perm is not None:
+        perm_t = perm.to(device=dev, dtype=torch.int32).contiguous()
+        if perm_t.dim() != 2 or perm_t.shape[1] != n or perm_t.shape[0] not in (1, g):
+            raise ValueError(f"perm must be (G, N) or (1, N), got {tuple(perm_t.shape)}")
+        perm_rows = perm_t.shape[0]
+    u8 = torch.uint8
+    q8 = torch.empty((g, n_pad, d), dtype=u8, device=dev)
+    k8 = torch.empty((g, n_pad, d), dtype=u8, device=dev)
+    v8 = torch.empty((g, n_pad, d), dtype=u8, device=dev) if want_v else None
+    v8t = torch.empty((g, nb, d, block_rows), dtype=u8, device=dev) if want_v_t else None
+    qs = torch.empty((g, n_pad), dtype=torch.float32, device=dev)
+    ks = torch.empty((g, n_pad), dtype=torch.float32, device=dev)
+    vs = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
+    mu = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
+    flags = (N.HADAMARD if hadamard else 0) | (N.SMOOTH_K if smooth_k else 0)
+    sc = scale if scale is not None else d ** -0.5
+    route = None
+    k_mean = v_mean = q_cent = q_bar = None
+    if sparse:
+        if n_pad % q_block:
+            raise ValueError("n_pad must be a multiple of q_block for routing")
+        nqb = n_pad // q_block
+        k_mean = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
+        v_mean = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
+        q_cent = torch.empty((g, nqb, d), dtype=torch.float32, device=dev)
+        q_bar = torch.empty((g, nqb, d), dtype=torch.float32, device=dev)
+        route = N.RouteStats(q_block, k_mean.data_ptr(), q_cent.data_ptr(), q_bar.data_ptr(),
+                             v_mean.data_ptr(), float(sc))
+    ws_bytes = lib.vcattn_prepare_workspace_bytes(g, n, d)
+    ws = torch.empty(ws_bytes, dtype=u8, device=dev)
+    N.check("vcattn_prepare_fp8", lib.vcattn_prepare_fp8(
+        qv, kv, vv, dt, b, h, n, d, _ptr(perm_t), perm_rows, block_rows, flags,
+        q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), _ptr(v8), vs.data_ptr(),
+        mu.data_ptr(), _ptr(v8t), route, ws.data_ptr(), ws_bytes, _stream(q)))
+    keep = thresh = None
+    nqb = 0
+    if sparse:
+        nqb = n_pad // q_block
+        keep, thresh = route_mask(route, g, n, n_pad, d, block_rows, tau, local_blocks, sink_blocks,
+                                  sc, dev, q)
+    f8 = torch.float8_e4m3fn
+    return Prepared(
+        q=q8.view(f8).view(b, h, n_pad, d), q_scale=qs.view(b, h, n_pad),
+        k=k8.view(f8).view(b, h, n_pad, d), k_scale=ks.view(b, h, n_pad),
+        v=None if v8 is None else v8.view(f8).view(b, h, n_pad, d),
+        v_scale=vs.view(b, h, nb, d), mu=mu.view(b, h, nb, d), n_pad=n_pad,
+        k_mean=None if k_mean is None else k_mean.view(b, h, nb, d),
+        v_mean=None if v_mean is None else v_mean.view(b, h, nb, d),
+        thresh=None if thresh is None else thresh.view(b, h, nqb), n_qblk=nqb,
+        v_t=v8t, q_cent=q_cent, q_bar=q_bar, keep=keep, block_rows=block_rows)
+
+
+def route_mask(route: "N.RouteStats", g: int, n: int, n_pad: int, d: int, block_rows: int, tau: float,
+               local_blocks: int, sink_blocks: int, sm_scale: float, dev, like: torch.Tensor):
+    nqb = n_pad // route.q_block
+    nb = n_pad // block_rows
+    keep = torch.empty((g, nqb, nb), dtype=torch.uint8, device=dev)
+    thresh = torch.empty((g, nqb), dtype=torch.float32, device=dev)
+    lib = N.lib()
+    N.check("vcattn_route_mask", lib.vcattn_route_mask(
+        route, g, n, n_pad, d, block_rows, float(tau), int(local_blocks), int(sink_blocks),
+        float(sm_scale), keep.data_ptr(), thresh.data_ptr(), _stream(like)))
+    return keep, thresh
+
+
+def restore(p: Prepared, block_rows: int = 128):
+    """Dequantise a Prepared back to value/score units (tests; triton_attn.py:582-598)."""
+    from ..quant import e4m3_decode
+    b, h, np_, d = p.q.shape
+    g = b * h
+    qd = e4m3_decode(p.q.view(torch.uint8).reshape(g, np_, d)) * p.q_scale.reshape(g, np_, 1)
+    kd = e4m3_decode(p.k.view(torch.uint8).reshape(g, np_, d)) * p.k_scale.reshape(g, np_, 1)
+    vs = p.v_scale.reshape(g, -1, d).repeat_interleave(block_rows, dim=1)
+    vd = e4m3_decode(p.v.view(torch.uint8).reshape(g, np_, d)) * vs
+    vd = vd + p.mu.reshape(g, -1, d).repeat_interleave(block_rows, dim=1) * vs
+    return qd, kd, vd
+
+
+def _out_view(q: torch.Tensor, dtype: torch.dtype):
+    """Output buffer in the input's token layout: a transposed (B, N, H, D)
+    input (the ComfyUI 3-D path) gets a (B, N, H, D) buffer, so the caller's
+    transpose-back is free."""
+    b, h, n, d = q.shape
+    if q.stride(-1) == 1 and q.stride(1) == d and q.stride(2) == h * d:
+        buf = torch.empty((b, n, h, d), dtype=dtype, device=q.device)
+        return buf.transpose(1, 2)
+    return torch.empty((b, h, n, d), dtype=dtype, device=q.device)
+
+
+def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      perm: Optional[torch.Tensor] = None, cfg: Optional[TritonConfig] = None,
+                      scale: Optional[float] = None) -> torch.Tensor:
+    """Fused VC-Attention (triton_attn.py:757-855 semantics, no fallback).
+
+    q, k, v: (B, H, N, D) CUDA bf16/fp16/fp32 (strided views accepted);
+    perm: (G, N) or (1, N) int32 V-Smooth permutation or None.
+    Returns (B, H, N, D) in q.dtype.
+    """
+    cfg = cfg or TritonConfig()
+    _check_qkv(q, k, v)
+    b, h, n, d = q.shape
+    if scale is None:
+        scale = d ** -0.5
+    if cfg.qk_fp4 and cfg.sparse:
+        cfg = TritonConfig(**{**cfg.__dict__, "qk_fp4": False})
+    if cfg.qk_fp4:
+        raise NotImplementedError("NVFP4 QK^T kernel is not built in this version")
+    br = cfg.block_n
+    sparse = bool(cfg.sparse)
+    p = prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
+                tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=False, want_v_t=True,
+                local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks)
+    out = _out_view(q, q.dtype)
+    return attention_prepared(p, n, out, scale, cfg)
+
+
+def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
+                       cfg: TritonConfig) -> torch.Tensor:
+    """Run the attention kernel on prepared operands, writing into ``out``."""
+    lib = N.lib()
+    b, h, n_pad, d = p.q.shape
+    g = b * h
+    flags = N.EXPCAST if cfg.enable_expcast else 0
+    odt = _dtype_code(out)
+    q8 = p.q.view(torch.uint8)
+    k8 = p.k.view(torch.uint8)
+    if p.v_t is None:
+        raise ValueError("attention needs the block-transposed V codes (prepare(want_v_t=True))")
+    if cfg.sparse:
+        N.check("vcattn_attn_fp8_sparse", lib.vcattn_attn_fp8_sparse(
+            q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
+            p.v_t.data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), p.k_mean.data_ptr(),
+            p.v_mean.data_ptr(), p.keep.data_ptr(), cfg.block_m, cfg.group, b, h, n, n_pad, d,
+            p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
+            out.stride(0), out.stride(1), out.stride(2), _stream(out)))
+    else:
+        N.check("vcattn_attn_fp8", lib.vcattn_attn_fp8(
+            q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
+            p.v_t.data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), b, h, n, n_pad, d,
+            p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
+            out.stride(0), out.stride(1), out.stride(2), _stream(out)))
+    return out
+
+
+vc_attention_triton = vc_attention_cuda

@@ -1,0 +1,408 @@
+"""Installing VC-Attention into a running model (behaviour of the reference's
+vc_attention/patch.py:60-603).
+
+Three entry routes reach one funnel, ``VCAttentionRuntime.attention``:
+
+* ComfyUI's ``optimized_attention_override`` chain (``install_attention_override``),
+* a wrapper around ``comfy.ldm.modules.attention.optimized_attention``
+  (plus modules that imported it by value),
+* a hook on ``torch.nn.functional.scaled_dot_product_attention``.
+
+The runtime takes only the calls it supports (non-causal, no mask, q/k/v of
+one (B, H, N, D) shape, head_dim 64/128, N >= min_tokens, CUDA tensors on an
+sm_100 GPU with libvcattn.so loaded) and returns None for everything else,
+which every route turns into a call of the original attention.  Any error
+inside VC-Attention is reported once on the console and also defers: the hook
+never takes a sampling run down.
+"""
+
+from __future__ import annotations
+
+import functools
+import sys
+from dataclasses import dataclass
+from typing import Any, Callable, Dict, Optional
+
+import torch
+
+from .device import detect_profile, is_supported, resolve_backend
+from .grouping import GroupingConfig, build_permutation
+from .schedule import GroupSchedule, PermutationCache, StepTracker
+
+__all__ = [
+    "VCAttentionConfig", "VCAttentionRuntime", "get_runtime", "install", "uninstall",
+    "is_installed", "install_attention_override", "fast_path_available", "kernel_status",
+]
+
+_ORIGINALS: Dict[str, Any] = {}
+_NOTIFIED: set = set()
+
+
+def _notify_once(msg: str) -> None:
+    if msg not in _NOTIFIED and len(_NOTIFIED) < 16:
+        _NOTIFIED.add(msg)
+        print(f"[VC-Attention] {msg}")
+
+
+try:  # ComfyUI >= 0.38 wraps q/k/v in single-owner containers
+    from comfy.ldm.modules.attention import AttentionTensorContainer as _ATTN_CONTAINER  # type: ignore
+except Exception:  # pragma: no cover - ComfyUI absent
+    _ATTN_CONTAINER = None
+
+
+@dataclass
+class VCAttentionConfig:
+    enabled: bool = True
+    backend: str = "auto"            # auto | fp8 | nvfp4 | int4 | reference
+    enable_vsmooth: bool = True
+    enable_expcast: bool = False
+    block_rows: int = 128
+    block_m: int = 64
+    min_tokens: int = 8192
+    hadamard: bool = True
+    smooth_k: bool = True
+    enable_sparsity: bool = True
+    tau: float = 1.3
+    sparsity_min_tokens: int = 8192
+    sink_tokens: int = 512
+    local_blocks: int = 1
+    kmeans_iters: int = 3
+    warm_iters: int = 2
+    modality_aware: bool = False
+    group_fraction: float = 0.25
+    reuse_every: int = 4
+    total_steps_hint: int = 8
+    allow_slow_fallback: bool = False
+    override_priority: str = "front"
+    supported_head_dims: tuple = (64, 128)
+
+
+class VCAttentionRuntime:
+    """Owns the schedule, the permutation cache and the routing decision."""
+
+    def __init__(self, config: Optional[VCAttentionConfig] = None):
+        self.config = config or VCAttentionConfig()
+        self.profile = detect_profile()
+        self.backend = resolve_backend(self.config.backend, self.profile)
+        self.schedule = GroupSchedule(group_fraction=self.config.group_fraction,
+                                      reuse_every=self.config.reuse_every,
+                                      total_steps_hint=self.config.total_steps_hint,
+                                      min_tokens=self.config.min_tokens)
+        self.tracker = StepTracker(total_steps_hint=self.config.total_steps_hint)
+        self.cache = PermutationCache()
+        self.tags: Optional[torch.Tensor] = None
+        self.stats: Dict[str, int] = {"calls": 0, "used": 0, "skipped": 0, "grouped": 0}
+
+    # -- schedule ----------------------------------------------------------
+    def begin_step(self) -> int:
+        return self.tracker.begin_step()
+
+    def observe_total_steps(self, total: int) -> None:
+        self.tracker.observe_total(total)
+
+    def reset(self) -> None:
+        self.tracker.reset()
+        self.cache.clear()
+
+    def set_tags(self, tags: Optional[torch.Tensor]) -> None:
+        self.tags = tags
+
+    # -- permutation -------------------------------------------------------
+    def permutation(self, v: torch.Tensor) -> Optional[torch.Tensor]:
+        """(G, N) int32 permutation on the device, or None when not grouping."""
+        cfg = self.config
+        step = self.tracker.current
+        if not cfg.enable_vsmooth or not self.schedule.should_group(step, self.tracker.total_steps):
+            return None
+        b, h, n, d = v.shape
+        g = b * h
+        bucket = self.schedule.window_index(step)
+        cached = self.cache.get(bucket, n, g)
+        if cached is not None and not self.schedule.should_recompute(step):
+            return cached[0]
+        gcfg = GroupingConfig(block_rows=cfg.block_rows,
+                              iters=cfg.kmeans_iters if cached is None else cfg.warm_iters,
+                              warm_iters=cfg.warm_iters, modality_aware=cfg.modality_aware)
+        warm = None if cached is None else cached[1]
+        res = build_permutation(v, gcfg, tags=self.tags, centroids=warm)
+        self.cache.put(bucket, n, g, res.perm, res.centroids)
+        return res.perm
+
+    # -- attention ---------------------------------------------------------
+    def attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, is_causal: bool = False,
+                  attn_mask: Any = None, scale: Optional[float] = None,
+                  dropout_p: float = 0.0) -> Optional[torch.Tensor]:
+        """VC-Attention output, or None to defer to the original attention."""
+        self.stats["calls"] += 1
+        cfg = self.config
+        if not cfg.enabled or is_causal or attn_mask is not None or (dropout_p or 0.0) > 0.0:
+            self.stats["skipped"] += 1
+            return None
+        if not all(isinstance(t, torch.Tensor) for t in (q, k, v)) or q.dim() != 4 \
+                or q.shape != k.shape or q.shape != v.shape:
+            self.stats["skipped"] += 1
+            return None
+        b, h, n, d = q.shape
+        if d not in cfg.supported_head_dims or n < cfg.min_tokens:
+            self.stats["skipped"] += 1
+            _notify_once(f"call n={n} (head_dim={d}) below min_tokens={cfg.min_tokens} -> native SDPA")
+            return None
+        if q.device.type != "cuda" or not fast_path_available(q.device):
+            self.stats["skipped"] += 1
+            return None
+        perm = self.permutation(v)
+        if perm is not None:
+            self.stats["grouped"] += 1
+        self.stats["used"] += 1
+        from .kernels.cuda_attn import TritonConfig, vc_attention_triton
+        tcfg = TritonConfig(
+            block_m=cfg.block_m,
+            block_n=cfg.block_rows,
+            enable_expcast=bool(cfg.enable_expcast and self.backend == "fp8"),
+            qk_fp4=(self.backend == "nvfp4"),
+            sparse=bool(cfg.enable_sparsity and n >= cfg.sparsity_min_tokens),
+            tau=cfg.tau,
+            local_blocks=cfg.local_blocks,
+            sink_blocks=max(0, int(cfg.sink_tokens) // max(1, cfg.block_rows)),
+        )
+        return vc_attention_triton(q, k, v, perm=perm, cfg=tcfg, scale=scale)
+
+
+def fast_path_available(device: Optional[torch.device] = None) -> bool:
+    """True when the fused kernels can run: an sm_100 GPU and libvcattn.so loaded."""
+    if not torch.cuda.is_available():
+        return False
+    from .kernels.cuda_attn import has_kernel
+    if not has_kernel():
+        return False
+    return is_supported(detect_profile(device))
+
+
+def kernel_status() -> str:
+    if not torch.cuda.is_available():
+        return "no CUDA visible -> VC-Attention inactive, using native SDPA"
+    from . import _native as N
+    if not N.available():
+        return f"CUDA present but libvcattn.so is unavailable ({N.load_error()}) -> VC-Attention inactive"
+    prof = detect_profile()
+    if not is_supported(prof):
+        return f"{prof.name} is not an sm_100 GPU -> VC-Attention inactive, using native SDPA"
+    return f"fused kernel available on {torch.cuda.get_device_name(0)}"
+
+
+_RUNTIME = VCAttentionRuntime()
+
+
+def get_runtime() -> VCAttentionRuntime:
+    return _RUNTIME
+
+
+# ---------------------------------------------------------------------------
+# Routes into the runtime
+# ---------------------------------------------------------------------------
+
+def _try_vc(runtime: VCAttentionRuntime, q, k, v, heads: int, mask=None,
+            skip_reshape: bool = False, skip_output_reshape: bool = False, **kwargs):
+    """ComfyUI-style call -> VC-Attention output or None.
+
+    4-D (B, H, N, D) passes through; 3-D (B, N, H*D) is viewed as
+    (B, H, N, D) without a copy (the kernels read strided views) and the
+    output comes back in the caller's layout.
+    """
+    if not runtime.config.enabled or mask is not None:
+        return None
+    if not all(isinstance(t, torch.Tensor) for t in (q, k, v)):
+        return None
+    if q.dim() == 4:
+        b, h_, s_, d_ = q.shape
+        out = runtime.attention(q, k, v)
+        if out is None:
+            return None
+        return out if skip_output_reshape else out.transpose(1, 2).reshape(b, s_, h_ * d_)
+    if q.dim() != 3 or heads <= 0 or q.shape[-1] % heads:
+        return None
+    b, n, inner = q.shape
+    d = inner // heads
+    q4 = q.view(b, n, heads, d).transpose(1, 2)
+    k4 = k.view(k.shape[0], k.shape[1], heads, d).transpose(1, 2)
+    v4 = v.view(v.shape[0], v.shape[1], heads, d).transpose(1, 2)
+    out = runtime.attention(q4, k4, v4)
+    if out is None:
+        return None
+    return out if skip_output_reshape else out.transpose(1, 2).reshape(b, n, heads * d)
+
+
+def install_attention_override(runtime: VCAttentionRuntime, model: Any,
+                               priority: Optional[str] = None) -> bool:
+    """Enter ComfyUI's ``transformer_options["optimized_attention_override"]``
+    chain.  With ``priority="front"`` VC-Attention chains in front of an
+    existing override and hands it the calls it does not take; with
+    ``"defer"`` it stays out when another backend owns the slot."""
+    try:
+        opts = model.model_options["transformer_options"]
+    except Exception:
+        return False
+    prev = opts.get("optimized_attention_override")
+    priority = priority or runtime.config.override_priority
+    if prev is not None and priority != "front":
+        _notify_once("another attention backend already owns attention "
+                     "(`optimized_attention_override`) -> VC-Attention stays out. Set "
+                     "override_priority='front' to take priority instead.")
+        return False
+
+    def override(func, *args, **kwargs):
+        try:
+            out = _try_vc(runtime, *args, **kwargs)
+        except Exception as e:   # never take a run down
+            _notify_once(f"override deferring after {type(e).__name__}: {e}")
+            out = None
+        if out is not None:
+            return out
+        return prev(func, *args, **kwargs) if prev is not None else func(*args, **kwargs)
+
+    if prev is not None:
+        override._vc_prev = prev   # type: ignore[attr-defined]
+    opts["optimized_attention_override"] = override
+    _ORIGINALS["override"] = (opts, prev, override)
+    _notify_once("registered in the attention-override chain"
+                 + (" (chained in front of an existing backend)" if prev is not None else ""))
+    return True
+
+
+def _make_hook(runtime: VCAttentionRuntime, orig: Callable) -> Callable:
+    @functools.wraps(orig)
+    def hooked(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None,
+               *args, **kwargs):
+        if runtime.config.enabled and not args and not kwargs:
+            try:
+                out = runtime.attention(query, key, value, is_causal=is_causal, attn_mask=attn_mask,
+                                        scale=scale, dropout_p=dropout_p)
+            except Exception as e:
+                _notify_once(f"SDPA hook deferring after {type(e).__name__}: {e}")
+                out = None
+            if out is not None:
+                return out
+        return orig(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
+                    is_causal=is_causal, scale=scale, *args, **kwargs)
+
+    return hooked
+
+
+def install(config: Optional[VCAttentionConfig] = None, model: Any = None) -> VCAttentionRuntime:
+    """Patch attention globally and optionally count steps on ``model``."""
+    global _RUNTIME
+    if config is not None:
+        _RUNTIME = VCAttentionRuntime(config)
+    runtime = _RUNTIME
+    if "sdpa" not in _ORIGINALS and hasattr(torch.nn.functional, "scaled_dot_product_attention"):
+        orig = torch.nn.functional.scaled_dot_product_attention
+        _ORIGINALS["sdpa"] = orig
+        torch.nn.functional.scaled_dot_product_attention = _make_hook(runtime, orig)
+    elif "sdpa" in _ORIGINALS:
+        # A re-install with a new runtime re-targets the existing hook.
+        torch.nn.functional.scaled_dot_product_attention = _make_hook(runtime, _ORIGINALS["sdpa"])
+    try:
+        from comfy.ldm.modules import attention as comfy_attention  # type: ignore
+        if "comfy" not in _ORIGINALS and hasattr(comfy_attention, "optimized_attention"):
+            orig_c = comfy_attention.optimized_attention
+            _ORIGINALS["comfy"] = orig_c
+            hooked_c = _make_comfy_hook(orig_c)
+            comfy_attention.optimized_attention = hooked_c
+            _rebind_by_value_imports(orig_c, hooked_c)
+    except Exception:
+        pass
+    if model is not None:
+        install_attention_override(runtime, model)
+        _install_step_counter(model, runtime)
+    return runtime
+
+
+def _make_comfy_hook(orig: Callable) -> Callable:
+    @functools.wraps(orig)
+    def hooked(q, k, v, heads, *args, **kwargs):
+        try:
+            t_opts = kwargs.get("transformer_options")
+            if isinstance(t_opts, dict) and t_opts.get("optimized_attention_override") is not None:
+                if "override" not in _ORIGINALS:
+                    _notify_once("another attention backend is active (`optimized_attention_override`) "
+                                 "and VC-Attention is not in the chain -> VC-Attention is INACTIVE. "
+                                 "Pass model= to install() to chain in, or remove that node.")
+                return orig(q, k, v, heads, *args, **kwargs)
+            if _ATTN_CONTAINER is not None and isinstance(q, _ATTN_CONTAINER):
+                q, k, v = q.peek(), k.peek(), v.peek()
+            if not all(isinstance(t, torch.Tensor) for t in (q, k, v)):
+                return orig(q, k, v, heads, *args, **kwargs)
+            out = _try_vc(get_runtime(), q, k, v, heads, *args, **kwargs)
+            if out is None:
+                return orig(q, k, v, heads, *args, **kwargs)
+            return out
+        except Exception as e:
+            _notify_once(f"deferring to original attention after {type(e).__name__}: {e}")
+            return orig(q, k, v, heads, *args, **kwargs)
+
+    return hooked
+
+
+def _install_step_counter(model: Any, runtime: VCAttentionRuntime) -> None:
+    """Wrap the denoiser's forward so the runtime knows the step index."""
+    denoiser = None
+    for cand in (getattr(model, "diffusion_model", None),
+                 getattr(getattr(model, "model", None), "diffusion_model", None)):
+        if cand is not None and hasattr(cand, "forward"):
+            denoiser = cand
+            break
+    if denoiser is None or getattr(denoiser, "_vc_step_wrapped", False):
+        return
+    orig_forward = denoiser.forward
+
+    @functools.wraps(orig_forward)
+    def wrapped(*args, **kwargs):
+        runtime.begin_step()
+        t_opts = kwargs.get("transformer_options") or {}
+        sigmas = t_opts.get("sample_sigmas") if isinstance(t_opts, dict) else None
+        if sigmas is not None:
+            try:
+                runtime.observe_total_steps(len(sigmas) - 1)
+            except Exception:
+                pass
+        return orig_forward(*args, **kwargs)
+
+    wrapped._vc_step_wrapped = True   # type: ignore[attr-defined]
+    denoiser.forward = wrapped
+    denoiser._vc_step_wrapped = True  # type: ignore[attr-defined]
+    _ORIGINALS.setdefault("denoiser", orig_forward)
+
+
+def _rebind_by_value_imports(orig: Callable, hooked: Callable) -> None:
+    """Swap ``optimized_attention`` in comfy modules that imported it by value."""
+    for name, mod in list(sys.modules.items()):
+        if not name.startswith("comfy"):
+            continue
+        mdict = getattr(mod, "__dict__", None)
+        if mdict and mdict.get("optimized_attention", None) is orig:
+            mdict["optimized_attention"] = hooked
+
+
+def uninstall() -> None:
+    """Restore every patched callable."""
+    entry = _ORIGINALS.pop("override", None)
+    if entry is not None:
+        opts, prev, ours = entry
+        if opts.get("optimized_attention_override") is ours:
+            if prev is None:
+                opts.pop("optimized_attention_override", None)
+            else:
+                opts["optimized_attention_override"] = prev
+    if "sdpa" in _ORIGINALS:
+        torch.nn.functional.scaled_dot_product_attention = _ORIGINALS.pop("sdpa")
+    if "comfy" in _ORIGINALS:
+        try:
+            from comfy.ldm.modules import attention as comfy_attention  # type: ignore
+            comfy_attention.optimized_attention = _ORIGINALS.pop("comfy")
+        except Exception:
+            _ORIGINALS.pop("comfy", None)
+    _ORIGINALS.pop("denoiser", None)
+
+
+def is_installed() -> bool:
+    return "sdpa" in _ORIGINALS

@@ -1,0 +1,167 @@
+/*
+ * vcattn.h -- C ABI of the B200 (sm_100a) VC-Attention hot path.
+ *
+ * One shared library, libvcattn.so, built from comfyui_vc_attention_b200/csrc.
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as void*, enqueues its kernels on that stream and returns a status
+ * code (0 = VCATTN_OK).  Nothing here aborts, traps or synchronises the device
+ * unless the entry point says so.  Device buffers are borrowed; the library
+ * allocates nothing: scratch memory is a caller-provided workspace whose size
+ * the matching *_workspace_bytes() function reports.
+ *
+ * The reference (bingling360/comfyui_vc_attention) is Python + Triton, so its
+ * "FFI" for this path is the Python call boundary; each function below names
+ * the reference interface (file:line inside that project) whose work it
+ * performs.  The Python host layer (comfyui_vc_attention_b200.vc_attention)
+ * binds these with ctypes under the reference's own function names.
+ *
+ * Layout conventions
+ *   B, H, N, D   batch, heads, tokens, head dim (D in {64, 128}); G = B*H.
+ *   NP           N rounded up to a multiple of block_rows; NB = NP/block_rows.
+ *   "(G, NP, D)" means a dense row-major array, head-major.
+ *   Codes are E4M3 bytes (float8_e4m3fn bit patterns), scales are fp32.
+ */
+#ifndef VCATTN_H_
+#define VCATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VCATTN_API __attribute__((visibility("default")))
+#else
+#define VCATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define VCATTN_OK 0
+#define VCATTN_ERR_ARG 1        /* unsupported shape / option / alignment     */
+#define VCATTN_ERR_CUDA 2       /* a CUDA call failed; see vcattn_last_error() */
+#define VCATTN_ERR_WORKSPACE 3  /* workspace smaller than *_workspace_bytes()  */
+#define VCATTN_ERR_DEVICE 4     /* a kernel reported failure in its status word */
+#define VCATTN_ERR_INJECTED 5   /* host-side fault injection (tests)           */
+
+/* ---- element types ----------------------------------------------------- */
+#define VCATTN_DTYPE_BF16 0
+#define VCATTN_DTYPE_F16 1
+#define VCATTN_DTYPE_F32 2
+
+/* ---- prepare flags (triton_attn.py:504-512 hadamard / smooth_k) --------- */
+#define VCATTN_HADAMARD 1
+#define VCATTN_SMOOTH_K 2
+
+/* ---- attention flags (TritonConfig, triton_attn.py:93-129) ------------- */
+#define VCATTN_EXPCAST 1        /* write P bytes with ExpCast (expcast.py:52-70) */
+
+/* A strided (B, H, N, D) view: element (b,h,n,d) sits at
+ * data + b*sb + h*sh + n*sn + d (strides in elements, d contiguous).  This is
+ * what lets the 3-D (B, N, H*D) ComfyUI layout (patch.py:331-337) be read
+ * without a transpose copy. */
+typedef struct vcattn_bhnd {
+  const void* data;
+  int64_t sb, sh, sn;
+} vcattn_bhnd;
+
+/* Optional routing statistics produced by vcattn_prepare_fp8 for the
+ * block-sparse kernel (triton_attn.py:716-735).  Any pointer may be NULL. */
+typedef struct vcattn_route_stats {
+  int q_block;     /* rows per routing query block (TritonConfig.block_m)     */
+  float* k_mean;   /* (G, NB, D)  block mean of the rotated, smoothed, permuted K */
+  float* q_cent;   /* (G, NP/q_block, D) query-block mean of the rotated Q      */
+  float* q_bar;    /* (G, NP/q_block, D) sum over the block of q8 * (qs * sm_scale) */
+  float* v_mean;   /* (G, NB, D)  value block mean (the skipped-block value)      */
+  float sm_scale;  /* softmax scale folded into q_bar                           */
+} vcattn_route_stats;
+
+/* ---- library ------------------------------------------------------------ */
+VCATTN_API int vcattn_abi_version(void);
+/* Text of the last error on the calling thread ("" if none). */
+VCATTN_API const char* vcattn_last_error(void);
+/* Host-side fault injection for the router's fallback tests: while set, the
+ * named entry point (e.g. "vcattn_attn_fp8") returns VCATTN_ERR_INJECTED
+ * without launching anything.  NULL or "" clears it. */
+VCATTN_API void vcattn_inject_fault(const char* entry_point);
+
+/* ---- V-Smooth grouping: grouping.py:127-147 (kmeans) + :150-186
+ *      (build_permutation) ------------------------------------------------
+ * v: (B,H,N,D) view, any of the three dtypes (rounded to bf16 first, as
+ *    grouping.py:299 does).  k clusters; iters Lloyd iterations (warm_iters
+ *    when warm_centroids != NULL).  key_offset (N,) int32 or NULL is added to
+ *    the cluster label before the stable sort (modality / padding keys,
+ *    grouping.py:176-183); nkeys bounds the keys (k when key_offset is NULL).
+ * Outputs: centroids_out (G,k,D) bf16 bits, perm_out (G,N) int32, and
+ *    labels_out (G,N) int32 (may be NULL). */
+VCATTN_API size_t vcattn_kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys);
+VCATTN_API int vcattn_kmeans(const vcattn_bhnd* v, int dtype, int B, int H, int N, int D,
+                  int k, int iters, const uint16_t* warm_centroids,
+                  const int32_t* key_offset, int nkeys,
+                  uint16_t* centroids_out, int32_t* perm_out, int32_t* labels_out,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- prepare: triton_attn.py:504-579 (the portable Prepared producer) ----
+ * perm: (perm_rows, N) int32 gather index applied to K and V; perm_rows is 0
+ *    (no permutation), 1 (shared by every head) or G.
+ * Outputs (all dense, zero-padded to NP rows):
+ *    q8, k8, v8 (G,NP,D) E4M3 codes; q_scale, k_scale (G,NP); v_scale,
+ *    mu (G,NB,D) with mu = block mean / v_scale.
+ *    v8t: NULL, or the same V codes stored block-transposed (G,NB,D,block_rows)
+ *    (the operand layout of the register-MMA attention kernels); v8 may be
+ *    NULL when only v8t is wanted.
+ * route: NULL, or routing statistics to fill (block-sparse path). */
+VCATTN_API size_t vcattn_prepare_workspace_bytes(int G, int N, int D);
+VCATTN_API int vcattn_prepare_fp8(const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_bhnd* v,
+                       int dtype, int B, int H, int N, int D,
+                       const int32_t* perm, int perm_rows, int block_rows, int flags,
+                       uint8_t* q8, float* q_scale, uint8_t* k8, float* k_scale,
+                       uint8_t* v8, float* v_scale, float* mu, uint8_t* v8t,
+                       const vcattn_route_stats* route,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- routing mask: triton_attn.py:449-459 with the threshold of :716-735 -
+ * keep (G, NP/q_block, NB) uint8: 1 = exact tile, 0 = block-mean approximation.
+ * thresh (G, NP/q_block) fp32 output (may be NULL). */
+VCATTN_API int vcattn_route_mask(const vcattn_route_stats* route, int G, int N, int n_pad, int D,
+                      int block_rows, float tau, int local_blocks, int sink_blocks,
+                      float sm_scale, uint8_t* keep, float* thresh, void* stream);
+
+/* ---- fused dense FP8 attention: triton_attn.py:203-322 (+ launch :831-844)
+ * Consumes the prepare outputs (V as the block-transposed v8t); writes O
+ * (B,H,N,D) through the out view (out_dtype one of the three dtypes; out
+ * strides in elements). */
+VCATTN_API int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8,
+                    const float* k_scale, const uint8_t* v8t, const float* v_scale,
+                    const float* mu, int B, int H, int N, int n_pad, int D,
+                    int block_rows, float sm_scale, int flags, double expcast_beta,
+                    void* out, int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn,
+                    void* stream);
+
+/* ---- fused block-sparse FP8 attention: triton_attn.py:384-501 ----------
+ * keep from vcattn_route_mask; k_mean/v_mean (G,NB,D) fp32; q_block rows per
+ * routing query block; group KV blocks routed together. */
+VCATTN_API int vcattn_attn_fp8_sparse(const uint8_t* q8, const float* q_scale, const uint8_t* k8,
+                           const float* k_scale, const uint8_t* v8t, const float* v_scale,
+                           const float* mu, const float* k_mean, const float* v_mean,
+                           const uint8_t* keep, int q_block, int group,
+                           int B, int H, int N, int n_pad, int D, int block_rows,
+                           float sm_scale, int flags, double expcast_beta,
+                           void* out, int out_dtype, int64_t out_sb, int64_t out_sh,
+                           int64_t out_sn, void* stream);
+
+/* ---- element codecs, exposed for bit-exact tests ------------------------
+ * vcattn_e4m3_encode: quant.py:56-84.  vcattn_fp4_encode: quant.py:144-161
+ * (one code per byte).  vcattn_expcast_codes: expcast.py:52-70 on a (rows,
+ * cols) score tile and its (rows,) running maxima; mode 0 is the kernel's
+ * one-FMA form, mode 1 the reference's operation sequence. */
+VCATTN_API int vcattn_e4m3_encode(const float* x, int64_t n, uint8_t* out, void* stream);
+VCATTN_API int vcattn_fp4_encode(const float* x, int64_t n, uint8_t* out, void* stream);
+VCATTN_API int vcattn_expcast_codes(const float* s, const float* m, int rows, int cols, double beta,
+                         int mode, uint8_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VCATTN_H_ */

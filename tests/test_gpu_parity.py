@@ -1,0 +1,318 @@
+"""GPU parity: the sm_100a kernels of libvcattn.so against the CPU oracle.
+
+Bit-exact: E4M3/E2M1 encoders, ExpCast bytes (reference operation order),
+k-means labels / centroids / permutation, prepared Q/K/V codes and scales.
+Tolerance (attention output, fp32 accumulation order differs): rel-L2 <= 2e-3
+against the reference's portable path and PSNR vs fp32 SDPA within 0.3 dB of
+the reference's own PSNR; a tighter 1e-3 against the oracle of the kernel's
+own code-unit arithmetic.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import vc_oracle as O
+from oracle.inputs import digest, make_qkv
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+REL_L2_REF = 2e-3        # north-star tolerance vs the reference's portable path
+PSNR_DB = 0.3
+REL_L2_CODES = 1e-3      # vs the oracle of the kernel's own arithmetic
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from comfyui_vc_attention_b200.vc_attention import _native as N
+    N.lib()   # raises if the library is missing: a GPU box must have it
+    return torch.device("cuda:0")
+
+
+def _load(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def _t(a, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return t.to(dtype) if dtype is not None else t
+
+
+def _bf16(a, dev):
+    return _t(a, dev, torch.bfloat16)
+
+
+# ---------------------------------------------------------------- codecs ----
+
+def test_e4m3_encoder_bit_exact(dev):
+    from comfyui_vc_attention_b200.vc_attention.quant import e4m3_encode
+    c = _load("codecs.npz")
+    got = e4m3_encode(_t(c["e4m3_x"], dev)).cpu().numpy()
+    assert np.array_equal(got, c["e4m3_codes"])
+    # every fp32 bit pattern class near E4M3 ties / subnormals / saturation
+    rng = np.random.default_rng(11)
+    x = np.concatenate([rng.standard_normal(200000).astype(np.float32) * 50,
+                        rng.standard_normal(100000).astype(np.float32) * 1e-2,
+                        (np.arange(-4000, 4000, dtype=np.float32) / 16.0)])
+    assert np.array_equal(e4m3_encode(_t(x, dev)).cpu().numpy(), O.e4m3_encode(x))
+
+
+def test_fp4_encoder_bit_exact(dev):
+    from comfyui_vc_attention_b200.vc_attention.quant import fp4_encode
+    c = _load("codecs.npz")
+    assert np.array_equal(fp4_encode(_t(c["fp4_x"], dev)).cpu().numpy(), c["fp4_codes"])
+    x = (np.arange(-1000, 1000, dtype=np.float32) / 128.0)
+    assert np.array_equal(fp4_encode(_t(x, dev)).cpu().numpy(), O.fp4_encode(x))
+
+
+def test_expcast_bytes_bit_exact(dev):
+    from comfyui_vc_attention_b200.vc_attention.expcast import expcast_codes
+    c = _load("codecs.npz")
+    s, m = _t(c["ec_s"], dev), _t(c["ec_m"], dev)
+    exact = expcast_codes(s, m, exact=True).cpu().numpy()
+    assert np.array_equal(exact, c["ec_codes"])
+    fast = expcast_codes(s, m, exact=False).cpu().numpy().astype(np.int32)
+    diff = np.abs(fast - exact.astype(np.int32))
+    assert diff.max() <= 1
+    assert (diff == 0).mean() >= 0.99
+
+
+# --------------------------------------------------------------- k-means ----
+
+def test_kmeans_config0_bit_exact(dev):
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
+    g = _load("config0.npz")
+    q, k, v = make_qkv(1, 2, 1024, 128, seed=0)
+    assert digest(q, k, v) == str(g["inputs_digest"])
+    res = build_permutation(_bf16(v.reshape(2, 1024, 128), dev), GroupingConfig(block_rows=64, iters=10))
+    assert res.k == 16
+    assert np.array_equal(res.perm.cpu().numpy(), g["perm"])
+    assert np.array_equal(res.centroids.float().cpu().numpy(), g["centroids"])
+    assert np.array_equal(res.labels.cpu().numpy(), g["labels"])
+
+
+def test_kmeans_k64_bit_exact(dev):
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
+    g = _load("kmeans64.npz")
+    q, k, v = make_qkv(1, 2, 4096, 128, seed=1)
+    res = build_permutation(_bf16(v.reshape(2, 4096, 128), dev),
+                            GroupingConfig(block_rows=64, iters=3, max_clusters=64))
+    assert res.k == 64
+    assert np.array_equal(res.perm.cpu().numpy(), g["perm"])
+    assert np.array_equal(res.centroids.float().cpu().numpy(), g["centroids"])
+
+
+@pytest.mark.parametrize("n,k_clusters,iters", [(1000, 8, 3), (3000, 200, 2), (257, 3, 4)])
+def test_kmeans_matches_oracle(dev, n, k_clusters, iters):
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
+    q, k, v = make_qkv(1, 3, n, 128, seed=n)
+    vb = v.reshape(3, n, 128)
+    br = max(1, -(-n // k_clusters))
+    perm_o, cent_o, kk, lab_o = O.build_permutation(vb, block_rows=br, iters=iters)
+    res = build_permutation(_bf16(vb, dev), GroupingConfig(block_rows=br, iters=iters))
+    assert res.k == kk
+    assert np.array_equal(res.labels.cpu().numpy(), lab_o)
+    assert np.array_equal(res.centroids.float().cpu().numpy(), cent_o)
+    assert np.array_equal(res.perm.cpu().numpy(), perm_o)
+
+
+def test_kmeans_warm_start_and_keys(dev):
+    """Warm-started centroids and the modality / padding sort keys."""
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
+    n = 2048
+    q, k, v = make_qkv(1, 2, n, 128, seed=5)
+    vb = v.reshape(2, n, 128)
+    _, cent0, kk, _ = O.build_permutation(vb, block_rows=128, iters=2)
+    tags = np.zeros(n, np.int64)
+    tags[:128] = 1
+    tags[128:384] = 2
+    tags[-100:] = -1
+    perm_o, cent_o, _, lab_o = O.build_permutation(vb, block_rows=128, iters=1, warm=cent0, warm_iters=2,
+                                                   tags=tags, modality_aware=True, valid_len=n - 50)
+    cfg = GroupingConfig(block_rows=128, iters=1, warm_iters=2, modality_aware=True)
+    res = build_permutation(_bf16(vb, dev), cfg, tags=torch.from_numpy(tags),
+                            centroids=_bf16(cent0, dev), valid_len=n - 50)
+    assert np.array_equal(res.centroids.float().cpu().numpy(), cent_o)
+    assert np.array_equal(res.perm.cpu().numpy(), perm_o)
+
+
+def test_kmeans_input_layouts_agree(dev):
+    """fp32 input and a strided (B, N, H, D)-backed view give the bf16 result."""
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, kmeans
+    n = 1536
+    q, k, v = make_qkv(1, 4, n, 128, seed=9)
+    vt = _bf16(v, dev)                                           # (1, 4, n, 128)
+    cfg = GroupingConfig(block_rows=128, iters=3)
+    lab_a, cent_a, perm_a = kmeans(vt, 12, cfg)
+    strided = vt.transpose(1, 2).contiguous().transpose(1, 2)    # same values, (B,N,H,D) memory
+    lab_b, cent_b, perm_b = kmeans(strided, 12, cfg)
+    lab_c, cent_c, perm_c = kmeans(vt.float(), 12, cfg)
+    for lab, cent, perm in ((lab_b, cent_b, perm_b), (lab_c, cent_c, perm_c)):
+        assert torch.equal(lab, lab_a) and torch.equal(cent, cent_a) and torch.equal(perm, perm_a)
+
+
+# --------------------------------------------------------------- prepare ----
+
+def _prep_gpu(q, k, v, perm, br, dev, **kw):
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import prepare
+    return prepare(_bf16(q, dev), _bf16(k, dev), _bf16(v, dev),
+                   None if perm is None else _t(perm, dev), block_rows=br, **kw)
+
+
+def _assert_prepare_equal(p, ref, g_shape):
+    G = g_shape
+    np.testing.assert_array_equal(p.q.view(torch.uint8).reshape(G, -1, p.q.shape[-1]).cpu().numpy(), ref["q"])
+    np.testing.assert_array_equal(p.k.view(torch.uint8).reshape(G, -1, p.k.shape[-1]).cpu().numpy(), ref["k"])
+    np.testing.assert_array_equal(p.v.view(torch.uint8).reshape(G, -1, p.v.shape[-1]).cpu().numpy(), ref["v"])
+    for f in ("q_scale", "k_scale", "v_scale", "mu"):
+        got = getattr(p, f).reshape(ref[f].shape).cpu().numpy()
+        np.testing.assert_array_equal(got, ref[f], err_msg=f)
+
+
+def test_prepare_config0_bit_exact(dev):
+    g = _load("config0.npz")
+    q, k, v = make_qkv(1, 2, 1024, 128, seed=0)
+    q, k, v = (a.reshape(1, 2, 1024, 128) for a in (q, k, v))
+    p = _prep_gpu(q, k, v, g["perm"], 64, dev, want_v_t=True)
+    ref = O.prepare(q.reshape(2, 1024, 128), k.reshape(2, 1024, 128), v.reshape(2, 1024, 128),
+                    g["perm"], block_rows=64)
+    _assert_prepare_equal(p, ref, 2)
+    # codes equal the reference's own prepare() bytes
+    assert np.array_equal(p.q.view(torch.uint8).cpu().numpy().reshape(g["q8"].shape), g["q8"])
+    assert np.array_equal(p.k.view(torch.uint8).cpu().numpy().reshape(g["k8"].shape), g["k8"])
+    assert np.array_equal(p.v.view(torch.uint8).cpu().numpy().reshape(g["v8"].shape), g["v8"])
+    # block-transposed V holds the same codes
+    vt = p.v_t.cpu().numpy()                                   # (G, NB, D, BR)
+    v8 = ref["v"].reshape(2, 16, 64, 128).transpose(0, 1, 3, 2)
+    assert np.array_equal(vt, v8)
+
+
+@pytest.mark.parametrize("n,br,h", [(200, 128, 2), (1000, 128, 3), (333, 64, 2), (64, 64, 1)])
+def test_prepare_ragged_bit_exact(dev, n, br, h):
+    q, k, v = make_qkv(1, h, n, 128, seed=n + br)
+    rng = np.random.default_rng(n)
+    perm = np.stack([rng.permutation(n) for _ in range(h)]).astype(np.int32)
+    p = _prep_gpu(q, k, v, perm, br, dev)
+    ref = O.prepare(q.reshape(h, n, 128), k.reshape(h, n, 128), v.reshape(h, n, 128), perm, block_rows=br)
+    assert p.n_pad == ref["n_pad"]
+    _assert_prepare_equal(p, ref, h)
+
+
+def test_prepare_head_dim_64_and_shared_perm(dev):
+    n, h = 500, 2
+    q, k, v = make_qkv(1, h, n, 64, seed=4)
+    perm = np.random.default_rng(3).permutation(n).astype(np.int32)[None, :]
+    p = _prep_gpu(q, k, v, perm, 128, dev)
+    ref = O.prepare(q.reshape(h, n, 64), k.reshape(h, n, 64), v.reshape(h, n, 64), perm, block_rows=128)
+    _assert_prepare_equal(p, ref, h)
+
+
+def test_prepare_without_hadamard_or_smoothing(dev):
+    n, h = 300, 2
+    q, k, v = make_qkv(1, h, n, 128, seed=8)
+    p = _prep_gpu(q, k, v, None, 128, dev, hadamard=False, smooth_k=False)
+    ref = O.prepare(q.reshape(h, n, 128), k.reshape(h, n, 128), v.reshape(h, n, 128), None,
+                    block_rows=128, hadamard=False, smooth_k=False)
+    _assert_prepare_equal(p, ref, h)
+
+
+# ------------------------------------------------------------- attention ----
+
+def _attn_gpu(q, k, v, perm, br, dev, expcast=False, out_dtype=torch.float32):
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig,
+                                                                          attention_prepared)
+    p = _prep_gpu(q, k, v, perm, br, dev, want_v=False, want_v_t=True)
+    b, h, n, d = q.shape
+    out = torch.empty((b, h, n, d), dtype=out_dtype, device=dev)
+    cfg = TritonConfig(block_n=br, enable_expcast=expcast)
+    attention_prepared(p, n, out, d ** -0.5, cfg)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy().reshape(b * h, n, d)
+
+
+@pytest.mark.parametrize("expcast", [False, True])
+def test_attention_config0(dev, expcast):
+    g = _load("config0.npz")
+    q, k, v = make_qkv(1, 2, 1024, 128, seed=0)
+    got = _attn_gpu(q, k, v, g["perm"], 64, dev, expcast=expcast)
+    G = 2
+    qg, kg, vg = (a.reshape(G, 1024, 128) for a in (q, k, v))
+    ref = g["out_expcast" if expcast else "out_plain"].reshape(G, 1024, 128)
+    assert O.rel_l2(got, ref) <= REL_L2_REF
+    prep = O.prepare(qg, kg, vg, g["perm"], block_rows=64)
+    codes = O.attention_codes(prep, 1024, 64, 128, 128 ** -0.5, expcast=expcast)
+    assert O.rel_l2(got, codes) <= REL_L2_CODES
+    sd = O.sdpa_f32(qg, kg, vg)
+    assert abs(O.psnr(got, sd) - O.psnr(ref, sd)) <= PSNR_DB
+
+
+@pytest.mark.parametrize("n,br,d,h", [(200, 128, 128, 2), (1000, 64, 128, 2), (700, 128, 64, 3),
+                                      (64, 64, 128, 1), (2048, 128, 128, 2)])
+def test_attention_shapes(dev, n, br, d, h):
+    q, k, v = make_qkv(1, h, n, d, seed=n + d)
+    qg, kg, vg = (a.reshape(h, n, d) for a in (q, k, v))
+    perm = np.stack([np.random.default_rng(i).permutation(n) for i in range(h)]).astype(np.int32)
+    got = _attn_gpu(q, k, v, perm, br, dev)
+    ref = O.attention_reference(qg, kg, vg, perm, block_rows=br, block_m=64)
+    assert O.rel_l2(got, ref) <= REL_L2_REF
+    sd = O.sdpa_f32(qg, kg, vg)
+    assert abs(O.psnr(got, sd) - O.psnr(ref, sd)) <= PSNR_DB
+
+
+def test_attention_bf16_output_and_layouts(dev):
+    """Product entry point: bf16 in/out, 4-D and 3-D ComfyUI layouts agree."""
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import TritonConfig, vc_attention_cuda
+    n, h, d = 1024, 4, 128
+    q, k, v = make_qkv(1, h, n, d, seed=21)
+    qt, kt, vt = _bf16(q, dev), _bf16(k, dev), _bf16(v, dev)
+    perm = torch.stack([torch.randperm(n, generator=torch.Generator().manual_seed(i)) for i in range(h)])
+    perm = perm.to(torch.int32).to(dev)
+    cfg = TritonConfig(block_n=128)
+    o4 = vc_attention_cuda(qt, kt, vt, perm, cfg)
+    assert o4.dtype == torch.bfloat16 and o4.shape == (1, h, n, d)
+    # (B, N, H*D) memory viewed as (B, H, N, D): no copy on the way in or out
+    q3 = qt.transpose(1, 2).contiguous().transpose(1, 2)
+    k3 = kt.transpose(1, 2).contiguous().transpose(1, 2)
+    v3 = vt.transpose(1, 2).contiguous().transpose(1, 2)
+    o3 = vc_attention_cuda(q3, k3, v3, perm, cfg)
+    assert torch.equal(o3, o4)
+    assert o3.transpose(1, 2).is_contiguous()
+    ref = O.attention_reference(q.reshape(h, n, d), k.reshape(h, n, d), v.reshape(h, n, d),
+                                perm.cpu().numpy(), block_rows=128)
+    got = o4.float().cpu().numpy().reshape(h, n, d)
+    assert O.rel_l2(got, O.bf16_round(ref)) <= REL_L2_REF
+
+
+def test_router_routes_and_defers(dev):
+    """SDPA hook: large calls go through the kernels, a host-injected kernel
+    failure defers to the original attention, uninstall restores it."""
+    import torch.nn.functional as F
+    from comfyui_vc_attention_b200.vc_attention import _native as N
+    from comfyui_vc_attention_b200.vc_attention.patch import (VCAttentionConfig, get_runtime, install,
+                                                              uninstall)
+    orig = F.scaled_dot_product_attention
+    n, h, d = 1024, 2, 128
+    q, k, v = make_qkv(1, h, n, d, seed=31)
+    qt, kt, vt = _bf16(q, dev), _bf16(k, dev), _bf16(v, dev)
+    try:
+        rt = install(VCAttentionConfig(min_tokens=512, enable_sparsity=False))
+        rt.begin_step()
+        out = torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)
+        assert rt.stats["used"] == 1 and rt.stats["grouped"] == 1
+        sd = O.sdpa_f32(q.reshape(h, n, d), k.reshape(h, n, d), v.reshape(h, n, d))
+        assert O.psnr(out.float().cpu().numpy().reshape(h, n, d), sd) > 35.0
+        N.inject_fault("vcattn_attn_fp8")
+        try:
+            out2 = torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)
+        finally:
+            N.inject_fault(None)
+        assert torch.equal(out2, orig(qt, kt, vt))
+        assert get_runtime().stats["used"] == 2
+    finally:
+        uninstall()
+    assert F.scaled_dot_product_attention is orig

@@ -1,0 +1,170 @@
+"""Host-side interface (no GPU): schedule, cache, router gating, hooks, step
+counter and the ComfyUI nodes.  Mirrors the reference's tests/test_install.py."""
+
+import torch
+
+from comfyui_vc_attention_b200.vc_attention.h3 import H3, estimate_tokens, recommended_config
+from comfyui_vc_attention_b200.vc_attention.patch import (VCAttentionConfig, VCAttentionRuntime, _try_vc,
+                                                          get_runtime, install,
+                                                          install_attention_override, is_installed,
+                                                          kernel_status, uninstall)
+from comfyui_vc_attention_b200.vc_attention.schedule import GroupSchedule, PermutationCache, StepTracker
+
+
+def test_h3_schedule():
+    h3 = recommended_config(total_steps=8)
+    assert h3["group_steps"] == 2 and h3["block_rows"] == 128
+    rt = VCAttentionRuntime(VCAttentionConfig(total_steps_hint=8))
+    s = rt.schedule
+    assert s.should_group(0, 8) and s.should_group(1, 8) and not s.should_group(2, 8)
+    assert s.should_recompute(0) and not s.should_recompute(1) and s.should_recompute(4)
+    assert GroupSchedule(group_fraction=0.0).group_steps(8) == 1
+    assert GroupSchedule(group_fraction=0.5).group_steps(20) == 10
+    assert H3.qkv_dim == 7168 and H3.rope_dims == 96
+    est = estimate_tokens(243, 768, 1344, audio_seconds=10.1)
+    assert est["latent_grid"] == (61, 24, 42) and est["audio"] == 404
+
+
+def test_step_tracker_and_cache():
+    t = StepTracker()
+    assert t.current == 0
+    t.begin_step(); t.begin_step()
+    assert t.current == 1
+    t.observe_total(20)
+    assert t.total_steps == 20
+    t.reset()
+    assert t.index == -1 and t.total_steps is None
+    c = PermutationCache(max_entries=2)
+    assert c.get(0, 10, 2) is None and c.misses == 1
+    c.put(0, 10, 2, "p0", "c0")
+    c.put(1, 10, 2, "p1", "c1")
+    c.put(2, 10, 2, "p2", "c2")      # FIFO: evicts bucket 0
+    assert c.get(0, 10, 2) is None and c.get(2, 10, 2) == ("p2", "c2") and c.hits == 1
+    assert len(c) == 2
+    c.clear()
+    assert len(c) == 0 and c.hits == 0
+
+
+def test_runtime_gating_on_cpu():
+    rt = VCAttentionRuntime(VCAttentionConfig(min_tokens=256))
+    q = torch.randn(1, 2, 512, 128)
+    assert rt.attention(q, q, q) is None                      # CPU tensors defer
+    assert rt.attention(q, q, q, is_causal=True) is None
+    assert rt.attention(q, q, q, attn_mask=torch.ones(1)) is None
+    assert rt.attention(q[..., :96], q[..., :96], q[..., :96]) is None
+    assert rt.attention(q[:, :, :100], q[:, :, :100], q[:, :, :100]) is None
+    assert rt.stats["calls"] == 5 and rt.stats["skipped"] == 5 and rt.stats["used"] == 0
+
+
+def test_sdpa_hook_falls_through_and_uninstalls():
+    orig = torch.nn.functional.scaled_dot_product_attention
+    install(VCAttentionConfig(enabled=True, min_tokens=256), model=None)
+    try:
+        assert is_installed()
+        q, k, v = (torch.randn(1, 4, 512, 128) for _ in range(3))
+        got = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+        assert torch.allclose(got, orig(q, k, v))
+        assert get_runtime().stats["calls"] > 0
+    finally:
+        uninstall()
+    assert torch.nn.functional.scaled_dot_product_attention is orig
+    assert not is_installed()
+
+
+class _FakeDenoiser:
+    def __init__(self):
+        self.calls = 0
+
+    def forward(self, *a, **kw):
+        self.calls += 1
+
+
+class _FakeModel:
+    def __init__(self):
+        self.diffusion_model = _FakeDenoiser()
+        self.model_options = {"transformer_options": {}}
+
+
+def test_step_counter_and_override_chain():
+    model = _FakeModel()
+    rt = install(VCAttentionConfig(), model=model)
+    try:
+        for _ in range(3):
+            model.diffusion_model.forward(transformer_options={"sample_sigmas": list(range(21))})
+        assert rt.tracker.index == 2 and rt.tracker.total_steps == 20
+        ov = model.model_options["transformer_options"]["optimized_attention_override"]
+        calls = []
+
+        def func(q, k, v, heads, **kw):
+            calls.append(heads)
+            return "original"
+
+        q = torch.randn(1, 64, 256)           # 3-D ComfyUI layout, CPU -> defers
+        assert ov(func, q, q, q, 2) == "original" and calls == [2]
+    finally:
+        uninstall()
+    assert "optimized_attention_override" not in model.model_options["transformer_options"]
+
+
+def test_override_priority_defer_and_front():
+    model = _FakeModel()
+    prev_calls = []
+
+    def prev(func, *a, **kw):
+        prev_calls.append(1)
+        return "prev"
+
+    model.model_options["transformer_options"]["optimized_attention_override"] = prev
+    rt = VCAttentionRuntime(VCAttentionConfig(override_priority="defer"))
+    assert install_attention_override(rt, model) is False
+    assert model.model_options["transformer_options"]["optimized_attention_override"] is prev
+    assert install_attention_override(rt, model, priority="front") is True
+    ov = model.model_options["transformer_options"]["optimized_attention_override"]
+    assert ov is not prev and ov._vc_prev is prev
+    q = torch.randn(1, 64, 256)
+    assert ov(lambda *a, **k: "func", q, q, q, 2) == "prev" and prev_calls == [1]
+    uninstall()
+    assert model.model_options["transformer_options"]["optimized_attention_override"] is prev
+
+
+def test_try_vc_reshapes_3d_and_4d(monkeypatch):
+    seen = {}
+
+    class RT:
+        config = VCAttentionConfig()
+
+        def attention(self, q, k, v):
+            seen["shape"] = tuple(q.shape)
+            seen["stride"] = q.stride()
+            return q * 2
+
+    q3 = torch.randn(2, 10, 4 * 8)
+    out = _try_vc(RT(), q3, q3, q3, 4)
+    assert seen["shape"] == (2, 4, 10, 8) and seen["stride"] == (320, 8, 32, 1)   # a view, no copy
+    assert torch.allclose(out, q3 * 2)
+    q4 = torch.randn(2, 4, 10, 8)
+    assert torch.allclose(_try_vc(RT(), q4, q4, q4, 4, skip_output_reshape=True), q4 * 2)
+    assert _try_vc(RT(), q3, q3, q3, 4, mask=torch.ones(1)) is None
+    assert _try_vc(RT(), q3, q3, q3, 5) is None
+
+
+def test_nodes_execute():
+    import comfyui_vc_attention_b200 as pkg
+
+    class DummyModel:
+        pass
+
+    Node = pkg.VCAttentionMiniMaxH3
+    assert "model" in Node.INPUT_TYPES()["required"]
+    assert pkg.NODE_DISPLAY_NAME_MAPPINGS["VCAttentionMiniMaxH3"] == "VC Attention (MiniMax-H3)"
+    try:
+        out = Node().apply(model=DummyModel())
+        assert isinstance(out, tuple) and out[0] is not None
+        for kw in ({"backend": "reference"}, {"backend": "fp8", "enable_expcast": True},
+                   {"backend": "nvfp4", "total_steps": 20, "block_rows": 64, "min_tokens": 512},
+                   {"enable_vsmooth": False, "modality_aware": True, "kmeans_iters": 1, "reuse_every": 1}):
+            Node().apply(model=DummyModel(), **kw)
+        assert isinstance(pkg.VCAttentionDisable().apply(model=DummyModel()), tuple)
+    finally:
+        uninstall()
+    assert "inactive" in kernel_status()
