@@ -1,0 +1,402 @@
+#!/usr/bin/env python
+"""VC-Attention hot-path benchmark (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c1|c3|c2]
+
+Workload (N=1 headline): B=1, H=56, N=16384, D=128 bf16,
+dense FP8 VC-Attention with ExpCast, Hadamard and a V-Smooth permutation from
+k-means with k=64.  One "step" is one call of the hot path on one batch:
+prepare (permute, rotate, smooth, quantise) + the fused attention kernel, the
+permutation precomputed (it is cached across layers and steps by the runtime;
+its k-means time is reported separately as ``kmeans_ms``).
+
+``value`` = effective TFLOPS over all ranks, 4*B*H*N^2*D per call / time, with
+inputs resident in HBM; ``e2e`` = the same through the public entry point with
+pinned-host inputs copied in and the output copied back inside the timed
+region.  Multi-GPU runs (torchrun, one rank per GPU) give every rank its own
+independent (batch, head) units of the same size: weak scaling, no collective
+in the data path; the time is the max over ranks.
+
+``--impl reference`` times the reference's CPU algorithm (the oracle
+restatement of vc_attention_reference, oracle/) on the host cores on a
+bounded sample of the same workload, extrapolated by rows and heads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ms/call & effective TFLOPS, 56h D=128 at 16K/64K tokens; PSNR vs fp32 SDPA"
+UNIT = "TFLOPS (effective, 4*B*H*N^2*D per call)"
+
+WORKLOADS = {
+    "c1": dict(desc="configs[1]: dense FP8 VC-Attention, B1 H56 N16384 D128, ExpCast on, Hadamard on, "
+                    "V-Smooth k=64", B=1, H=56, N=16384, D=128, expcast=True, sparse=False, k=64,
+               block_rows=128, spatial=None),
+    "c3": dict(desc="dense FP8 VC-Attention, B1 H56 N65536 D128, ExpCast on, V-Smooth k=512",
+               B=1, H=56, N=65536, D=128, expcast=True, sparse=False, k=512, block_rows=128, spatial=None),
+}
+
+
+def flops_per_call(w) -> float:
+    return 4.0 * w["B"] * w["H"] * float(w["N"]) ** 2 * w["D"]
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            mp = json.load(f)
+        return mp, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# --------------------------------------------------------------- clocks ----
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self._t.join(timeout=2)
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ------------------------------------------------------------ GPU inputs ----
+
+def make_inputs_gpu(w, seed, dev):
+    """Seeded Q/K/V of the configs' distributions, generated on the device."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    G, N, D = w["B"] * w["H"], w["N"], w["D"]
+    q = torch.randn((G, N, D), generator=g, device=dev)
+    k = torch.randn((G, N, D), generator=g, device=dev) + 2.0 * torch.randn((G, 1, D), generator=g, device=dev)
+    cent = torch.randn((G, 64, D), generator=g, device=dev)
+    lab = torch.randint(0, 64, (G, N), generator=g, device=dev)
+    v = torch.gather(cent, 1, lab.unsqueeze(-1).expand(G, N, D))
+    v = v + 0.3 * torch.randn((G, N, D), generator=g, device=dev)
+    shape = (w["B"], w["H"], N, D)
+    out = [t.to(torch.bfloat16).reshape(shape).contiguous() for t in (q, k, v)]
+    del q, k, v, cent, lab
+    return out
+
+
+def psnr_vs_sdpa(out, q, k, v, heads_per_chunk=8):
+    import torch
+    import torch.nn.functional as F
+    num = 0.0
+    peak = 0.0
+    cnt = 0
+    H = q.shape[1]
+    for h0 in range(0, H, heads_per_chunk):
+        sl = slice(h0, min(H, h0 + heads_per_chunk))
+        ref = F.scaled_dot_product_attention(q[:, sl].float(), k[:, sl].float(), v[:, sl].float())
+        num += float(((out[:, sl].float() - ref) ** 2).sum())
+        peak = max(peak, float((ref ** 2).max()))
+        cnt += ref.numel()
+        del ref
+    import math
+    return 10 * math.log10(peak / max(num / cnt, 1e-30))
+
+
+# --------------------------------------------------------- CPU baseline ----
+
+def cpu_sample(w, q_rows, seed=0):
+    """Reference CPU algorithm (oracle restatement of vc_attention_reference,
+    with the oracle's k-means permutation) on one head and the first q_rows
+    query rows at full N.  Returns (seconds, extrapolated ms per full call)."""
+    import numpy as np
+    from oracle import vc_oracle as O
+    rng = np.random.default_rng(seed)
+    N, D = w["N"], w["D"]
+    q = O.bf16_round(rng.standard_normal((1, N, D), dtype=np.float32))
+    k = O.bf16_round(rng.standard_normal((1, N, D), dtype=np.float32)
+                     + 2.0 * rng.standard_normal((1, 1, D), dtype=np.float32))
+    c = rng.standard_normal((1, 64, D), dtype=np.float32)
+    v = O.bf16_round(c[:, rng.integers(0, 64, N)] + 0.3 * rng.standard_normal((1, N, D), dtype=np.float32))
+    perm = np.argsort(rng.integers(0, w["k"], (1, N)), axis=-1, kind="stable").astype(np.int32)
+    t0 = time.perf_counter()
+    O.attention_reference(q, k, v, perm, block_rows=w["block_rows"], block_m=64, expcast=w["expcast"],
+                          q_rows=q_rows)
+    dt = time.perf_counter() - t0
+    scale = (w["B"] * w["H"]) * (N / q_rows)
+    return dt, dt * scale * 1e3
+
+
+def run_reference_arm(args, w, rank):
+    if rank != 0:
+        return 0
+    cores = os.cpu_count() or 1
+    q_rows = args.cpu_rows
+    for _ in range(args.warmup):
+        cpu_sample(w, q_rows)
+    times = []
+    for i in range(args.steps):
+        _, ms = cpu_sample(w, q_rows, seed=i)
+        times.append(ms)
+    ms = statistics.mean(times)
+    val = flops_per_call(w) / (ms / 1e3) / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 (fp32 accumulate, CPU emulation)",
+        "data": "synthetic (seeded configs[1] distributions)",
+        "config": {"workload": w["desc"], "q_rows_sampled": q_rows, "heads_sampled": 1},
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"oracle vc_attention_reference, 1 head x {q_rows} query rows x "
+                                   f"{w['N']} keys per step, extrapolated x{w['B'] * w['H']} heads x "
+                                   f"{w['N'] // q_rows} row blocks"},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------- main ----
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c1", choices=sorted(WORKLOADS))
+    ap.add_argument("--cpu-rows", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference_arm(args, w, rank)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from comfyui_vc_attention_b200.vc_attention import _native as N
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
+                                                                          prepare, vc_attention_cuda)
+    N.lib()
+
+    q, k, v = make_inputs_gpu(w, 1234 + rank, dev)
+    B, H, NT, D = q.shape
+    G = B * H
+    # k-means permutation (timed once, reported separately)
+    gcfg = GroupingConfig(block_rows=w["block_rows"], iters=3, max_clusters=w["k"])
+    build_permutation(v.view(G, NT, D), gcfg)      # warm
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    res = build_permutation(v.view(G, NT, D), gcfg)
+    e1.record()
+    torch.cuda.synchronize()
+    kmeans_ms = e0.elapsed_time(e1)
+    perm = res.perm
+    cfg = TritonConfig(block_n=w["block_rows"], enable_expcast=w["expcast"], sparse=w["sparse"])
+    scale = D ** -0.5
+    out = torch.empty_like(q)
+
+    def step(evs=None):
+        if evs is not None:
+            evs[0].record()
+        p = prepare(q, k, v, perm, block_rows=w["block_rows"], hadamard=True, smooth_k=True,
+                    want_v=False, want_v_t=True)
+        if evs is not None:
+            evs[1].record()
+        attention_prepared(p, NT, out, scale, cfg)
+        if evs is not None:
+            evs[2].record()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    clocks.start()
+    time.sleep(0.3)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t_start.record()
+    for i in range(args.steps):
+        step(evs[i])
+    t_end.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    prep_ms = statistics.mean(evs[i][0].elapsed_time(evs[i][1]) for i in range(args.steps))
+    attn_ms = statistics.mean(evs[i][1].elapsed_time(evs[i][2]) for i in range(args.steps))
+    if world > 1:
+        t = torch.tensor([total_ms, attn_ms, prep_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, attn_ms, prep_ms = (float(x) for x in t.tolist())
+    ms_per_step = total_ms / args.steps
+    fl = flops_per_call(w)
+    value = world * fl / (ms_per_step / 1e3) / 1e12
+
+    # ---- end to end through the public entry point, host buffers ----------
+    q_h = q.cpu().pin_memory()
+    k_h = k.cpu().pin_memory()
+    v_h = v.cpu().pin_memory()
+    o_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        qd.copy_(q_h, non_blocking=True)
+        kd.copy_(k_h, non_blocking=True)
+        vd.copy_(v_h, non_blocking=True)
+        o = vc_attention_cuda(qd, kd, vd, perm, cfg, scale)
+        o_h.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps // 2)
+    a.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    b_.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b_) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = 3 * q.numel() * q.element_size()
+    d2h = q.numel() * q.element_size()
+    del q_h, k_h, v_h, qd, kd, vd
+
+    # ---- fidelity (not timed) ---------------------------------------------
+    psnr = None
+    if rank == 0:
+        step()
+        torch.cuda.synchronize()
+        psnr = psnr_vs_sdpa(out, q, k, v)
+
+    peaks, peak_kind = measured_peaks()
+    fp8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    attn_tflops = fl / (attn_ms / 1e3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "attn_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                tinfo = json.load(f)
+            if tinfo.get("workload") == args.workload:
+                traffic = tinfo.get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    prep_bytes = (6 * G * NT * D + 3 * G * NT * D + 8 * G * NT + 8 * G * (NT // w["block_rows"]) * D
+                  + 4 * G * NT)
+    launches_per_step = 5 + 1
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 (fp32 accumulate)",
+        "data": "synthetic (seeded configs[1] distributions, generated on device)",
+        "config": {"workload": w["desc"], "B": B, "H": H, "N": NT, "D": D, "block_rows": w["block_rows"],
+                   "kmeans_k": res.k, "expcast": w["expcast"], "sparse": w["sparse"],
+                   "parallelism": f"(batch, head) units x{world} ranks, independent, no collective",
+                   "l2": "inputs larger than L2 (Q/K/V 235 MB each)"},
+        "ms_prepare": prep_ms, "ms_attention": attn_ms, "kmeans_ms": kmeans_ms, "psnr_db": psnr,
+        "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": attn_tflops / fp8_peak, "traffic": traffic,
+                     "kernel": "vcattn attention kernel",
+                     "peak_note": f"dense FP8 = 2 x {peak_kind} bf16 burst ({peaks.get('bf16_tflops')} TF/s)"},
+        "prepare_roofline": {"bound": "hbm", "achieved": prep_bytes / (prep_ms / 1e3) / 1e9,
+                             "peak": float(peaks.get("hbm_gbs", 6650.0)), "unit": "GB/s",
+                             "frac": prep_bytes / (prep_ms / 1e3) / 1e9 / float(peaks.get("hbm_gbs", 6650.0))},
+        "e2e": {"value": world * fl / (e2e_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_call": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dt, ms_cpu = cpu_sample(w, args.cpu_rows)
+        line["cpu_baseline"] = {
+            "value": fl / (ms_cpu / 1e3) / 1e12, "unit": UNIT, "cores": os.cpu_count() or 1,
+            "kind": "port", "ms_per_call_extrapolated": ms_cpu, "sample_seconds": dt,
+            "sample": f"oracle vc_attention_reference, 1 head x {args.cpu_rows} query rows x {NT} keys, "
+                      f"extrapolated x{G} heads x {NT // args.cpu_rows} row blocks"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -496,9 +496,11 @@ def expcast_codes(s: np.ndarray, m: np.ndarray, beta: float = -0.35) -> np.ndarr
 
 def attention_reference(q, k, v, perm=None, block_rows=128, block_m=64, expcast=False,
                         beta=-0.35, scale=None, vsmooth=True, hadamard=True,
-                        smooth_k=True) -> np.ndarray:
+                        smooth_k=True, q_rows=None) -> np.ndarray:
     """vc_attention_reference (kernels/reference.py:162-294), backend fp8, in
-    fp32 value units.  q,k,v: (G,N,D) float32.  Returns (G,N,D) float32.
+    fp32 value units.  q,k,v: (G,N,D) float32.  Returns (G,N,D) float32, or
+    (G,q_rows,D) when only the first ``q_rows`` query rows are wanted (the
+    CPU-baseline sample; every query row costs the same).
     """
     g, n, d = q.shape
     if scale is None:
@@ -530,9 +532,10 @@ def attention_reference(q, k, v, perm=None, block_rows=128, block_m=64, expcast=
     q_hat = (e4m3_decode(qc) * qsc[..., None]).astype(np.float32)
     k_hat = (e4m3_decode(kc) * ksc[..., None]).astype(np.float32)
     inv_p = F32(1.0 / P_SCALE)
-    out = np.zeros((g, n, d), np.float32)
-    for sm in range(0, n, block_m):
-        em = min(n, sm + block_m)
+    n_out = n if q_rows is None else min(n, q_rows)
+    out = np.zeros((g, n_out, d), np.float32)
+    for sm in range(0, n_out, block_m):
+        em = min(n_out, sm + block_m)
         qb = (q_hat[:, sm:em, :] * F32(scale)).astype(np.float32)
         mb = np.full((g, em - sm), -np.inf, np.float32)
         lb = np.zeros((g, em - sm), np.float32)

@@ -254,12 +254,22 @@ def test_attention_config0(dev, expcast):
 @pytest.mark.parametrize("n,br,d,h", [(200, 128, 128, 2), (1000, 64, 128, 2), (700, 128, 64, 3),
                                       (64, 64, 128, 1), (2048, 128, 128, 2)])
 def test_attention_shapes(dev, n, br, d, h):
+    """Ragged N, head_dim 64, single tile.  For N not a multiple of the block,
+    the reference's prepare() takes the K token mean over N rows while its
+    vc_attention_reference takes it over the padded rows; the kernel follows
+    prepare() (whose bytes it reproduces), so the tight check is against the
+    code-unit oracle on those bytes and the reference path is compared by
+    PSNR (and by rel-L2 when the two definitions coincide)."""
     q, k, v = make_qkv(1, h, n, d, seed=n + d)
     qg, kg, vg = (a.reshape(h, n, d) for a in (q, k, v))
     perm = np.stack([np.random.default_rng(i).permutation(n) for i in range(h)]).astype(np.int32)
     got = _attn_gpu(q, k, v, perm, br, dev)
+    prep = O.prepare(qg, kg, vg, perm, block_rows=br)
+    codes = O.attention_codes(prep, n, br, 64, d ** -0.5)
+    assert O.rel_l2(got, codes) <= REL_L2_CODES
     ref = O.attention_reference(qg, kg, vg, perm, block_rows=br, block_m=64)
-    assert O.rel_l2(got, ref) <= REL_L2_REF
+    if n % br == 0:
+        assert O.rel_l2(got, ref) <= REL_L2_REF
     sd = O.sdpa_f32(qg, kg, vg)
     assert abs(O.psnr(got, sd) - O.psnr(ref, sd)) <= PSNR_DB
 
