@@ -111,6 +111,13 @@ bool dtype_ok(int dtype) {
 
 }  // namespace
 
+namespace vcattn {
+// Lets entry points defined in other translation units report through
+// vcattn_last_error().
+int record_error(int code, const char* msg) { return fail(code, msg); }
+void clear_error() { g_last_error.clear(); }
+}  // namespace vcattn
+
 extern "C" {
 
 int vcattn_abi_version(void) { return 1; }

@@ -73,6 +73,10 @@ _SIGNATURES = {
                                    c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                    c_void_p, c_void_p, POINTER(RouteStats), c_void_p, c_size_t,
                                    c_void_p]),
+    "vcattn_prepare_fp8_noalloc": (c_int, [POINTER(BHND), POINTER(BHND), POINTER(BHND), c_int, c_int,
+                                           c_int, c_int, c_int, c_void_p, c_int, c_int, c_int,
+                                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                           c_void_p, c_void_p, POINTER(RouteStats), c_void_p]),
     "vcattn_route_mask": (c_int, [POINTER(RouteStats), c_int, c_int, c_int, c_int, c_int, c_float,
                                   c_int, c_int, c_float, c_void_p, c_void_p, c_void_p]),
     "vcattn_attn_fp8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

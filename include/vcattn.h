@@ -121,6 +121,24 @@ VCATTN_API int vcattn_prepare_fp8(const vcattn_bhnd* q, const vcattn_bhnd* k, co
                        const vcattn_route_stats* route,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- prepare without a workspace (no counterpart in the reference) ------
+ * Same inputs, outputs and results as vcattn_prepare_fp8, for callers that
+ * cannot allocate device memory: a host that owns every device byte through
+ * its own pool and forbids plugins to allocate, or a plain FFI binding with no
+ * device allocator.  Its scratch is a 16 MiB array inside the library, which
+ * every GPU that loads the library holds until the process exits.  Shapes
+ * whose scratch exceeds it (G * ceil(N/256) * D * 8 + G * D * 4 bytes when
+ * VCATTN_SMOOTH_K is set) are rejected with VCATTN_ERR_ARG before any launch.
+ * The first call on a device looks the array's address up (with that device
+ * current) and should come before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race and must be serialised. */
+VCATTN_API int vcattn_prepare_fp8_noalloc(const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_bhnd* v,
+                                          int dtype, int B, int H, int N, int D,
+                                          const int32_t* perm, int perm_rows, int block_rows, int flags,
+                                          uint8_t* q8, float* q_scale, uint8_t* k8, float* k_scale,
+                                          uint8_t* v8, float* v_scale, float* mu, uint8_t* v8t,
+                                          const vcattn_route_stats* route, void* stream);
+
 /* ---- routing mask: triton_attn.py:449-459 with the threshold of :716-735 -
  * keep (G, NP/q_block, NB) uint8: 1 = exact tile, 0 = block-mean approximation.
  * thresh (G, NP/q_block) fp32 output (may be NULL). */
