@@ -238,20 +238,48 @@ static int attn_common_checks(const char* name, const uint8_t* q8, const float* 
 }
 
 int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
-                    const uint8_t* v8t, const float* v_scale, const float* mu, int B, int H, int N, int n_pad,
+                    const uint8_t* v8, const float* v_scale, const float* mu, int B, int H, int N, int n_pad,
                     int D, int block_rows, float sm_scale, int flags, double expcast_beta, void* out,
                     int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn, void* stream) {
   g_last_error.clear();
   if (injected("vcattn_attn_fp8")) return fail(VCATTN_ERR_INJECTED, "vcattn_attn_fp8: injected fault");
-  const int rc = attn_common_checks("vcattn_attn_fp8", q8, q_scale, k8, k_scale, v8t, v_scale, mu, B, H, N, n_pad,
+  const int rc = attn_common_checks("vcattn_attn_fp8", q8, q_scale, k8, k_scale, v8, v_scale, mu, B, H, N, n_pad,
                                     D, block_rows, out, out_dtype);
+  if (rc != VCATTN_OK) return rc;
+  VC_CHECK(D == 128, "vcattn_attn_fp8: the tcgen05 kernel needs D = 128 (use vcattn_attn_fp8_mma for D = 64)");
+  VC_CHECK(aligned16(out) && (out_sn % 8) == 0 && (out_sh % 8) == 0 && (out_sb % 8) == 0,
+           "vcattn_attn_fp8: out must be 16-byte aligned with 8-element multiple strides");
+  AttnParams p{};
+  p.q8 = q8; p.k8 = k8; p.v8 = v8; p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
+  p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
+  p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
+  p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
+  return cuda_status(launch_attn_tc(p, static_cast<cudaStream_t>(stream)), "vcattn_attn_fp8");
+}
+
+int vcattn_attn_fp8_mma(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
+                        const uint8_t* v8t, const float* v_scale, const float* mu, int B, int H, int N, int n_pad,
+                        int D, int block_rows, float sm_scale, int flags, double expcast_beta, void* out,
+                        int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn, void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_attn_fp8_mma")) return fail(VCATTN_ERR_INJECTED, "vcattn_attn_fp8_mma: injected fault");
+  const int rc = attn_common_checks("vcattn_attn_fp8_mma", q8, q_scale, k8, k_scale, v8t, v_scale, mu, B, H, N,
+                                    n_pad, D, block_rows, out, out_dtype);
   if (rc != VCATTN_OK) return rc;
   AttnParams p{};
   p.q8 = q8; p.k8 = k8; p.v8t = v8t; p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
   p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
   p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
   p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
-  return cuda_status(launch_attn_mma(p, static_cast<cudaStream_t>(stream)), "vcattn_attn_fp8");
+  return cuda_status(launch_attn_mma(p, static_cast<cudaStream_t>(stream)), "vcattn_attn_fp8_mma");
+}
+
+int vcattn_attn_status(int* code, int* where, int* block, int reset) {
+  g_last_error.clear();
+  VC_CHECK(code && where && block, "vcattn_attn_status: null output");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "vcattn_attn_status");
+  return cuda_status(attn_tc_status(code, where, block, reset != 0), "vcattn_attn_status");
 }
 
 int vcattn_attn_fp8_sparse(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,

@@ -250,39 +250,69 @@ def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         raise NotImplementedError("NVFP4 QK^T kernel is not built in this version")
     br = cfg.block_n
     sparse = bool(cfg.sparse)
+    use_tc = d == 128 and not sparse
     p = prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
-                tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=False, want_v_t=True,
+                tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=use_tc, want_v_t=not use_tc,
                 local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks)
     out = _out_view(q, q.dtype)
     return attention_prepared(p, n, out, scale, cfg)
 
 
 def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
-                       cfg: TritonConfig) -> torch.Tensor:
-    """Run the attention kernel on prepared operands, writing into ``out``."""
+                       cfg: TritonConfig, kernel: str = "auto") -> torch.Tensor:
+    """Run the attention kernel on prepared operands, writing into ``out``.
+
+    kernel: "tc" (tcgen05, D = 128, needs ``p.v``), "mma" (register MMA,
+    needs ``p.v_t``) or "auto" (tcgen05 whenever it applies).  The sparse
+    path always runs on the register-MMA kernel.
+    """
     lib = N.lib()
     b, h, n_pad, d = p.q.shape
-    g = b * h
     flags = N.EXPCAST if cfg.enable_expcast else 0
     odt = _dtype_code(out)
     q8 = p.q.view(torch.uint8)
     k8 = p.k.view(torch.uint8)
-    if p.v_t is None:
-        raise ValueError("attention needs the block-transposed V codes (prepare(want_v_t=True))")
+    st = _stream(out)
     if cfg.sparse:
+        if p.v_t is None:
+            raise ValueError("the sparse kernel needs the block-transposed V codes (want_v_t=True)")
         N.check("vcattn_attn_fp8_sparse", lib.vcattn_attn_fp8_sparse(
             q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
             p.v_t.data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), p.k_mean.data_ptr(),
             p.v_mean.data_ptr(), p.keep.data_ptr(), cfg.block_m, cfg.group, b, h, n, n_pad, d,
             p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
-            out.stride(0), out.stride(1), out.stride(2), _stream(out)))
-    else:
+            out.stride(0), out.stride(1), out.stride(2), st))
+        return out
+    if kernel == "auto":
+        kernel = "tc" if (d == 128 and p.v is not None) else "mma"
+    if kernel == "tc":
+        if p.v is None:
+            raise ValueError("the tcgen05 kernel reads V in the Prepared layout (want_v=True)")
         N.check("vcattn_attn_fp8", lib.vcattn_attn_fp8(
+            q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
+            p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), b, h, n, n_pad, d,
+            p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
+            out.stride(0), out.stride(1), out.stride(2), st))
+    else:
+        if p.v_t is None:
+            raise ValueError("the register-MMA kernel needs the block-transposed V codes (want_v_t=True)")
+        N.check("vcattn_attn_fp8_mma", lib.vcattn_attn_fp8_mma(
             q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
             p.v_t.data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), b, h, n, n_pad, d,
             p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
-            out.stride(0), out.stride(1), out.stride(2), _stream(out)))
+            out.stride(0), out.stride(1), out.stride(2), st))
     return out
+
+
+def attention_status(reset: bool = True):
+    """(code, where, block) of the tcgen05 kernels' device status word; code 0
+    means every bounded wait completed.  Synchronises the device."""
+    import ctypes
+    code, where, block = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    lib = N.lib()
+    N.check("vcattn_attn_status", lib.vcattn_attn_status(ctypes.byref(code), ctypes.byref(where),
+                                                          ctypes.byref(block), 1 if reset else 0))
+    return code.value, where.value, block.value
 
 
 vc_attention_triton = vc_attention_cuda

@@ -147,15 +147,31 @@ VCATTN_API int vcattn_route_mask(const vcattn_route_stats* route, int G, int N, 
                       float sm_scale, uint8_t* keep, float* thresh, void* stream);
 
 /* ---- fused dense FP8 attention: triton_attn.py:203-322 (+ launch :831-844)
- * Consumes the prepare outputs (V as the block-transposed v8t); writes O
- * (B,H,N,D) through the out view (out_dtype one of the three dtypes; out
- * strides in elements). */
+ * The tcgen05 kernel (D = 128, block_rows 64 or 128).  Consumes the prepare
+ * outputs in the Prepared layout (v8 row-major (G,NP,D)); writes O (B,H,N,D)
+ * through the out view (out_dtype one of the three dtypes; strides in
+ * elements).  Its bounded waits report through vcattn_attn_status(). */
 VCATTN_API int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8,
+                    const float* k_scale, const uint8_t* v8, const float* v_scale,
+                    const float* mu, int B, int H, int N, int n_pad, int D,
+                    int block_rows, float sm_scale, int flags, double expcast_beta,
+                    void* out, int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn,
+                    void* stream);
+
+/* Same computation on the register-MMA (mma.sync m16n8k32) kernel, for head
+ * dims 64 and 128; V as the block-transposed v8t (G,NB,D,block_rows).  P bytes
+ * follow the reference's ExpCast operation order exactly. */
+VCATTN_API int vcattn_attn_fp8_mma(const uint8_t* q8, const float* q_scale, const uint8_t* k8,
                     const float* k_scale, const uint8_t* v8t, const float* v_scale,
                     const float* mu, int B, int H, int N, int n_pad, int D,
                     int block_rows, float sm_scale, int flags, double expcast_beta,
                     void* out, int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn,
                     void* stream);
+
+/* Device status word of the tcgen05 kernels: code 0 = ok, 1 = a bounded wait
+ * expired (the kernel gave up and returned); where = which wait; block = the
+ * first failing CTA.  Synchronises the current device.  reset != 0 clears it. */
+VCATTN_API int vcattn_attn_status(int* code, int* where, int* block, int reset);
 
 /* ---- fused block-sparse FP8 attention: triton_attn.py:384-501 ----------
  * keep from vcattn_route_mask; k_mean/v_mean (G,NB,D) fp32; q_block rows per

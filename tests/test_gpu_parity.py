@@ -223,23 +223,31 @@ def test_prepare_without_hadamard_or_smoothing(dev):
 
 # ------------------------------------------------------------- attention ----
 
-def _attn_gpu(q, k, v, perm, br, dev, expcast=False, out_dtype=torch.float32):
+def _attn_gpu(q, k, v, perm, br, dev, expcast=False, out_dtype=torch.float32, kernel="mma"):
     from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig,
-                                                                          attention_prepared)
-    p = _prep_gpu(q, k, v, perm, br, dev, want_v=False, want_v_t=True)
+                                                                          attention_prepared,
+                                                                          attention_status)
+    p = _prep_gpu(q, k, v, perm, br, dev, want_v=True, want_v_t=True)
     b, h, n, d = q.shape
     out = torch.empty((b, h, n, d), dtype=out_dtype, device=dev)
     cfg = TritonConfig(block_n=br, enable_expcast=expcast)
-    attention_prepared(p, n, out, d ** -0.5, cfg)
+    attention_prepared(p, n, out, d ** -0.5, cfg, kernel=kernel)
     torch.cuda.synchronize()
+    if kernel == "tc":
+        assert attention_status() == (0, 0, 0), "a bounded wait of the tcgen05 kernel expired"
     return out.float().cpu().numpy().reshape(b * h, n, d)
 
 
+def _kernels(d):
+    return ["tc", "mma"] if d == 128 else ["mma"]
+
+
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
 @pytest.mark.parametrize("expcast", [False, True])
-def test_attention_config0(dev, expcast):
+def test_attention_config0(dev, expcast, kernel):
     g = _load("config0.npz")
     q, k, v = make_qkv(1, 2, 1024, 128, seed=0)
-    got = _attn_gpu(q, k, v, g["perm"], 64, dev, expcast=expcast)
+    got = _attn_gpu(q, k, v, g["perm"], 64, dev, expcast=expcast, kernel=kernel)
     G = 2
     qg, kg, vg = (a.reshape(G, 1024, 128) for a in (q, k, v))
     ref = g["out_expcast" if expcast else "out_plain"].reshape(G, 1024, 128)
@@ -253,7 +261,8 @@ def test_attention_config0(dev, expcast):
 
 @pytest.mark.parametrize("n,br,d,h", [(200, 128, 128, 2), (1000, 64, 128, 2), (700, 128, 64, 3),
                                       (64, 64, 128, 1), (2048, 128, 128, 2)])
-def test_attention_shapes(dev, n, br, d, h):
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
+def test_attention_shapes(dev, n, br, d, h, kernel):
     """Ragged N, head_dim 64, single tile.  For N not a multiple of the block,
     the reference's prepare() takes the K token mean over N rows while its
     vc_attention_reference takes it over the padded rows; the kernel follows
@@ -263,7 +272,9 @@ def test_attention_shapes(dev, n, br, d, h):
     q, k, v = make_qkv(1, h, n, d, seed=n + d)
     qg, kg, vg = (a.reshape(h, n, d) for a in (q, k, v))
     perm = np.stack([np.random.default_rng(i).permutation(n) for i in range(h)]).astype(np.int32)
-    got = _attn_gpu(q, k, v, perm, br, dev)
+    if kernel not in _kernels(d):
+        pytest.skip("the tcgen05 kernel is built for head_dim 128")
+    got = _attn_gpu(q, k, v, perm, br, dev, kernel=kernel)
     prep = O.prepare(qg, kg, vg, perm, block_rows=br)
     codes = O.attention_codes(prep, n, br, 64, d ** -0.5)
     assert O.rel_l2(got, codes) <= REL_L2_CODES
