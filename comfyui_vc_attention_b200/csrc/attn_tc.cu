@@ -36,7 +36,7 @@ using namespace tc;
 constexpr int kBM = 128;
 constexpr int kD = 128;
 constexpr int kStages = 3;
-constexpr int kThreads = 320;   // 10 warps: 65536 / 320 = 204 registers per thread
+constexpr int kThreads = 320;   // 10 warps at <= 192 registers each (61440 of 65536)
 constexpr uint32_t kColS = 0, kColT = 256, kColR = 384;
 
 template <int BR>
@@ -168,7 +168,7 @@ __device__ __forceinline__ void store_row(void* out, int64_t off, const float (&
 }
 
 template <int BR, bool EXPCAST, int ODT>
-__global__ void __maxnreg__(200)
+__global__ void __maxnreg__(192)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
