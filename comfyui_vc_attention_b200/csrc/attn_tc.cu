@@ -8,11 +8,13 @@
 //   acc = alpha * acc + (P @ V8) * (vs / 448) + (rowsum(P) / 448) * (mu * vs)
 //   l   = alpha * l + rowsum(P) / 448 ;  O = acc / l
 //
-// One CTA = 128 query rows of one (batch, head); 10 warps:
+// One CTA = 128 query rows of one (batch, head); 12 warps (register-limited
+// blocks are sized in whole warpgroups, so the 168-register budget needs 384
+// threads, of which warps 2-3 are idle):
 //   warp 0      TMA producer (Q once; K, V codes + ks, vs, mu per tile, 3 stages)
 //   warp 1      MMA issuer and TMEM owner
-//   warps 2-5   softmax: thread = query row = TMEM lane; P row -> shared memory
-//   warps 6-9   correction: thread = row; O row in registers
+//   warps 4-7   softmax: thread = query row = TMEM lane; P row -> shared memory
+//   warps 8-11  correction: thread = row; O row in registers
 // A warp reads TMEM lanes 32 * (warp % 4) .. +31, so each group of four
 // consecutive warps covers the 128 rows once.
 // TMEM columns: S double buffer [0,128) [128,256), PV tile T [256,384),
@@ -20,6 +22,7 @@
 // Operands in shared memory use the 128-byte swizzle: Q, K and P K-major, V
 // MN-major (straight from the prepare layout).  Every wait is bounded.
 #include <cuda.h>
+#include <cstdio>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -32,11 +35,12 @@ __device__ tc::DevStatus g_attn_tc_status;
 namespace {
 
 using namespace tc;
+char g_tc_diag[256];
 
 constexpr int kBM = 128;
 constexpr int kD = 128;
 constexpr int kStages = 3;
-constexpr int kThreads = 320;   // 10 warps at <= 192 registers each (61440 of 65536)
+constexpr int kThreads = 384;   // 12 warps (3 warpgroups) at <= 168 registers each
 constexpr uint32_t kColS = 0, kColT = 256, kColR = 384;
 
 template <int BR>
@@ -168,7 +172,7 @@ __device__ __forceinline__ void store_row(void* out, int64_t off, const float (&
 }
 
 template <int BR, bool EXPCAST, int ODT>
-__global__ void __maxnreg__(192)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -295,7 +299,7 @@ __global__ void __maxnreg__(192)
       }
     }
     __syncwarp();
-  } else if (warp >= 2 && warp < 6) {
+  } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ softmax
     const int t = (warp & 3) * 32 + lane;          // query row within the tile = TMEM lane
     const uint32_t lane_base = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -380,7 +384,7 @@ __global__ void __maxnreg__(192)
       mbar_arrive(&sm.a_full[j & 3]);
       m = m_new;
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 8) {
     // ------------------------------------------------------------ correction
     const int t = (warp & 3) * 32 + lane;
     const uint32_t lane_base = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -407,22 +411,22 @@ __global__ void __maxnreg__(192)
       tc_fence_after();
       const float alpha = sm.alpha[i & 3][t];
       const float rsum = tmem_ld1(lane_base + kColR);
-      float tv[32];
-      tmem_ld32(lane_base + kColT, tv);
+      float tv[16];
+      tmem_ld16(lane_base + kColT, tv);
       tmem_ld_wait();
       const float r = __fdiv_rn(rsum, 448.0f);
       const float* cv = sm.cm[bi][0];
       const float* mv = sm.cm[bi][1];
       const bool rescale = !__all_sync(0xffffffffu, alpha == 1.0f);
 #pragma unroll
-      for (int q = 0; q < kD / 32; ++q) {
+      for (int q = 0; q < kD / 16; ++q) {
         if (q > 0) {
-          tmem_ld32(lane_base + kColT + q * 32, tv);
+          tmem_ld16(lane_base + kColT + q * 16, tv);
           tmem_ld_wait();
         }
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const int col = q * 32 + c;
+        for (int c = 0; c < 16; c += 2) {
+          const int col = q * 16 + c;
           if (rescale) mul2(o[col], o[col + 1], alpha, alpha);
           const float2 cc = *reinterpret_cast<const float2*>(cv + col);
           const float2 mm = *reinterpret_cast<const float2*>(mv + col);
@@ -493,7 +497,16 @@ cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const dim3 grid((p.n_pad + kBM - 1) / kBM, p.B * p.H);
   k<<<grid, kThreads, smem, st>>>(mq, mk, mv, a);
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, k);
+    snprintf(g_tc_diag, sizeof(g_tc_diag),
+             "regs=%d maxThreadsPerBlock=%d staticSmem=%zu dynSmem=%zu maxDynSmem=%d local=%zu threads=%d",
+             fa.numRegs, fa.maxThreadsPerBlock, fa.sharedSizeBytes, smem, fa.maxDynamicSharedSizeBytes,
+             fa.localSizeBytes, kThreads);
+  }
+  return e;
 }
 
 template <int BR>
@@ -515,6 +528,8 @@ cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t st) {
   if (p.D != 128) return cudaErrorNotSupported;
   return p.block_rows == 128 ? dispatch_tc<128>(p, st) : dispatch_tc<64>(p, st);
 }
+
+const char* attn_tc_diag() { return g_tc_diag; }
 
 cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset) {
   tc::DevStatus s{};

@@ -254,7 +254,10 @@ int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8, 
   p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
   p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
   p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
-  return cuda_status(launch_attn_tc(p, static_cast<cudaStream_t>(stream)), "vcattn_attn_fp8");
+  const cudaError_t e = launch_attn_tc(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(VCATTN_ERR_CUDA, std::string("vcattn_attn_fp8: ") + cudaGetErrorString(e) + " [" + attn_tc_diag() + "]");
+  return VCATTN_OK;
 }
 
 int vcattn_attn_fp8_mma(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,

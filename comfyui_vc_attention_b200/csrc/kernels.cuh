@@ -62,6 +62,7 @@ cudaError_t launch_kmeans(const KMeansParams& p, cudaStream_t st);
 cudaError_t launch_attn_mma(const AttnParams& p, cudaStream_t st);
 cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t st);
 cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset);
+const char* attn_tc_diag();
 cudaError_t launch_attn_sparse_mma(const AttnParams& p, cudaStream_t st);
 cudaError_t launch_codecs_e4m3(const float* x, int64_t n, uint8_t* out, cudaStream_t st);
 cudaError_t launch_codecs_fp4(const float* x, int64_t n, uint8_t* out, cudaStream_t st);
