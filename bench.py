@@ -44,6 +44,9 @@ WORKLOADS = {
     "c1": dict(desc="configs[1]: dense FP8 VC-Attention, B1 H56 N16384 D128, ExpCast on, Hadamard on, "
                     "V-Smooth k=64", B=1, H=56, N=16384, D=128, expcast=True, sparse=False, k=64,
                block_rows=128, spatial=None),
+    "c1h16": dict(desc="profiling slice of configs[1]: B1 H16 N16384 D128, ExpCast on, V-Smooth k=64",
+                  B=1, H=16, N=16384, D=128, expcast=True, sparse=False, k=64, block_rows=128,
+                  spatial=None),
     "c3": dict(desc="dense FP8 VC-Attention, B1 H56 N65536 D128, ExpCast on, V-Smooth k=512",
                B=1, H=56, N=65536, D=128, expcast=True, sparse=False, k=512, block_rows=128, spatial=None),
 }
@@ -222,6 +225,8 @@ def main() -> int:
     ap.add_argument("--workload", default="c1", choices=sorted(WORKLOADS))
     ap.add_argument("--cpu-rows", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="timed steps only (no e2e, PSNR or CPU baseline): the command profiled by ncu")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -302,6 +307,14 @@ def main() -> int:
     ms_per_step = total_ms / args.steps
     fl = flops_per_call(w)
     value = world * fl / (ms_per_step / 1e3) / 1e12
+
+    if args.profile:
+        if rank == 0:
+            print(json.dumps({"profile": args.workload, "ms_per_step": ms_per_step, "ms_prepare": prep_ms,
+                              "ms_attention": attn_ms}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
 
     # ---- end to end through the public entry point, host buffers ----------
     q_h = q.cpu().pin_memory()
