@@ -53,7 +53,7 @@ struct TcSmem {
   alignas(16) float ks[kStages][BR];
   alignas(16) float vs[kStages][kD];
   alignas(16) float mu[kStages][kD];
-  alignas(16) float cm[2][2][kD];
+  alignas(16) float cm[4][2][kD];    // per tile: vs / 448 and mu * vs (softmax -> correction)
   alignas(16) float alpha[4][kBM];
   alignas(8) uint64_t q_full;
   alignas(8) uint64_t kv_full[kStages];
@@ -116,23 +116,6 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
   asm("fma.rn.sat.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
-__device__ __forceinline__ void named_bar(int id, int count) {
-  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
-}
-// Named barrier that also ANDs a predicate over the participating threads.
-__device__ __forceinline__ bool named_bar_and(int id, int count, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 q, %1, 0;\n\t"
-      "bar.red.and.pred p, %2, %3, q;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
-
 template <int ODT>
 __device__ __forceinline__ void store_row(void* out, int64_t off, const float (&o)[kD], float l) {
   if constexpr (ODT == VCATTN_DTYPE_BF16) {
@@ -190,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&sm.q_full, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 2);
+      mbar_init(&sm.kv_empty[s], 1 + kBM);   // PV commit + the 128 softmax threads
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.s_full[b], 1);
@@ -216,6 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = sm.tmem_base;
   volatile int* abort = &sm.abort;
 
+  if (warp < 4) {
+  // Register budget per warpgroup (launched at 168 x 384 = 64512):
+  // 128 x 56 (producer, MMA, 2 idle) + 128 x 200 (softmax) + 128 x 232 (correction) = 62464.
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     int issued = 0;
@@ -299,7 +286,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp >= 4 && warp < 8) {
+  }
+  } else if (warp < 8) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
     // ------------------------------------------------------------ softmax
     const int t = (warp & 3) * 32 + lane;          // query row within the tile = TMEM lane
     const uint32_t lane_base = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -380,11 +369,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&sm.p_full[b]);
+      // Per-tile column factors for the correction warps (thread t = channel t).
+      const float vsc = sm.vs[s][t];
+      sm.cm[j & 3][0][t] = __fdiv_rn(vsc, 448.0f);
+      sm.cm[j & 3][1][t] = __fmul_rn(sm.mu[s][t], vsc);
       sm.alpha[j & 3][t] = alpha;
+      mbar_arrive(&sm.kv_empty[s]);
       mbar_arrive(&sm.a_full[j & 3]);
       m = m_new;
     }
-  } else if (warp >= 8) {
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;\n" ::: "memory");
     // ------------------------------------------------------------ correction
     const int t = (warp & 3) * 32 + lane;
     const uint32_t lane_base = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -394,39 +389,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.f;
     bool ok = true;
     for (int i = 0; i < nb; ++i) {
-      const int s = i % kStages, bi = i & 1;
+      const int ri = i & 3;
       ok = mbar_wait(&sm.t_full, i & 1, abort, status, 10) &&
-           mbar_wait(&sm.kv_full[s], (i / kStages) & 1, abort, status, 11) &&
-           mbar_wait(&sm.a_full[i & 3], (i >> 2) & 1, abort, status, 12);
-      // All four correction warps leave together or not at all, so no thread
-      // is ever left waiting at the named barrier below.
-      ok = named_bar_and(1, 128, ok);
+           mbar_wait(&sm.a_full[ri], (i >> 2) & 1, abort, status, 12);
       if (!ok) break;
-      // Per-tile column factors: c = vs / 448, m = mu * vs (one channel per thread).
-      const float vsc = sm.vs[s][t];
-      sm.cm[bi][0][t] = __fdiv_rn(vsc, 448.0f);
-      sm.cm[bi][1][t] = __fmul_rn(sm.mu[s][t], vsc);
-      named_bar(1, 128);
-      if (t == 0) mbar_arrive(&sm.kv_empty[s]);
       tc_fence_after();
-      const float alpha = sm.alpha[i & 3][t];
+      const float alpha = sm.alpha[ri][t];
+      const float* cv = sm.cm[ri][0];
+      const float* mv = sm.cm[ri][1];
+      const bool rescale = !__all_sync(0xffffffffu, alpha == 1.0f);
+      float tv[64];
       const float rsum = tmem_ld1(lane_base + kColR);
-      float tv[16];
-      tmem_ld16(lane_base + kColT, tv);
+      tmem_ld32(lane_base + kColT, *reinterpret_cast<float(*)[32]>(&tv[0]));
+      tmem_ld32(lane_base + kColT + 32, *reinterpret_cast<float(*)[32]>(&tv[32]));
       tmem_ld_wait();
       const float r = __fdiv_rn(rsum, 448.0f);
-      const float* cv = sm.cm[bi][0];
-      const float* mv = sm.cm[bi][1];
-      const bool rescale = !__all_sync(0xffffffffu, alpha == 1.0f);
 #pragma unroll
-      for (int q = 0; q < kD / 16; ++q) {
-        if (q > 0) {
-          tmem_ld16(lane_base + kColT + q * 16, tv);
+      for (int h = 0; h < 2; ++h) {
+        if (h == 1) {
+          tmem_ld32(lane_base + kColT + 64, *reinterpret_cast<float(*)[32]>(&tv[0]));
+          tmem_ld32(lane_base + kColT + 96, *reinterpret_cast<float(*)[32]>(&tv[32]));
           tmem_ld_wait();
+          tc_fence_before();
+          mbar_arrive(&sm.t_free);          // T fully read: the next PV may start
         }
 #pragma unroll
-        for (int c = 0; c < 16; c += 2) {
-          const int col = q * 16 + c;
+        for (int c = 0; c < 64; c += 2) {
+          const int col = h * 64 + c;
           if (rescale) mul2(o[col], o[col + 1], alpha, alpha);
           const float2 cc = *reinterpret_cast<const float2*>(cv + col);
           const float2 mm = *reinterpret_cast<const float2*>(mv + col);
@@ -434,8 +423,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           fma2(o[col], o[col + 1], r, r, mm.x, mm.y);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&sm.t_free);
       l = __fadd_rn(__fmul_rn(l, alpha), r);
     }
     const int row = row0 + t;
