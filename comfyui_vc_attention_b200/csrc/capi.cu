@@ -298,7 +298,7 @@ int vcattn_attn_fp8_sparse(const uint8_t* q8, const float* q_scale, const uint8_
   if (rc != VCATTN_OK) return rc;
   VC_CHECK(k_mean && v_mean && keep, "vcattn_attn_fp8_sparse: missing routing inputs");
   VC_CHECK(q_block == 64 && n_pad % q_block == 0, "vcattn_attn_fp8_sparse: q_block must be 64");
-  VC_CHECK(group >= 1 && group <= 64, "vcattn_attn_fp8_sparse: group out of range");
+  VC_CHECK(group == 16, "vcattn_attn_fp8_sparse: group must be 16 (TritonConfig.group default)");
   AttnParams p{};
   p.q8 = q8; p.k8 = k8; p.v8t = v8t; p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
   p.k_mean = k_mean; p.v_mean = v_mean; p.keep = keep; p.q_block = q_block; p.group = group;

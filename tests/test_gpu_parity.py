@@ -337,3 +337,86 @@ def test_router_routes_and_defers(dev):
     finally:
         uninstall()
     assert F.scaled_dot_product_attention is orig
+
+
+# ------------------------------------------------------- block-sparse path ----
+
+def _sparse_case(n=1024, h=2, seed=3, grid=(4, 16, 16)):
+    q, k, v = make_qkv(1, h, n, 128, seed=seed, spatial=grid)
+    G = h
+    vb = v.reshape(G, n, 128)
+    perm, _, _, _ = O.build_permutation(vb, block_rows=128, iters=3)
+    return q, k, v, perm
+
+
+@pytest.mark.parametrize("tau,local,sink", [(1.3, 1, 0), (0.5, 0, 1), (2.0, 1, 2)])
+def test_route_mask_bit_exact(dev, tau, local, sink):
+    n, h, br, qb = 1024, 2, 128, 64
+    q, k, v, perm = _sparse_case(n, h)
+    sc = 128 ** -0.5
+    p = _prep_gpu(q, k, v, perm, br, dev, sparse=True, tau=tau, q_block=qb, want_v_t=True,
+                  local_blocks=local, sink_blocks=sink)
+    prep = O.prepare(q.reshape(h, n, 128), k.reshape(h, n, 128), v.reshape(h, n, 128), perm, block_rows=br)
+    st = O.route_stats(prep, br, qb, tau, sc)
+    keep, score = O.route_mask(prep, st, n, br, qb, sc, local_blocks=local, sink_blocks=sink)
+    assert np.array_equal(p.k_mean.reshape(st["k_mean"].shape).cpu().numpy(), st["k_mean"])
+    assert np.array_equal(p.v_mean.reshape(st["v_mean"].shape).cpu().numpy(), st["v_mean"])
+    assert np.array_equal(p.thresh.reshape(st["thresh"].shape).cpu().numpy(), st["thresh"])
+    got = p.keep.cpu().numpy().astype(bool)
+    assert np.array_equal(got, keep)
+    assert 0.0 < keep.mean() < 1.0, "routing must be non-trivial on the spatial inputs"
+
+
+def _sparse_gpu(q, k, v, perm, dev, tau, local=1, sink=0, expcast=False, out_dtype=torch.float32):
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import TritonConfig, attention_prepared
+    b, h, n, d = q.shape
+    p = _prep_gpu(q, k, v, perm, 128, dev, sparse=True, tau=tau, q_block=64, want_v_t=True,
+                  local_blocks=local, sink_blocks=sink)
+    out = torch.empty((b, h, n, d), dtype=out_dtype, device=dev)
+    cfg = TritonConfig(block_m=64, block_n=128, sparse=True, tau=tau, local_blocks=local, sink_blocks=sink,
+                       enable_expcast=expcast)
+    attention_prepared(p, n, out, d ** -0.5, cfg)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy().reshape(b * h, n, d), p
+
+
+@pytest.mark.parametrize("expcast", [False, True])
+def test_sparse_attention_matches_oracle(dev, expcast):
+    n, h = 1024, 2
+    q, k, v, perm = _sparse_case(n, h)
+    got, p = _sparse_gpu(q, k, v, perm, dev, tau=1.3, expcast=expcast)
+    qg, kg, vg = (a.reshape(h, n, 128) for a in (q, k, v))
+    prep = O.prepare(qg, kg, vg, perm, block_rows=128)
+    st = O.route_stats(prep, 128, 64, 1.3, 128 ** -0.5)
+    keep = p.keep.cpu().numpy().astype(bool)
+    ref = O.attention_sparse_codes(prep, st, keep, n, 128, 64, 128 ** -0.5, group=16, expcast=expcast)
+    assert O.rel_l2(got, ref) <= REL_L2_CODES
+    sd = O.sdpa_f32(qg, kg, vg)
+    assert O.psnr(got, sd) > 20.0
+
+
+def test_sparse_keep_all_equals_dense(dev):
+    """tau -> -inf keeps every block: the sparse kernel must reproduce the
+    dense register-MMA kernel bit for bit (exact tiles, same order)."""
+    n, h = 1024, 2
+    q, k, v, perm = _sparse_case(n, h)
+    sparse, p = _sparse_gpu(q, k, v, perm, dev, tau=-1000.0)
+    assert p.keep.bool().all()
+    dense = _attn_gpu(q, k, v, perm, 128, dev, kernel="mma")
+    assert np.array_equal(sparse, dense)
+
+
+def test_sparse_ragged_and_multi_group(dev):
+    """N not a multiple of the block, more than one 16-block group."""
+    n, h = 2500, 2
+    q, k, v = make_qkv(1, h, n, 128, seed=12)
+    perm = np.stack([np.random.default_rng(i).permutation(n) for i in range(h)]).astype(np.int32)
+    got, p = _sparse_gpu(q, k, v, perm, dev, tau=0.8, local=0)
+    qg, kg, vg = (a.reshape(h, n, 128) for a in (q, k, v))
+    prep = O.prepare(qg, kg, vg, perm, block_rows=128)
+    st = O.route_stats(prep, 128, 64, 0.8, 128 ** -0.5)
+    keep_o, _ = O.route_mask(prep, st, n, 128, 64, 128 ** -0.5, local_blocks=0)
+    keep = p.keep.cpu().numpy().astype(bool)
+    assert np.array_equal(keep, keep_o)
+    ref = O.attention_sparse_codes(prep, st, keep, n, 128, 64, 128 ** -0.5, group=16)
+    assert O.rel_l2(got, ref) <= REL_L2_CODES
