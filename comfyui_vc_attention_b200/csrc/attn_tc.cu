@@ -8,19 +8,30 @@
 //   acc = alpha * acc + (P @ V8) * (vs / 448) + (rowsum(P) / 448) * (mu * vs)
 //   l   = alpha * l + rowsum(P) / 448 ;  O = acc / l
 //
-// One CTA = 128 query rows of one (batch, head); 12 warps (register-limited
-// blocks are sized in whole warpgroups, so the 168-register budget needs 384
-// threads, of which warps 2-3 are idle):
-//   warp 0      TMA producer (Q once; K, V codes + ks, vs, mu per tile, 3 stages)
-//   warp 1      MMA issuer and TMEM owner
-//   warps 4-7   softmax: thread = query row = TMEM lane; P row -> shared memory
-//   warps 8-11  correction: thread = row; O row in registers
-// A warp reads TMEM lanes 32 * (warp % 4) .. +31, so each group of four
-// consecutive warps covers the 128 rows once.
-// TMEM columns: S double buffer [0,128) [128,256), PV tile T [256,384),
-// row sum R [384,400) (from an N=16 MMA of P against a ones block).
-// Operands in shared memory use the 128-byte swizzle: Q, K and P K-major, V
-// MN-major (straight from the prepare layout).  Every wait is bounded.
+// One CTA = 128 query rows of one (batch, head); 16 warps in 4 warpgroups:
+//   warp 0       TMA producer (Q once; K, V codes + ks, vs, mu per tile)
+//   warp 1       MMA issuer and TMEM owner
+//   warps 2-3    per-tile factors: vs / 448, mu * vs and ks, reordered for
+//                the fragments below
+//   warps 4-11   softmax, two warpgroups: warp w of group s reads TMEM lanes
+//                32 (w%4) + 16 s .. +15 with the 16x256b shape, so a thread
+//                owns 2 rows x 32 key columns (columns 8 grp + 2 (lane%4) +
+//                {0,1}); the row max is finished with two lane shuffles
+//   warps 12-15  correction: O in registers, 4 rows x 32 channels per thread
+// Row sums and per-column factors reach a thread only for the columns it
+// owns, which keeps shared-memory reads per tile small.
+// TMEM columns: S double buffer [0,128) [128,256); the P bytes (E4M3, four
+// keys per column) go over the first BR/4 columns of their S buffer and feed
+// the PV MMA from tensor memory; PV tile T_j double buffer [256,384)
+// [384,512); the row sum R_j (an N=16 MMA of P_j against an all-ones block)
+// goes to the first 16 columns of the other T buffer, whose first quarter
+// (T_{j-1}) the correction warps have already read.  Every MMA gate points at
+// least one MMA back, so the in-order tensor pipe never drains while a
+// handshake completes.
+// A thread's P bytes for keys 8 r + 2 q + e of each 32-key chunk land at
+// A-operand positions 8 q + 2 r + e, so V rows are stored in that order
+// (VCATTN_V_MMA_ORDER).  Q, K use the 128-byte swizzle K-major, V MN-major.
+// Every wait is bounded.
 #include <cuda.h>
 #include <cstdio>
 #include <mutex>
@@ -39,32 +50,53 @@ char g_tc_diag[256];
 
 constexpr int kBM = 128;
 constexpr int kD = 128;
-constexpr int kStages = 3;
-constexpr int kThreads = 384;   // 12 warps (3 warpgroups) at <= 168 registers each
-constexpr uint32_t kColS = 0, kColT = 256, kColR = 384;
+constexpr int kStages = 4;
+constexpr int kRing = 4;        // per-tile factor / alpha hand-off depth
+constexpr int kThreads = 512;   // 16 warps = 4 warpgroups
+constexpr uint32_t kColS = 0, kColT = 256;
+// Factor tables in fragment order: the 32 entries lane group q (= lane % 4)
+// reads are contiguous, groups 36 floats apart so their float4 reads fall
+// in different banks.
+constexpr int kFStride = 36;
+// channel c -> slot of (q = c/2 % 4, grp = c/8, e = c % 2)
+__host__ __device__ constexpr int cm_index(int c) { return ((c & 7) >> 1) * kFStride + (c >> 3) * 2 + (c & 1); }
+// key column k -> slot of (q = k/2 % 4, chunk = k/32, r = k/8 % 4, e = k % 2)
+__host__ __device__ constexpr int ks_index(int k) {
+  return ((k >> 1) & 3) * kFStride + (k >> 5) * 8 + ((k >> 3) & 3) * 2 + (k & 1);
+}
+
+// One arrival per warp: the lanes' earlier shared-memory and tensor-memory
+// work is ordered before lane 0's (release) arrive by __syncwarp.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
 
 template <int BR>
 struct TcSmem {
+  // q, k and v are contiguous: after the last tile they stage the output.
   alignas(1024) uint8_t q[kBM * 128];
   alignas(1024) uint8_t k[kStages][BR * 128];
   alignas(1024) uint8_t v[kStages][BR * 128];
-  alignas(1024) uint8_t p[2][kBM * 128];
   alignas(1024) uint8_t ones[16 * 128];
   alignas(16) float ks[kStages][BR];
   alignas(16) float vs[kStages][kD];
   alignas(16) float mu[kStages][kD];
-  alignas(16) float cm[4][2][kD];    // per tile: vs / 448 and mu * vs (softmax -> correction)
-  alignas(16) float alpha[4][kBM];
+  alignas(16) float cm[kRing][2][4 * kFStride];   // vs / 448 and mu * vs at cm_index
+  alignas(16) float ksf[kRing][4 * kFStride];     // ks at ks_index
+  alignas(16) float alpha[kRing][kBM];            // row r at 32 (r/32) + 4 (r%8) + (r%32)/8
   alignas(8) uint64_t q_full;
   alignas(8) uint64_t kv_full[kStages];
   alignas(8) uint64_t kv_empty[kStages];
   alignas(8) uint64_t s_full[2];
-  alignas(8) uint64_t s_free[2];
   alignas(8) uint64_t p_full[2];
-  alignas(8) uint64_t p_free[2];
-  alignas(8) uint64_t t_full;
-  alignas(8) uint64_t t_free;
-  alignas(8) uint64_t a_full[4];   // alpha of tile j ready (ring of 4, softmax -> correction)
+  alignas(8) uint64_t t_full[2];
+  alignas(8) uint64_t tr_free[2];  // T buffer b holds nothing unread (T_{i-1} done, R_i read)
+  alignas(8) uint64_t q0_free;     // first quarter of T_i read: R_{i+1} may land there
+  alignas(8) uint64_t a_full[kRing];
+  alignas(8) uint64_t a_free[kRing];
+  alignas(8) uint64_t f_full[kRing];
+  alignas(8) uint64_t f_free[kRing];
   alignas(8) uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -90,9 +122,8 @@ __device__ __forceinline__ void mul2(float& a, float& b, float x, float y) {
       : "+f"(a), "+f"(b)
       : "f"(x), "f"(y));
 }
-// (a, b) = (a, b) * (s, s) + (x, y) * (c0, c1) style helpers
+// (a, b) = (x0, x1) * (y0, y1) + (a, b)
 __device__ __forceinline__ void fma2(float& a, float& b, float x0, float x1, float y0, float y1) {
-  // (a, b) = (x0, x1) * (y0, y1) + (a, b)
   asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
       "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%0, %1};\n\t"
       "fma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}\n"
@@ -116,41 +147,34 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
   asm("fma.rn.sat.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
+// Four ExpCast codes (fma.sat to [0,1] in units of 128 codes, then + 98304
+// rounds to an integer in the low byte) packed into one word.
+__device__ __forceinline__ uint32_t expcast4(float x0, float x1, float x2, float x3, float As, float Bs) {
+  float c0 = fma_sat(x0, As, Bs), c1 = fma_sat(x1, As, Bs);
+  float c2 = fma_sat(x2, As, Bs), c3 = fma_sat(x3, As, Bs);
+  add2(c0, c1, 98304.0f, 98304.0f);
+  add2(c2, c3, 98304.0f, 98304.0f);
+  const uint32_t lo = __byte_perm(__float_as_uint(c0), __float_as_uint(c1), 0x0040);
+  const uint32_t hi = __byte_perm(__float_as_uint(c2), __float_as_uint(c3), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
+}
+__device__ __forceinline__ uint32_t exp4(float x0, float x1, float x2, float x3, float Ae, float Be) {
+  float t0 = Be, t1 = Be, t2 = Be, t3 = Be;
+  fma2(t0, t1, x0, x1, Ae, Ae);
+  fma2(t2, t3, x2, x3, Ae, Ae);
+  return e4m3x4(exp2f(t0), exp2f(t1), exp2f(t2), exp2f(t3));
+}
+
+// Two adjacent output values of one row, converted and written to the
+// staging tile.
 template <int ODT>
-__device__ __forceinline__ void store_row(void* out, int64_t off, const float (&o)[kD], float l) {
+__device__ __forceinline__ void stage2(uint8_t* base, float v0, float v1) {
   if constexpr (ODT == VCATTN_DTYPE_BF16) {
-    __nv_bfloat16* p = static_cast<__nv_bfloat16*>(out) + off;
-#pragma unroll
-    for (int c = 0; c < kD; c += 8) {
-      uint4 w;
-      __nv_bfloat162 t0 = __floats2bfloat162_rn(__fdiv_rn(o[c], l), __fdiv_rn(o[c + 1], l));
-      __nv_bfloat162 t1 = __floats2bfloat162_rn(__fdiv_rn(o[c + 2], l), __fdiv_rn(o[c + 3], l));
-      __nv_bfloat162 t2 = __floats2bfloat162_rn(__fdiv_rn(o[c + 4], l), __fdiv_rn(o[c + 5], l));
-      __nv_bfloat162 t3 = __floats2bfloat162_rn(__fdiv_rn(o[c + 6], l), __fdiv_rn(o[c + 7], l));
-      w.x = *reinterpret_cast<uint32_t*>(&t0); w.y = *reinterpret_cast<uint32_t*>(&t1);
-      w.z = *reinterpret_cast<uint32_t*>(&t2); w.w = *reinterpret_cast<uint32_t*>(&t3);
-      *reinterpret_cast<uint4*>(p + c) = w;
-    }
+    *reinterpret_cast<__nv_bfloat162*>(base) = __floats2bfloat162_rn(v0, v1);
   } else if constexpr (ODT == VCATTN_DTYPE_F16) {
-    __half* p = static_cast<__half*>(out) + off;
-#pragma unroll
-    for (int c = 0; c < kD; c += 8) {
-      uint4 w;
-      __half2 t0 = __floats2half2_rn(__fdiv_rn(o[c], l), __fdiv_rn(o[c + 1], l));
-      __half2 t1 = __floats2half2_rn(__fdiv_rn(o[c + 2], l), __fdiv_rn(o[c + 3], l));
-      __half2 t2 = __floats2half2_rn(__fdiv_rn(o[c + 4], l), __fdiv_rn(o[c + 5], l));
-      __half2 t3 = __floats2half2_rn(__fdiv_rn(o[c + 6], l), __fdiv_rn(o[c + 7], l));
-      w.x = *reinterpret_cast<uint32_t*>(&t0); w.y = *reinterpret_cast<uint32_t*>(&t1);
-      w.z = *reinterpret_cast<uint32_t*>(&t2); w.w = *reinterpret_cast<uint32_t*>(&t3);
-      *reinterpret_cast<uint4*>(p + c) = w;
-    }
+    *reinterpret_cast<__half2*>(base) = __floats2half2_rn(v0, v1);
   } else {
-    float* p = static_cast<float*>(out) + off;
-#pragma unroll
-    for (int c = 0; c < kD; c += 4) {
-      *reinterpret_cast<float4*>(p + c) =
-          make_float4(__fdiv_rn(o[c], l), __fdiv_rn(o[c + 1], l), __fdiv_rn(o[c + 2], l), __fdiv_rn(o[c + 3], l));
-    }
+    *reinterpret_cast<float2*>(base) = make_float2(v0, v1);
   }
 }
 
@@ -158,6 +182,7 @@ template <int BR, bool EXPCAST, int ODT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
+  constexpr int NCH = BR / 32;   // 32-key chunks per tile
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   TcSmem<BR>& sm = *reinterpret_cast<TcSmem<BR>*>(smem_raw + pad);
@@ -173,22 +198,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&sm.q_full, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1 + kBM);   // PV commit + the 128 softmax threads
+      mbar_init(&sm.kv_empty[s], 1 + 2);   // PV commit + factor warps
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.s_full[b], 1);
-      mbar_init(&sm.s_free[b], kBM);
-      mbar_init(&sm.p_full[b], kBM);
-      mbar_init(&sm.p_free[b], 1);
+      mbar_init(&sm.p_full[b], 8);
+      mbar_init(&sm.t_full[b], 1);
+      mbar_init(&sm.tr_free[b], 4);
     }
-    mbar_init(&sm.t_full, 1);
-    mbar_init(&sm.t_free, kBM);
-    for (int r = 0; r < 4; ++r) mbar_init(&sm.a_full[r], kBM);
+    mbar_init(&sm.q0_free, 4);
+    for (int r = 0; r < kRing; ++r) {
+      mbar_init(&sm.a_full[r], 8);
+      mbar_init(&sm.a_free[r], 4);
+      mbar_init(&sm.f_full[r], 2);
+      mbar_init(&sm.f_free[r], 8 + 4);
+    }
     mbar_init(&sm.drain, 1);
     fence_mbar_init();
   }
-  // Constant ones block (B operand of the row-sum MMA): row 0 = E4M3 1.0.
-  for (int i = tid; i < 16 * 128; i += kThreads) sm.ones[i] = (i < 128) ? 0x38 : 0x00;
+  // All-ones block (B operand of the row-sum MMA): every R column = rowsum(P).
+  for (int i = tid; i < 16 * 128; i += kThreads) sm.ones[i] = 0x38;
   fence_proxy_async_smem();
   if (warp == 1) {
     tmem_alloc(&sm.tmem_base, 512);
@@ -200,9 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = &sm.abort;
 
   if (warp < 4) {
-  // Register budget per warpgroup (launched at 168 x 384 = 64512):
-  // 128 x 56 (producer, MMA, 2 idle) + 128 x 200 (softmax) + 128 x 232 (correction) = 62464.
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+  // Register budget per warpgroup (launched at 128 x 512 = 65536):
+  // 128 x (40 producer/MMA/factors + 2 x 112 softmax + 248 correction) = 65536.
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 40;\n" ::: "memory");
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     int issued = 0;
@@ -247,9 +276,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(&sm.q_full, 0, abort, status, 2);
       for (int j = 0; ok && j <= nb; ++j) {
         if (j < nb) {
+          // S_b was last read as P by PV_{j-2}, issued earlier by this thread
+          // (tcgen05.mma from one thread run in order), after p_full(j-2).
           const int s = j % kStages, b = j & 1;
           ok = mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 3);
-          if (ok && j >= 2) ok = mbar_wait(&sm.s_free[b], ((j >> 1) + 1) & 1, abort, status, 4);
           if (!ok) break;
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sm.k[s]);
@@ -262,21 +292,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j >= 1) {
           const int i = j - 1, bi = i & 1, si = i % kStages;
           ok = mbar_wait(&sm.p_full[bi], (i >> 1) & 1, abort, status, 5);
-          if (ok && i >= 1) ok = mbar_wait(&sm.t_free, (i - 1) & 1, abort, status, 6);
+          // T_bi last held T_{i-2} and R_{i-1}: both read (signalled at tile i-1).
+          if (ok && i >= 1) ok = mbar_wait(&sm.tr_free[bi], ((i - 1) >> 1) & 1, abort, status, 6);
+          // R_i goes over the first quarter of T_{i-1}, already read.
+          if (ok && i >= 1) ok = mbar_wait(&sm.q0_free, (i - 1) & 1, abort, status, 9);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t p_addr = smem_u32(sm.p[bi]);
           const uint32_t v_addr = smem_u32(sm.v[si]);
+          const uint32_t p_t = tbase + kColS + bi * 128;   // A positions [32kk, 32kk+32) at columns 8kk..8kk+7
 #pragma unroll
           for (int kk = 0; kk < BR / 32; ++kk)
-            mma_f8(tbase + kColT, desc_kmajor(p_addr + kk * 32), desc_mnmajor(v_addr + kk * 32 * 128), id_pv,
-                   kk > 0);
+            mma_f8_ts(tbase + kColT + bi * 128, p_t + 8 * kk, desc_mnmajor(v_addr + kk * 32 * 128), id_pv,
+                      kk > 0);
 #pragma unroll
           for (int kk = 0; kk < BR / 32; ++kk)
-            mma_f8(tbase + kColR, desc_kmajor(p_addr + kk * 32), desc_kmajor(ones_addr + kk * 32), id_r, kk > 0);
-          tc_commit(&sm.t_full);
+            mma_f8_ts(tbase + kColT + (bi ^ 1) * 128, p_t + 8 * kk, desc_kmajor(ones_addr + kk * 32), id_r, kk > 0);
+          tc_commit(&sm.t_full[bi]);
           tc_commit(&sm.kv_empty[si]);
-          tc_commit(&sm.p_free[bi]);
         }
       }
       // Every MMA issued must finish before TMEM is released.
@@ -286,149 +318,246 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
+  } else {
+    // ------------------------------------------------------------ per-tile factors
+    const int c2 = tid - 64;   // 0..63
+    for (int j = 0; j < nb; ++j) {
+      const int s = j % kStages, ring = j % kRing;
+      if (!mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 13)) break;
+      if (j >= kRing && !mbar_wait(&sm.f_free[ring], ((j / kRing) + 1) & 1, abort, status, 14)) break;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = c2 + 64 * h;
+        const float vsc = sm.vs[s][c];
+        sm.cm[ring][0][cm_index(c)] = __fdiv_rn(vsc, 448.0f);
+        sm.cm[ring][1][cm_index(c)] = __fmul_rn(sm.mu[s][c], vsc);
+      }
+#pragma unroll
+      for (int kc = c2; kc < BR; kc += 64) sm.ksf[ring][ks_index(kc)] = sm.ks[s][kc];
+      warp_arrive(&sm.f_full[ring], lane);
+      warp_arrive(&sm.kv_empty[s], lane);
+    }
   }
-  } else if (warp < 8) {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
+  } else if (warp < 12) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 112;\n" ::: "memory");
     // ------------------------------------------------------------ softmax
-    const int t = (warp & 3) * 32 + lane;          // query row within the tile = TMEM lane
-    const uint32_t lane_base = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const int row = row0 + t;
-    const float qs = (row < a.n_pad) ? a.q_scale[static_cast<int64_t>(g) * a.n_pad + row] : 0.f;
-    const float qsm = __fmul_rn(qs, a.sm_scale);
+    // Group sg of warp w: rows ra = 32 (w%4) + 16 sg + lane/4 and rb = ra + 8;
+    // key columns 32 ch + 8 r + 2 q + e of every chunk ch (q = lane % 4).
+    const int sg = (warp >> 2) - 1;
+    const int wq = warp & 3, q = lane & 3, rl = lane >> 2;
+    const int ra = wq * 32 + 16 * sg + rl;
+    const uint32_t lane_base = tbase + (static_cast<uint32_t>(wq * 32 + 16 * sg) << 16);
+    const int64_t qrow = static_cast<int64_t>(g) * a.n_pad + row0;
+    const float qs_a = (row0 + ra < a.n_pad) ? a.q_scale[qrow + ra] : 0.f;
+    const float qs_b = (row0 + ra + 8 < a.n_pad) ? a.q_scale[qrow + ra + 8] : 0.f;
+    const float qsm_a = __fmul_rn(qs_a, a.sm_scale), qsm_b = __fmul_rn(qs_b, a.sm_scale);
     // ExpCast: c = A * (x - m) + c120 with A = 8 log2e qs sm; evaluated as
     // fma.sat(x, A/128, B/128) so the clamp at 0 is free and the /128 scale
     // makes a + 98304 round the code to an integer in the low bits.
-    const float A = __fmul_rn(8.0f * kLog2e, qsm);
-    const float As = A * (1.0f / 128.0f);
-    const float Ae = __fmul_rn(qsm, kLog2e);       // exp path: p = exp2(Ae (x - m)) * 448
-    float m = -INFINITY;
+    const float As_a = __fmul_rn(8.0f * kLog2e, qsm_a) * (1.0f / 128.0f);
+    const float As_b = __fmul_rn(8.0f * kLog2e, qsm_b) * (1.0f / 128.0f);
+    const float Ae_a = __fmul_rn(qsm_a, kLog2e), Ae_b = __fmul_rn(qsm_b, kLog2e);
+    float m_a = -INFINITY, m_b = -INFINITY;
     for (int j = 0; j < nb; ++j) {
-      const int b = j & 1, s = j % kStages;
+      const int b = j & 1, ring = j % kRing;
       if (!mbar_wait(&sm.s_full[b], (j >> 1) & 1, abort, status, 7)) break;
-      if (!mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 8)) break;
+      if (!mbar_wait(&sm.f_full[ring], (j / kRing) & 1, abort, status, 8)) break;
       tc_fence_after();
-      float x[BR];
+      const uint32_t sb = lane_base + kColS + b * 128;
+      float x[NCH][16];
 #pragma unroll
-      for (int c = 0; c < BR; c += 32) tmem_ld32(lane_base + kColS + b * 128 + c, *reinterpret_cast<float(*)[32]>(&x[c]));
+      for (int ch = 0; ch < NCH; ++ch) tmem_ld_16x256b_x4(sb + 32 * ch, x[ch]);
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&sm.s_free[b]);
-      const float* ks = sm.ks[s];
 #pragma unroll
-      for (int c = 0; c < BR; c += 4) {
-        const float4 kv = *reinterpret_cast<const float4*>(ks + c);
-        mul2(x[c], x[c + 1], kv.x, kv.y);
-        mul2(x[c + 2], x[c + 3], kv.z, kv.w);
+      for (int ch = 0; ch < NCH; ++ch) reg_fence16(x[ch]);
+      const float* kf = sm.ksf[ring] + q * kFStride;
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const float4 k0 = *reinterpret_cast<const float4*>(kf + 8 * ch);
+        const float4 k1 = *reinterpret_cast<const float4*>(kf + 8 * ch + 4);
+        const float kr[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          mul2(x[ch][4 * r], x[ch][4 * r + 1], kr[2 * r], kr[2 * r + 1]);
+          mul2(x[ch][4 * r + 2], x[ch][4 * r + 3], kr[2 * r], kr[2 * r + 1]);
+        }
       }
-      const int valid = a.N - j * BR;                 // columns >= valid are padding keys
+      warp_arrive(&sm.f_free[ring], lane);
+      const int valid = a.N - j * BR;                 // keys >= valid are padding
       if (valid < BR) {
 #pragma unroll
-        for (int c = 0; c < BR; ++c)
-          if (c >= valid) x[c] = -1.0e30f;
-      }
-      float m0 = m, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+        for (int ch = 0; ch < NCH; ++ch)
 #pragma unroll
-      for (int c = 0; c < BR; c += 8) {
-        m0 = fmax3(m0, x[c], x[c + 1]);
-        m1 = fmax3(m1, x[c + 2], x[c + 3]);
-        m2 = fmax3(m2, x[c + 4], x[c + 5]);
-        m3 = fmax3(m3, x[c + 6], x[c + 7]);
+          for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+              if (32 * ch + 8 * r + 2 * q + e >= valid) x[ch][4 * r + e] = x[ch][4 * r + 2 + e] = -1.0e30f;
       }
-      const float m_new = fmax3(m0, m1, fmaxf(m2, m3));
-      const float alpha = (m == -INFINITY) ? 0.f : exp2f(__fmul_rn(__fsub_rn(m, m_new), Ae));
-      uint32_t packed[BR / 4];
+      float ma0 = m_a, ma1 = -INFINITY, mb0 = m_b, mb1 = -INFINITY;
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        ma0 = fmax3(ma0, x[ch][0], x[ch][1]);
+        mb0 = fmax3(mb0, x[ch][2], x[ch][3]);
+        ma1 = fmax3(ma1, x[ch][4], x[ch][5]);
+        mb1 = fmax3(mb1, x[ch][6], x[ch][7]);
+        ma0 = fmax3(ma0, x[ch][8], x[ch][9]);
+        mb0 = fmax3(mb0, x[ch][10], x[ch][11]);
+        ma1 = fmax3(ma1, x[ch][12], x[ch][13]);
+        mb1 = fmax3(mb1, x[ch][14], x[ch][15]);
+      }
+      float mn_a = fmaxf(ma0, ma1), mn_b = fmaxf(mb0, mb1);
+      mn_a = fmaxf(mn_a, __shfl_xor_sync(0xffffffffu, mn_a, 1));
+      mn_b = fmaxf(mn_b, __shfl_xor_sync(0xffffffffu, mn_b, 1));
+      mn_a = fmaxf(mn_a, __shfl_xor_sync(0xffffffffu, mn_a, 2));
+      mn_b = fmaxf(mn_b, __shfl_xor_sync(0xffffffffu, mn_b, 2));
+      const float al_a = (m_a == -INFINITY) ? 0.f : exp2f(__fmul_rn(__fsub_rn(m_a, mn_a), Ae_a));
+      const float al_b = (m_b == -INFINITY) ? 0.f : exp2f(__fmul_rn(__fsub_rn(m_b, mn_b), Ae_b));
+      // P words: per chunk (row a keys r=0,1 | r=2,3, row b keys r=0,1 | r=2,3)
+      uint32_t packed[4 * NCH];
       if constexpr (EXPCAST) {
-        const float Bs = __fmaf_rn(-As, m_new, a.c120 * (1.0f / 128.0f));
+        const float Bs_a = __fmaf_rn(-As_a, mn_a, a.c120 * (1.0f / 128.0f));
+        const float Bs_b = __fmaf_rn(-As_b, mn_b, a.c120 * (1.0f / 128.0f));
 #pragma unroll
-        for (int c = 0; c < BR; c += 4) {
-          float c0 = fma_sat(x[c], As, Bs), c1 = fma_sat(x[c + 1], As, Bs);
-          float c2 = fma_sat(x[c + 2], As, Bs), c3 = fma_sat(x[c + 3], As, Bs);
-          add2(c0, c1, 98304.0f, 98304.0f);
-          add2(c2, c3, 98304.0f, 98304.0f);
-          const uint32_t lo = __byte_perm(__float_as_uint(c0), __float_as_uint(c1), 0x0040);
-          const uint32_t hi = __byte_perm(__float_as_uint(c2), __float_as_uint(c3), 0x0040);
-          packed[c / 4] = __byte_perm(lo, hi, 0x5410);
+        for (int ch = 0; ch < NCH; ++ch) {
+          packed[4 * ch + 0] = expcast4(x[ch][0], x[ch][1], x[ch][4], x[ch][5], As_a, Bs_a);
+          packed[4 * ch + 1] = expcast4(x[ch][8], x[ch][9], x[ch][12], x[ch][13], As_a, Bs_a);
+          packed[4 * ch + 2] = expcast4(x[ch][2], x[ch][3], x[ch][6], x[ch][7], As_b, Bs_b);
+          packed[4 * ch + 3] = expcast4(x[ch][10], x[ch][11], x[ch][14], x[ch][15], As_b, Bs_b);
         }
       } else {
-        const float Be = __fmaf_rn(-Ae, m_new, 8.807354922057604f);   // log2(448)
+        const float Be_a = __fmaf_rn(-Ae_a, mn_a, 8.807354922057604f);   // log2(448)
+        const float Be_b = __fmaf_rn(-Ae_b, mn_b, 8.807354922057604f);
 #pragma unroll
-        for (int c = 0; c < BR; c += 4) {
-          float e0 = x[c], e1 = x[c + 1], e2 = x[c + 2], e3 = x[c + 3];
-          float t0 = Be, t1 = Be, t2 = Be, t3 = Be;
-          fma2(t0, t1, e0, e1, Ae, Ae);
-          fma2(t2, t3, e2, e3, Ae, Ae);
-          packed[c / 4] = e4m3x4(exp2f(t0), exp2f(t1), exp2f(t2), exp2f(t3));
+        for (int ch = 0; ch < NCH; ++ch) {
+          packed[4 * ch + 0] = exp4(x[ch][0], x[ch][1], x[ch][4], x[ch][5], Ae_a, Be_a);
+          packed[4 * ch + 1] = exp4(x[ch][8], x[ch][9], x[ch][12], x[ch][13], Ae_a, Be_a);
+          packed[4 * ch + 2] = exp4(x[ch][2], x[ch][3], x[ch][6], x[ch][7], Ae_b, Be_b);
+          packed[4 * ch + 3] = exp4(x[ch][10], x[ch][11], x[ch][14], x[ch][15], Ae_b, Be_b);
         }
       }
-      if (j >= 2 && !mbar_wait(&sm.p_free[b], ((j >> 1) + 1) & 1, abort, status, 9)) break;
-      uint8_t* prow = sm.p[b] + t * 128;
-#pragma unroll
-      for (int c = 0; c < BR / 16; ++c) {
-        *reinterpret_cast<uint4*>(prow + ((c ^ (t & 7)) << 4)) =
-            make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&sm.p_full[b]);
-      // Per-tile column factors for the correction warps (thread t = channel t).
-      const float vsc = sm.vs[s][t];
-      sm.cm[j & 3][0][t] = __fdiv_rn(vsc, 448.0f);
-      sm.cm[j & 3][1][t] = __fmul_rn(sm.mu[s][t], vsc);
-      sm.alpha[j & 3][t] = alpha;
-      mbar_arrive(&sm.kv_empty[s]);
-      mbar_arrive(&sm.a_full[j & 3]);
-      m = m_new;
+      if constexpr (NCH == 4) tmem_st_16x256b_x4(sb, packed);
+      else tmem_st_16x256b_x2(sb, packed);
+      tmem_st_wait();
+      tc_fence_before();
+      warp_arrive(&sm.p_full[b], lane);
+      if (j >= kRing && !mbar_wait(&sm.a_free[ring], ((j / kRing) + 1) & 1, abort, status, 10)) break;
+      if (q < 2) sm.alpha[ring][wq * 32 + 4 * rl + 2 * sg + q] = q ? al_b : al_a;
+      warp_arrive(&sm.a_full[ring], lane);
+      m_a = mn_a;
+      m_b = mn_b;
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;\n" ::: "memory");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 248;\n" ::: "memory");
     // ------------------------------------------------------------ correction
-    const int t = (warp & 3) * 32 + lane;
-    const uint32_t lane_base = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    float o[kD];
+    // Thread (warp w, lane) owns rows 32 (w%4) + lane/4 + {0, 8, 16, 24} and
+    // channels 8 grp + 2 (lane%4) + {0, 1}, grp = 0..15.
+    const int wq = warp & 3, q = lane & 3, rl = lane >> 2;
+    const uint32_t lb0 = tbase + (static_cast<uint32_t>(wq * 32) << 16);
+    const uint32_t lb1 = tbase + (static_cast<uint32_t>(wq * 32 + 16) << 16);
+    float o[128];   // o[(grp * 4 + k) * 2 + e]: row k, channel 8 grp + 2q + e
 #pragma unroll
-    for (int c = 0; c < kD; ++c) o[c] = 0.f;
-    float l = 0.f;
+    for (int c = 0; c < 128; ++c) o[c] = 0.f;
+    float l[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
     for (int i = 0; i < nb; ++i) {
-      const int ri = i & 3;
-      ok = mbar_wait(&sm.t_full, i & 1, abort, status, 10) &&
-           mbar_wait(&sm.a_full[ri], (i >> 2) & 1, abort, status, 12);
+      const int ring = i % kRing, tb = i & 1;
+      ok = mbar_wait(&sm.t_full[tb], (i >> 1) & 1, abort, status, 11) &&
+           mbar_wait(&sm.a_full[ring], (i / kRing) & 1, abort, status, 12) &&
+           mbar_wait(&sm.f_full[ring], (i / kRing) & 1, abort, status, 15);
       if (!ok) break;
       tc_fence_after();
-      const float alpha = sm.alpha[ri][t];
-      const float* cv = sm.cm[ri][0];
-      const float* mv = sm.cm[ri][1];
-      const bool rescale = !__all_sync(0xffffffffu, alpha == 1.0f);
-      float tv[64];
-      const float rsum = tmem_ld1(lane_base + kColR);
-      tmem_ld32(lane_base + kColT, *reinterpret_cast<float(*)[32]>(&tv[0]));
-      tmem_ld32(lane_base + kColT + 32, *reinterpret_cast<float(*)[32]>(&tv[32]));
+      const uint32_t tcol = kColT + tb * 128;
+      float r0[4], r1[4], t0a[16], t0b[16], t1a[16], t1b[16];
+      tmem_ld_16x256b_x1(lb0 + kColT + (tb ^ 1) * 128, r0);   // R_i sits in T_{(i+1)&1}
+      tmem_ld_16x256b_x1(lb1 + kColT + (tb ^ 1) * 128, r1);
+      tmem_ld_16x256b_x4(lb0 + tcol, t0a);
+      tmem_ld_16x256b_x4(lb1 + tcol, t0b);
+      const float4 al4 = *reinterpret_cast<const float4*>(&sm.alpha[ring][wq * 32 + 4 * rl]);
       tmem_ld_wait();
-      const float r = __fdiv_rn(rsum, 448.0f);
+      reg_fence4(r0);
+      reg_fence4(r1);
+      reg_fence16(t0a);
+      reg_fence16(t0b);
+      tc_fence_before();
+      warp_arrive(&sm.tr_free[tb ^ 1], lane); // T_{i-1} done and R_i read: PV_{i+1} may write that buffer
+      warp_arrive(&sm.q0_free, lane);        // first quarter of T_i read: R_{i+1} may land there
+      warp_arrive(&sm.a_free[ring], lane);
+      const float al[4] = {al4.x, al4.y, al4.z, al4.w};
+      const bool rescale =
+          !__all_sync(0xffffffffu, al4.x == 1.0f && al4.y == 1.0f && al4.z == 1.0f && al4.w == 1.0f);
+      constexpr float kInv448 = 1.0f / 448.0f;
+      const float r[4] = {r0[0] * kInv448, r0[2] * kInv448, r1[0] * kInv448, r1[2] * kInv448};
+      const float* cvp = sm.cm[ring][0] + q * kFStride;
+      const float* mvp = sm.cm[ring][1] + q * kFStride;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (h == 1) {
-          tmem_ld32(lane_base + kColT + 64, *reinterpret_cast<float(*)[32]>(&tv[0]));
-          tmem_ld32(lane_base + kColT + 96, *reinterpret_cast<float(*)[32]>(&tv[32]));
-          tmem_ld_wait();
-          tc_fence_before();
-          mbar_arrive(&sm.t_free);          // T fully read: the next PV may start
+      for (int qq = 0; qq < 4; ++qq) {
+        float (&ca)[16] = (qq & 1) ? t1a : t0a;
+        float (&cb)[16] = (qq & 1) ? t1b : t0b;
+        float (&na)[16] = (qq & 1) ? t0a : t1a;
+        float (&nb16)[16] = (qq & 1) ? t0b : t1b;
+        if (qq + 1 < 4) {
+          tmem_ld_16x256b_x4(lb0 + tcol + 32 * (qq + 1), na);
+          tmem_ld_16x256b_x4(lb1 + tcol + 32 * (qq + 1), nb16);
         }
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
-          const int col = h * 64 + c;
-          if (rescale) mul2(o[col], o[col + 1], alpha, alpha);
-          const float2 cc = *reinterpret_cast<const float2*>(cv + col);
-          const float2 mm = *reinterpret_cast<const float2*>(mv + col);
-          fma2(o[col], o[col + 1], tv[c], tv[c + 1], cc.x, cc.y);
-          fma2(o[col], o[col + 1], r, r, mm.x, mm.y);
+        for (int ii = 0; ii < 4; ii += 2) {
+          const float4 cv = *reinterpret_cast<const float4*>(cvp + (4 * qq + ii) * 2);
+          const float4 mv = *reinterpret_cast<const float4*>(mvp + (4 * qq + ii) * 2);
+#pragma unroll
+          for (int sub = 0; sub < 2; ++sub) {
+            const int gl = ii + sub, grp = 4 * qq + gl;
+            const float c0 = sub ? cv.z : cv.x, c1 = sub ? cv.w : cv.y;
+            const float u0 = sub ? mv.z : mv.x, u1 = sub ? mv.w : mv.y;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float* src = (k < 2 ? ca : cb) + 4 * gl + 2 * (k & 1);
+              float& oa = o[(grp * 4 + k) * 2];
+              float& ob = o[(grp * 4 + k) * 2 + 1];
+              if (rescale) mul2(oa, ob, al[k], al[k]);
+              fma2(oa, ob, src[0], src[1], c0, c1);
+              fma2(oa, ob, r[k], r[k], u0, u1);
+            }
+          }
+        }
+        if (qq + 1 < 4) {
+          tmem_ld_wait();
+          reg_fence16(na);
+          reg_fence16(nb16);
         }
       }
-      l = __fadd_rn(__fmul_rn(l, alpha), r);
+      warp_arrive(&sm.f_free[ring], lane);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) l[k] = __fadd_rn(__fmul_rn(l[k], al[k]), r[k]);
     }
-    const int row = row0 + t;
-    if (ok && !*abort && row < a.N) {
-      const int b = g / a.H, h = g % a.H;
-      store_row<ODT>(a.out, b * a.osb + h * a.osh + static_cast<int64_t>(row) * a.osn, o, l);
+    if (ok && !*abort) {
+      // Stage this warp's 32 rows (padded stride: conflict-free 4-byte
+      // writes), then write them out as whole 16-byte row chunks.
+      constexpr int ES = (ODT == VCATTN_DTYPE_F32) ? 4 : 2;
+      constexpr int RS = kD * ES + 16;
+      static_assert(kBM * RS <= static_cast<int>(sizeof(TcSmem<BR>::q) + sizeof(TcSmem<BR>::k) +
+                                                 sizeof(TcSmem<BR>::v)),
+                    "output staging must fit in the operand buffers");
+      uint8_t* stage = sm.q + wq * 32 * RS;
+#pragma unroll
+      for (int grp = 0; grp < 16; ++grp) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float v0 = __fdiv_rn(o[(grp * 4 + k) * 2], l[k]);
+          const float v1 = __fdiv_rn(o[(grp * 4 + k) * 2 + 1], l[k]);
+          stage2<ODT>(stage + (rl + 8 * k) * RS + (8 * grp + 2 * q) * ES, v0, v1);
+        }
+      }
+      __syncwarp();
+      constexpr int CPR = kD * ES / 16;   // 16-byte chunks per row
+      const int bq = g / a.H, hq = g % a.H;
+      uint8_t* out = static_cast<uint8_t*>(a.out) + (bq * a.osb + hq * a.osh) * ES;
+      for (int idx = lane; idx < 32 * CPR; idx += 32) {
+        const int rloc = idx / CPR, ch = idx % CPR;
+        const int orow = row0 + wq * 32 + rloc;
+        if (orow < a.N)
+          *reinterpret_cast<uint4*>(out + static_cast<int64_t>(orow) * a.osn * ES + ch * 16) =
+              *reinterpret_cast<const uint4*>(stage + rloc * RS + ch * 16);
+      }
     }
   }
   __syncthreads();

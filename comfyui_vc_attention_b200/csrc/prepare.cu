@@ -219,7 +219,14 @@ struct VArgs {
   float* scale;      // (G, NB, D)
   float* mu;         // (G, NB, D) block mean / scale
   float* mean;       // (G, NB, D) block mean, or nullptr
+  bool mma_order;    // codes rows in the tcgen05 kernel's key order
 };
+
+// Slot of value-block row r when VCATTN_V_MMA_ORDER is set: a 4 x 4
+// transpose of (row / 8 % 4, row / 2 % 4) inside each 32-row chunk.
+__host__ __device__ __forceinline__ int mma_key_slot(int r) {
+  return (r & ~31) | (((r >> 1) & 3) << 3) | (((r >> 3) & 3) << 1) | (r & 1);
+}
 
 template <int DT, int D>
 __global__ void __launch_bounds__(D) quant_v_kernel(VArgs a) {
@@ -275,7 +282,8 @@ __global__ void __launch_bounds__(D) quant_v_kernel(VArgs a) {
         const float* row = vs_smem + r * D + c;
         const uint32_t w = e4m3x4(__fdiv_rn(row[0], scs[c]), __fdiv_rn(row[1], scs[c + 1]),
                                   __fdiv_rn(row[2], scs[c + 2]), __fdiv_rn(row[3], scs[c + 3]));
-        *reinterpret_cast<uint32_t*>(a.codes + (static_cast<int64_t>(g) * a.n_pad + j * a.br + r) * D + c) = w;
+        const int slot = a.mma_order ? mma_key_slot(r) : r;
+        *reinterpret_cast<uint32_t*>(a.codes + (static_cast<int64_t>(g) * a.n_pad + j * a.br + slot) * D + c) = w;
       }
     }
   }
@@ -400,6 +408,7 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
     a.x = *p.v; a.H = p.H; a.N = p.N; a.n_pad = p.n_pad; a.br = p.block_rows;
     a.perm = p.perm; a.perm_rows = p.perm_rows;
     a.codes = p.v8; a.codes_t = p.v8t; a.scale = p.v_scale; a.mu = p.mu; a.mean = p.v_mean;
+    a.mma_order = (p.flags & VCATTN_V_MMA_ORDER) != 0;
     const size_t smem = static_cast<size_t>(p.block_rows) * D * sizeof(float);
     cudaFuncSetAttribute(quant_v_kernel<DT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     quant_v_kernel<DT, D><<<dim3(nb, G), D, smem, st>>>(a);

@@ -32,6 +32,7 @@ DTYPE_F32 = 2
 
 HADAMARD = 1
 SMOOTH_K = 2
+V_MMA_ORDER = 4
 EXPCAST = 1
 
 

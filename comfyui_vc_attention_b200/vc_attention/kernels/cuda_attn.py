@@ -83,6 +83,7 @@ class Prepared(NamedTuple):
     q_bar: Optional[torch.Tensor] = None    # (G, NQB, D) fp32
     keep: Optional[torch.Tensor] = None     # (G, NQB, NB) uint8 routing mask
     block_rows: int = 128
+    v_mma_order: bool = False               # v rows in the tcgen05 kernel's key order
 
 
 def has_kernel() -> bool:
@@ -118,7 +119,7 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
             block_rows: int = 128, hadamard: bool = True, smooth_k: bool = True, *,
             sparse: bool = False, tau: float = 1.3, q_block: int = 64,
             scale: Optional[float] = None, want_v: bool = True, want_v_t: bool = False,
-            local_blocks: int = 1, sink_blocks: int = 0) -> Prepared:
+            local_blocks: int = 1, sink_blocks: int = 0, v_mma_order: bool = True) -> Prepared:
     """Quantise and permute Q/K/V into the kernel layout (triton_attn.py:504-579).
 
     Byte-identical to the reference's portable ``prepare`` on the codes; the
@@ -156,6 +157,9 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
     vs = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
     mu = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
     flags = (N.HADAMARD if hadamard else 0) | (N.SMOOTH_K if smooth_k else 0)
+    v_mma_order = bool(v_mma_order and want_v)
+    if v_mma_order:
+        flags |= N.V_MMA_ORDER
     sc = scale if scale is not None else d ** -0.5
     route = None
     k_mean = v_mean = q_cent = q_bar = None
@@ -190,7 +194,7 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
         k_mean=None if k_mean is None else k_mean.view(b, h, nb, d),
         v_mean=None if v_mean is None else v_mean.view(b, h, nb, d),
         thresh=None if thresh is None else thresh.view(b, h, nqb), n_qblk=nqb,
-        v_t=v8t, q_cent=q_cent, q_bar=q_bar, keep=keep, block_rows=block_rows)
+        v_t=v8t, q_cent=q_cent, q_bar=q_bar, keep=keep, block_rows=block_rows, v_mma_order=v_mma_order)
 
 
 def route_mask(route: "N.RouteStats", g: int, n: int, n_pad: int, d: int, block_rows: int, tau: float,
@@ -206,6 +210,20 @@ def route_mask(route: "N.RouteStats", g: int, n: int, n_pad: int, d: int, block_
     return keep, thresh
 
 
+def mma_key_slot(r: torch.Tensor) -> torch.Tensor:
+    """Slot of value-block row r under VCATTN_V_MMA_ORDER (its own inverse)."""
+    return (r & ~31) | (((r >> 1) & 3) << 3) | (((r >> 3) & 3) << 1) | (r & 1)
+
+
+def v_natural(p: Prepared) -> torch.Tensor:
+    """V codes (uint8) in token order, whichever order ``p.v`` is stored in."""
+    v = p.v.view(torch.uint8)
+    if not p.v_mma_order:
+        return v
+    idx = mma_key_slot(torch.arange(v.shape[-2], device=v.device))
+    return v.index_select(-2, idx)
+
+
 def restore(p: Prepared, block_rows: int = 128):
     """Dequantise a Prepared back to value/score units (tests; triton_attn.py:582-598)."""
     from ..quant import e4m3_decode
@@ -214,7 +232,7 @@ def restore(p: Prepared, block_rows: int = 128):
     qd = e4m3_decode(p.q.view(torch.uint8).reshape(g, np_, d)) * p.q_scale.reshape(g, np_, 1)
     kd = e4m3_decode(p.k.view(torch.uint8).reshape(g, np_, d)) * p.k_scale.reshape(g, np_, 1)
     vs = p.v_scale.reshape(g, -1, d).repeat_interleave(block_rows, dim=1)
-    vd = e4m3_decode(p.v.view(torch.uint8).reshape(g, np_, d)) * vs
+    vd = e4m3_decode(v_natural(p).reshape(g, np_, d)) * vs
     vd = vd + p.mu.reshape(g, -1, d).repeat_interleave(block_rows, dim=1) * vs
     return qd, kd, vd
 
@@ -286,8 +304,8 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
     if kernel == "auto":
         kernel = "tc" if (d == 128 and p.v is not None) else "mma"
     if kernel == "tc":
-        if p.v is None:
-            raise ValueError("the tcgen05 kernel reads V in the Prepared layout (want_v=True)")
+        if p.v is None or not p.v_mma_order:
+            raise ValueError("the tcgen05 kernel reads V codes in its key order (want_v=True, v_mma_order=True)")
         N.check("vcattn_attn_fp8", lib.vcattn_attn_fp8(
             q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
             p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), b, h, n, n_pad, d,

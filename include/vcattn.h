@@ -53,6 +53,11 @@ extern "C" {
 /* ---- prepare flags (triton_attn.py:504-512 hadamard / smooth_k) --------- */
 #define VCATTN_HADAMARD 1
 #define VCATTN_SMOOTH_K 2
+/* V codes (v8) in the tcgen05 kernel's key order: inside every 32-row chunk
+ * of a value block, row 8a + 2b + e is stored at slot 8b + 2a + e (a, b in
+ * 0..3, e in 0..1).  The order is its own inverse.  vcattn_attn_fp8 requires
+ * it; the other outputs are unaffected.  No counterpart in the reference. */
+#define VCATTN_V_MMA_ORDER 4
 
 /* ---- attention flags (TritonConfig, triton_attn.py:93-129) ------------- */
 #define VCATTN_EXPCAST 1        /* write P bytes with ExpCast (expcast.py:52-70) */

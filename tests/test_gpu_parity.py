@@ -168,7 +168,8 @@ def _assert_prepare_equal(p, ref, g_shape):
     G = g_shape
     np.testing.assert_array_equal(p.q.view(torch.uint8).reshape(G, -1, p.q.shape[-1]).cpu().numpy(), ref["q"])
     np.testing.assert_array_equal(p.k.view(torch.uint8).reshape(G, -1, p.k.shape[-1]).cpu().numpy(), ref["k"])
-    np.testing.assert_array_equal(p.v.view(torch.uint8).reshape(G, -1, p.v.shape[-1]).cpu().numpy(), ref["v"])
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import v_natural
+    np.testing.assert_array_equal(v_natural(p).reshape(G, -1, p.v.shape[-1]).cpu().numpy(), ref["v"])
     for f in ("q_scale", "k_scale", "v_scale", "mu"):
         got = getattr(p, f).reshape(ref[f].shape).cpu().numpy()
         np.testing.assert_array_equal(got, ref[f], err_msg=f)
@@ -185,7 +186,9 @@ def test_prepare_config0_bit_exact(dev):
     # codes equal the reference's own prepare() bytes
     assert np.array_equal(p.q.view(torch.uint8).cpu().numpy().reshape(g["q8"].shape), g["q8"])
     assert np.array_equal(p.k.view(torch.uint8).cpu().numpy().reshape(g["k8"].shape), g["k8"])
-    assert np.array_equal(p.v.view(torch.uint8).cpu().numpy().reshape(g["v8"].shape), g["v8"])
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import v_natural
+    assert p.v_mma_order
+    assert np.array_equal(v_natural(p).cpu().numpy().reshape(g["v8"].shape), g["v8"])
     # block-transposed V holds the same codes
     vt = p.v_t.cpu().numpy()                                   # (G, NB, D, BR)
     v8 = ref["v"].reshape(2, 16, 64, 128).transpose(0, 1, 3, 2)

@@ -168,3 +168,21 @@ def test_nodes_execute():
     finally:
         uninstall()
     assert "inactive" in kernel_status()
+
+
+def test_mma_key_slot_is_an_involution_within_32_row_chunks():
+    """VCATTN_V_MMA_ORDER: the V-row order of the tcgen05 kernel transposes
+    (row/8 % 4, row/2 % 4) inside each 32-row chunk and is its own inverse."""
+    import torch
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import mma_key_slot
+    r = torch.arange(256)
+    s = mma_key_slot(r)
+    assert torch.equal(mma_key_slot(s), r)
+    assert torch.equal(torch.sort(s).values, r)
+    assert torch.equal(s // 32, r // 32)
+    # thread q of the 16x256b fragment holds keys 8r + 2q + e; their P bytes
+    # sit at A-operand positions 8q + 2r + e, where V row 8r + 2q + e must be
+    for q in range(4):
+        for rr in range(4):
+            for e in range(2):
+                assert int(mma_key_slot(torch.tensor(8 * rr + 2 * q + e))) == 8 * q + 2 * rr + e
