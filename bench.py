@@ -361,16 +361,13 @@ def main() -> int:
     peaks, peak_kind = measured_peaks()
     fp8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
     attn_tflops = fl / (attn_ms / 1e3) / 1e12
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "attn_traffic.json")
+    traffic = None   # DRAM bytes per attention launch from the committed ncu summary
+    tpath = os.path.join(ROOT, "profiles", "attn_tc_c1.md")
     if os.path.exists(tpath):
-        try:
-            with open(tpath) as f:
-                tinfo = json.load(f)
-            if tinfo.get("workload") == args.workload:
-                traffic = tinfo.get("bytes_per_launch")
-        except Exception:
-            traffic = None
+        with open(tpath) as f:
+            for ln in f:
+                if ln.startswith(f"traffic_bytes_per_launch {args.workload}:"):
+                    traffic = int(ln.split(":")[1])
     prep_bytes = (6 * G * NT * D + 3 * G * NT * D + 8 * G * NT + 8 * G * (NT // w["block_rows"]) * D
                   + 4 * G * NT)
     launches_per_step = 5 + 1

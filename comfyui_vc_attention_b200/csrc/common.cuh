@@ -111,6 +111,26 @@ __device__ __forceinline__ float e4m3_row_scale(float amax) {
   return __fdiv_rn(fmaxf(amax, kTiny), kE4M3Max);
 }
 
+// x / s for many x and one s, from y = RN(1 / s) (an IEEE division): Markstein's correction
+// (P. Markstein, IBM J. Res. Dev. 34(1), 1990): q0 = RN(x y), r = x - q0 s
+// exactly (fma), q = RN(q0 + r y).  It is the correctly rounded quotient
+// whenever x / s and the residual stay in the normal range.  The E4M3 codes
+// only use quotients up to 448, and any quotient below 2^-10 becomes code 0
+// whatever its last bit, so the codes equal those of an IEEE division.
+struct DivBy {
+  float s, y;
+  __device__ __forceinline__ explicit DivBy(float s_) : s(s_), y(0.f) {
+#ifdef __CUDA_ARCH__
+    y = __fdiv_rn(1.0f, s_);
+#endif
+  }
+  __device__ __forceinline__ float operator()(float x) const {
+    const float q0 = __fmul_rn(x, y);
+    const float r = __fmaf_rn(-q0, s, x);
+    return __fmaf_rn(r, y, q0);
+  }
+};
+
 // In-register Walsh-Hadamard transform of a 128-wide row spread over a warp
 // (lane l holds elements 4l..4l+3), followed by the IEEE division by
 // fp32(sqrt(128)).  Same butterfly pairing and the same a+b / a-b as the fp32
@@ -124,11 +144,13 @@ __device__ __forceinline__ void fwht128_warp(float v[4], int lane) {
   // h = 4 .. 64: partner lane = lane ^ (h / 4).
 #pragma unroll
   for (int m = 1; m < 32; m <<= 1) {
-    const bool upper = (lane & m) != 0;
+    // lower lane: v + p, upper lane: p - v, both as one fma with a +-1
+    // multiplier (rounded once, identical to the add / subtract)
+    const float sg = (lane & m) ? -1.0f : 1.0f;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       const float p = __shfl_xor_sync(0xffffffffu, v[t], m);
-      v[t] = upper ? __fsub_rn(p, v[t]) : __fadd_rn(v[t], p);
+      v[t] = __fmaf_rn(sg, v[t], p);
     }
   }
   const float r = 11.313708498984761f;   // fp32(sqrt(128))
@@ -145,11 +167,11 @@ __device__ __forceinline__ void fwht64_halfwarp(float v[4], int lane) {
   v[1] = __fadd_rn(a1, a3); v[3] = __fsub_rn(a1, a3);
 #pragma unroll
   for (int m = 1; m < 16; m <<= 1) {
-    const bool upper = (lane & m) != 0;
+    const float sg = (lane & m) ? -1.0f : 1.0f;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       const float p = __shfl_xor_sync(0xffffffffu, v[t], m);
-      v[t] = upper ? __fsub_rn(p, v[t]) : __fadd_rn(v[t], p);
+      v[t] = __fmaf_rn(sg, v[t], p);
     }
   }
   const float r = 8.0f;   // fp32(sqrt(64))

@@ -74,20 +74,29 @@ __global__ void __launch_bounds__(256) kmean_partial_kernel(
   double acc[4] = {0.0, 0.0, 0.0, 0.0};
   const int t0 = chunk * kChunkRows;
   const int t1 = min(N, t0 + kChunkRows);
-  // Rows advance in warp-uniform steps so every lane reaches the shuffles.
-  for (int base = t0 + warp * RM::kRowsPerWarp; base < t1; base += 8 * RM::kRowsPerWarp) {
-    const int t = base + RM::sub(lane);
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    const bool live = t < t1;
-    if (live) {
-      const int64_t off = b * k.sb + h * k.sh + static_cast<int64_t>(t) * k.sn + RM::col(lane);
-      const float4 x = load4<DT>(k.data, off);
-      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-    }
-    if (flags & VCATTN_HADAMARD) RM::fwht(v, lane);
-    if (live) {
+  // Rows advance in warp-uniform steps so every lane reaches the shuffles;
+  // kBatch rows are loaded before any is used (memory-level parallelism).
+  constexpr int kBatch = 8;
+  constexpr int kStep = 8 * RM::kRowsPerWarp;
+  for (int base = t0 + warp * RM::kRowsPerWarp; base < t1; base += kBatch * kStep) {
+    float v[kBatch][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[i] += static_cast<double>(v[i]);
+    for (int u = 0; u < kBatch; ++u) {
+      const int t = base + u * kStep + RM::sub(lane);
+      v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.f;
+      if (t < t1) {
+        const int64_t off = b * k.sb + h * k.sh + static_cast<int64_t>(t) * k.sn + RM::col(lane);
+        const float4 x = load4<DT>(k.data, off);
+        v[u][0] = x.x; v[u][1] = x.y; v[u][2] = x.z; v[u][3] = x.w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      if (flags & VCATTN_HADAMARD) RM::fwht(v[u], lane);
+      if (base + u * kStep + RM::sub(lane) < t1) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] += static_cast<double>(v[u][i]);
+      }
     }
   }
 #pragma unroll
@@ -144,16 +153,29 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(QKArgs a) {
     km[0] = t.x; km[1] = t.y; km[2] = t.z; km[3] = t.w;
   }
   const int nwarps = blockDim.x >> 5;
-  for (int base = warp * RM::kRowsPerWarp; base < a.rows; base += nwarps * RM::kRowsPerWarp) {
-    const int t = r0 + base + RM::sub(lane);
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    const bool real = t < a.N;
-    if (real) {
+  // kBatch rows per warp are loaded before any is used (memory-level
+  // parallelism); rows = 64 or 128 gives 8 or 16 rows per warp.
+  constexpr int kBatch = 8;
+  const int step = nwarps * RM::kRowsPerWarp;
+  for (int base0 = warp * RM::kRowsPerWarp; base0 < a.rows; base0 += kBatch * step) {
+  float vb[kBatch][4];
+#pragma unroll
+  for (int u = 0; u < kBatch; ++u) {
+    const int t = r0 + base0 + u * step + RM::sub(lane);
+    vb[u][0] = vb[u][1] = vb[u][2] = vb[u][3] = 0.f;
+    if (base0 + u * step < a.rows && t < a.N) {
       const int src = source_row(a.perm, a.perm_rows, g, a.N, t);
       const int64_t off = b * a.x.sb + h * a.x.sh + static_cast<int64_t>(src) * a.x.sn + RM::col(lane);
       const float4 x = load4<DT>(a.x.data, off);
-      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+      vb[u][0] = x.x; vb[u][1] = x.y; vb[u][2] = x.z; vb[u][3] = x.w;
     }
+  }
+#pragma unroll
+  for (int u = 0; u < kBatch; ++u) {
+    if (base0 + u * step >= a.rows) break;
+    const int t = r0 + base0 + u * step + RM::sub(lane);
+    float* v = vb[u];
+    const bool real = t < a.N;
     if (a.flags & VCATTN_HADAMARD) RM::fwht(v, lane);
     if (real && a.kmean != nullptr) {
 #pragma unroll
@@ -166,7 +188,8 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(QKArgs a) {
     float sc = 0.f;
     if (real) {
       sc = e4m3_row_scale(am);
-      packed = e4m3x4(__fdiv_rn(v[0], sc), __fdiv_rn(v[1], sc), __fdiv_rn(v[2], sc), __fdiv_rn(v[3], sc));
+      const DivBy div(sc);
+      packed = e4m3x4(div(v[0]), div(v[1]), div(v[2]), div(v[3]));
     }
     if (t < a.n_pad) {
       *reinterpret_cast<uint32_t*>(a.codes + (static_cast<int64_t>(g) * a.n_pad + t) * D + RM::col(lane)) = packed;
@@ -184,6 +207,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(QKArgs a) {
         }
       }
     }
+  }
   }
   if (!want_mean && !want_qbar) return;
   __shared__ double red_m[8][32][4];
@@ -228,63 +252,105 @@ __host__ __device__ __forceinline__ int mma_key_slot(int r) {
   return (r & ~31) | (((r >> 1) & 3) << 3) | (((r >> 3) & 3) << 1) | (r & 1);
 }
 
-template <int DT, int D>
-__global__ void __launch_bounds__(D) quant_v_kernel(VArgs a) {
-  extern __shared__ float vs_smem[];   // [br][D]
+// Each warp keeps the rows it owns in registers through the three passes
+// (block mean, residual max, codes); lanes own four channels as in the row
+// kernels, so every load and row-major store is a whole coalesced row.  The
+// transposed codes go through a shared byte tile whose 4-byte words are
+// XOR-swizzled by row / 4, which keeps both its row-major writes and its
+// column reads free of bank conflicts.
+template <int DT, int D, int BR>
+__global__ void __launch_bounds__(256) quant_v_kernel(VArgs a) {
+  using RM = RowMap<D>;
+  constexpr int kWarps = 8;
+  constexpr int kSteps = BR / (kWarps * RM::kRowsPerWarp);   // rows per lane
+  constexpr int kWords = D / 4;                              // 4-byte code words per row
+  __shared__ double red[kWarps][32][4];
+  __shared__ float mu_s[D], sc_s[D];
+  __shared__ uint32_t ct[BR * kWords];
   const int g = blockIdx.y, j = blockIdx.x;
   const int b = g / a.H, h = g % a.H;
-  const int tid = threadIdx.x;
-  const int nb = a.n_pad / a.br;
-  // Stage rows: thread tid loads channel tid of each row (coalesced per row).
-  for (int r = 0; r < a.br; ++r) {
-    const int t = j * a.br + r;
-    float x = 0.f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = a.n_pad / BR;
+  const int col = RM::col(lane);
+  // pass 1: load (zero past N), float64 channel sums
+  float x[kSteps][4];
+#pragma unroll
+  for (int k = 0; k < kSteps; ++k) {
+    const int r = (k * kWarps + warp) * RM::kRowsPerWarp + RM::sub(lane);
+    const int t = j * BR + r;
+    x[k][0] = x[k][1] = x[k][2] = x[k][3] = 0.f;
     if (t < a.N) {
       const int src = source_row(a.perm, a.perm_rows, g, a.N, t);
-      const int64_t off = b * a.x.sb + h * a.x.sh + static_cast<int64_t>(src) * a.x.sn + tid;
-      if constexpr (DT == VCATTN_DTYPE_BF16) x = __bfloat162float(static_cast<const __nv_bfloat16*>(a.x.data)[off]);
-      else if constexpr (DT == VCATTN_DTYPE_F16) x = __half2float(static_cast<const __half*>(a.x.data)[off]);
-      else x = static_cast<const float*>(a.x.data)[off];
+      const float4 v = load4<DT>(a.x.data, b * a.x.sb + h * a.x.sh + static_cast<int64_t>(src) * a.x.sn + col);
+      x[k][0] = v.x; x[k][1] = v.y; x[k][2] = v.z; x[k][3] = v.w;
     }
-    vs_smem[r * D + tid] = x;
   }
-  double s = 0.0;
-  for (int r = 0; r < a.br; ++r) s += static_cast<double>(vs_smem[r * D + tid]);
-  const float mu = __fdiv_rn(__double2float_rn(s), static_cast<float>(a.br));
-  float am = 0.f;
-  for (int r = 0; r < a.br; ++r) {
-    const float rr = __fsub_rn(vs_smem[r * D + tid], mu);
-    vs_smem[r * D + tid] = rr;
-    am = fmaxf(am, fabsf(rr));
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+  for (int k = 0; k < kSteps; ++k)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] += static_cast<double>(x[k][i]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) red[warp][lane][i] = acc[i];
+  __syncthreads();
+  if (threadIdx.x < D)
+    mu_s[threadIdx.x] = __fdiv_rn(__double2float_rn(reduce_lanes<D>(red, kWarps, threadIdx.x)), static_cast<float>(BR));
+  __syncthreads();
+  // pass 2: residual max per channel
+  float mu[4], am[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mu[i] = mu_s[col + i];
+#pragma unroll
+  for (int k = 0; k < kSteps; ++k)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) am[i] = fmaxf(am[i], fabsf(__fsub_rn(x[k][i], mu[i])));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) red[warp][lane][i] = am[i];
+  __syncthreads();
+  if (threadIdx.x < D) {
+    const int d = threadIdx.x, l = d / 4, i = d % 4;
+    float m = 0.f;
+    for (int w = 0; w < kWarps; ++w) {
+      m = fmaxf(m, static_cast<float>(red[w][l][i]));
+      if (D == 64) m = fmaxf(m, static_cast<float>(red[w][l + 16][i]));
+    }
+    const float sc = e4m3_row_scale(m);
+    sc_s[d] = sc;
+    const int64_t so = (static_cast<int64_t>(g) * nb + j) * D + d;
+    a.scale[so] = sc;
+    a.mu[so] = __fdiv_rn(mu_s[d], sc);
+    if (a.mean) a.mean[so] = mu_s[d];
   }
-  const float sc = e4m3_row_scale(am);
-  const int64_t so = (static_cast<int64_t>(g) * nb + j) * D + tid;
-  a.scale[so] = sc;
-  a.mu[so] = __fdiv_rn(mu, sc);
-  if (a.mean) a.mean[so] = mu;
+  __syncthreads();
+  // pass 3: codes
+  const DivBy dv[4] = {DivBy(sc_s[col]), DivBy(sc_s[col + 1]), DivBy(sc_s[col + 2]), DivBy(sc_s[col + 3])};
+#pragma unroll
+  for (int k = 0; k < kSteps; ++k) {
+    const int r = (k * kWarps + warp) * RM::kRowsPerWarp + RM::sub(lane);
+    const uint32_t w = e4m3x4(dv[0](__fsub_rn(x[k][0], mu[0])), dv[1](__fsub_rn(x[k][1], mu[1])),
+                              dv[2](__fsub_rn(x[k][2], mu[2])), dv[3](__fsub_rn(x[k][3], mu[3])));
+    if (a.codes) {
+      const int slot = a.mma_order ? mma_key_slot(r) : r;
+      *reinterpret_cast<uint32_t*>(a.codes + (static_cast<int64_t>(g) * a.n_pad + j * BR + slot) * D + col) = w;
+    }
+    if (a.codes_t) ct[r * kWords + ((col >> 2) ^ ((r >> 2) & (kWords - 1)))] = w;
+  }
   if (a.codes_t) {
-    uint8_t* dst = a.codes_t + ((static_cast<int64_t>(g) * nb + j) * D + tid) * a.br;
-    for (int r = 0; r < a.br; r += 4) {
-      const uint32_t w = e4m3x4(__fdiv_rn(vs_smem[(r + 0) * D + tid], sc), __fdiv_rn(vs_smem[(r + 1) * D + tid], sc),
-                                __fdiv_rn(vs_smem[(r + 2) * D + tid], sc), __fdiv_rn(vs_smem[(r + 3) * D + tid], sc));
-      *reinterpret_cast<uint32_t*>(dst + r) = w;
-    }
-  }
-  if (a.codes) {
-    __shared__ float scs[D];
-    scs[tid] = sc;
     __syncthreads();
-    // Row-major codes: warp w writes rows, lane owns 4 channels.
-    const int warp = tid >> 5, lane = tid & 31;
-    const int nw = D / 32;
-    for (int r = warp; r < a.br; r += nw) {
-      for (int c = lane * 4; c < D; c += 128) {
-        const float* row = vs_smem + r * D + c;
-        const uint32_t w = e4m3x4(__fdiv_rn(row[0], scs[c]), __fdiv_rn(row[1], scs[c + 1]),
-                                  __fdiv_rn(row[2], scs[c + 2]), __fdiv_rn(row[3], scs[c + 3]));
-        const int slot = a.mma_order ? mma_key_slot(r) : r;
-        *reinterpret_cast<uint32_t*>(a.codes + (static_cast<int64_t>(g) * a.n_pad + j * a.br + slot) * D + c) = w;
+    // thread -> (channel d, rows 4rq..4rq+3): one packed word of the
+    // transposed block; a warp writes 128 consecutive bytes of one channel
+    uint8_t* dst = a.codes_t + (static_cast<int64_t>(g) * nb + j) * D * BR;
+    for (int item = threadIdx.x; item < D * (BR / 4); item += blockDim.x) {
+      const int d = item / (BR / 4), rq = item % (BR / 4);
+      const int wd = d >> 2, bs = 8 * (d & 3);
+      uint32_t packed = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 4 * rq + i;
+        const uint32_t word = ct[r * kWords + (wd ^ ((r >> 2) & (kWords - 1)))];
+        packed |= ((word >> bs) & 0xffu) << (8 * i);
       }
+      *reinterpret_cast<uint32_t*>(dst + static_cast<int64_t>(d) * BR + 4 * rq) = packed;
     }
   }
 }
@@ -409,9 +475,8 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
     a.perm = p.perm; a.perm_rows = p.perm_rows;
     a.codes = p.v8; a.codes_t = p.v8t; a.scale = p.v_scale; a.mu = p.mu; a.mean = p.v_mean;
     a.mma_order = (p.flags & VCATTN_V_MMA_ORDER) != 0;
-    const size_t smem = static_cast<size_t>(p.block_rows) * D * sizeof(float);
-    cudaFuncSetAttribute(quant_v_kernel<DT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    quant_v_kernel<DT, D><<<dim3(nb, G), D, smem, st>>>(a);
+    if (p.block_rows == 128) quant_v_kernel<DT, D, 128><<<dim3(nb, G), 256, 0, st>>>(a);
+    else quant_v_kernel<DT, D, 64><<<dim3(nb, G), 256, 0, st>>>(a);
   }
   return cudaGetLastError();
 }
