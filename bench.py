@@ -26,6 +26,7 @@ bounded sample of the same workload, extrapolated by rows and heads.
 from __future__ import annotations
 
 import argparse
+import math
 import json
 import os
 import statistics
@@ -49,6 +50,13 @@ WORKLOADS = {
                   spatial=None),
     "c3": dict(desc="dense FP8 VC-Attention, B1 H56 N65536 D128, ExpCast on, V-Smooth k=512",
                B=1, H=56, N=65536, D=128, expcast=True, sparse=False, k=512, block_rows=128, spatial=None),
+    "c4": dict(desc="configs[4]: dense FP8 VC-Attention, B2 (CFG pair) H56 N65536 D128, (batch, head) units "
+                    "sharded over the ranks, NCCL all-gather of the bf16 output, ExpCast on, V-Smooth k=512",
+               B=2, H=56, N=65536, D=128, expcast=True, sparse=False, k=512, block_rows=128, spatial=None,
+               sharded=True, cfg_pair=True),
+    "c2": dict(desc="configs[2]: block-sparse FP8 VC-Attention, tau=1.3, B1 H56 N16384 D128 on a 16x32x32 "
+                    "grid, ExpCast on, V-Smooth k=64", B=1, H=56, N=16384, D=128, expcast=True, sparse=True,
+               k=64, block_rows=128, spatial=(16, 32, 32), tau=1.3),
 }
 
 
@@ -134,9 +142,34 @@ def make_inputs_gpu(w, seed, dev):
     q = torch.randn((G, N, D), generator=g, device=dev)
     k = torch.randn((G, N, D), generator=g, device=dev) + 2.0 * torch.randn((G, 1, D), generator=g, device=dev)
     cent = torch.randn((G, 64, D), generator=g, device=dev)
-    lab = torch.randint(0, 64, (G, N), generator=g, device=dev)
+    if w.get("spatial"):
+        # tokens on a T x Hg x W grid; a smooth positional field
+        # (8 separable low-frequency cosines projected to D, RMS 0.5) is shared
+        # by Q and K; V's centre is the token's region (4 x 4 x 4 regions)
+        t, hg, wd = w["spatial"]
+        tt, hh, ww = torch.meshgrid(torch.arange(t, device=dev), torch.arange(hg, device=dev),
+                                    torch.arange(wd, device=dev), indexing="ij")
+        fr = torch.rand((8, 3), generator=g, device=dev) * 2.0
+        ph = torch.rand((8, 3), generator=g, device=dev) * (2 * math.pi)
+        feats = torch.stack([torch.cos(math.pi * fr[i, 0] * tt / t + ph[i, 0])
+                             * torch.cos(math.pi * fr[i, 1] * hh / hg + ph[i, 1])
+                             * torch.cos(math.pi * fr[i, 2] * ww / wd + ph[i, 2]) for i in range(8)], -1)
+        pos = feats.reshape(N, 8) @ torch.randn((8, D), generator=g, device=dev)
+        pos = pos * (0.5 / pos.pow(2).mean().sqrt().clamp_min(1e-12))
+        q = q + pos
+        k = k + pos
+        reg = ((tt * 4) // t) * 16 + ((hh * 4) // hg) * 4 + (ww * 4) // wd
+        lab = (reg.reshape(1, N) % 64).expand(G, N)
+    else:
+        lab = torch.randint(0, 64, (G, N), generator=g, device=dev)
     v = torch.gather(cent, 1, lab.unsqueeze(-1).expand(G, N, D))
     v = v + 0.3 * torch.randn((G, N, D), generator=g, device=dev)
+    if w.get("cfg_pair"):
+        # batch 1 = batch 0 + 0.05 N(0, 1)
+        half = G // 2
+        q[half:] = q[:half] + 0.05 * torch.randn((half, N, D), generator=g, device=dev)
+        k[half:] = k[:half] + 0.05 * torch.randn((half, N, D), generator=g, device=dev)
+        v[half:] = v[:half] + 0.05 * torch.randn((half, N, D), generator=g, device=dev)
     shape = (w["B"], w["H"], N, D)
     out = [t.to(torch.bfloat16).reshape(shape).contiguous() for t in (q, k, v)]
     del q, k, v, cent, lab
@@ -216,6 +249,115 @@ def run_reference_arm(args, w, rank):
 
 # ----------------------------------------------------------------- main ----
 
+def run_sharded(args, w, rank, world, local) -> int:
+    """the job's (batch, head) units split over the ranks (strong
+    scaling), each rank running prepare + attention on its units and one NCCL
+    all-gather assembling the full bf16 output on every rank."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    from comfyui_vc_attention_b200.vc_attention import _native as N
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import TritonConfig
+    from comfyui_vc_attention_b200.vc_attention.sharded import shard_units, vc_attention_sharded
+    N.lib()
+    q, k, v = make_inputs_gpu(w, 1234, dev)          # the same inputs on every rank
+    B, H, NT, D = q.shape
+    G = B * H
+    lo, hi = shard_units(G, world, rank)
+    perm = torch.zeros((G, NT), dtype=torch.int32, device=dev)
+    gcfg = GroupingConfig(block_rows=w["block_rows"], iters=3, max_clusters=w["k"])
+    if hi > lo:
+        perm[lo:hi] = build_permutation(v.view(G, NT, D)[lo:hi], gcfg).perm
+    cfg = TritonConfig(block_n=w["block_rows"], enable_expcast=w["expcast"])
+    scale = D ** -0.5
+
+    def step():
+        return vc_attention_sharded(q, k, v, perm, cfg, scale, gather=True)
+
+    for _ in range(max(3, args.warmup)):
+        out = step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(args.steps):
+        out = step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    fl = flops_per_call(w)
+    value = fl / (ms / 1e3) / 1e12
+    # e2e: this rank's unit slabs from pinned host memory, the gathered
+    # output back to the host
+    g_h = [t.reshape(G, NT, D)[lo:hi].cpu().pin_memory() for t in (q, k, v)]
+    o_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def e2e_step():
+        for src, dst in zip(g_h, (q, k, v)):
+            dst.reshape(G, NT, D)[lo:hi].copy_(src, non_blocking=True)
+        o = step()
+        o_h.copy_(o, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(2):
+        e2e_step()
+    b_.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b_) / 2
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    peaks, peak_kind = measured_peaks()
+    fp8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp8-e4m3 (fp32 accumulate)",
+            "data": "synthetic (seeded configs[4] distributions, generated on device)",
+            "config": {"workload": w["desc"], "B": B, "H": H, "N": NT, "D": D, "block_rows": w["block_rows"],
+                       "units_per_rank": -(-G // world),
+                       "parallelism": f"(batch, head) units over {world} ranks + NCCL all-gather of the output",
+                       "l2": "inputs larger than L2"},
+            "roofline": {"bound": "tensor", "achieved": value / world, "peak": fp8_peak, "unit": "TFLOP/s",
+                         "frac": value / world / fp8_peak, "traffic": None,
+                         "kernel": "whole step per GPU (prepare + attn_tc_kernel + all-gather)",
+                         "peak_note": f"dense FP8 = 2 x {peak_kind} bf16 burst"},
+            "e2e": {"value": fl / (e2e_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_call": e2e_ms,
+                    "h2d_bytes_per_step": 3 * (hi - lo) * NT * D * q.element_size(),
+                    "d2h_bytes_per_step": out.numel() * out.element_size()},
+            "gpu_launches": 8 * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -235,6 +377,8 @@ def main() -> int:
 
     if args.impl == "reference":
         return run_reference_arm(args, w, rank)
+    if w.get("sharded"):
+        return run_sharded(args, w, rank, world, local)
 
     import torch
     import torch.distributed as dist
@@ -265,7 +409,8 @@ def main() -> int:
     torch.cuda.synchronize()
     kmeans_ms = e0.elapsed_time(e1)
     perm = res.perm
-    cfg = TritonConfig(block_n=w["block_rows"], enable_expcast=w["expcast"], sparse=w["sparse"])
+    cfg = TritonConfig(block_n=w["block_rows"], enable_expcast=w["expcast"], sparse=w["sparse"],
+                       tau=w.get("tau", 1.3))
     scale = D ** -0.5
     out = torch.empty_like(q)
 
@@ -273,12 +418,15 @@ def main() -> int:
         if evs is not None:
             evs[0].record()
         p = prepare(q, k, v, perm, block_rows=w["block_rows"], hadamard=True, smooth_k=True,
-                    want_v=True, want_v_t=False)
+                    sparse=cfg.sparse, tau=cfg.tau, q_block=cfg.block_m, scale=scale,
+                    want_v=not cfg.sparse, want_v_t=cfg.sparse, local_blocks=cfg.local_blocks,
+                    sink_blocks=cfg.sink_blocks)
         if evs is not None:
             evs[1].record()
         attention_prepared(p, NT, out, scale, cfg)
         if evs is not None:
             evs[2].record()
+        return p
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -360,7 +508,16 @@ def main() -> int:
 
     peaks, peak_kind = measured_peaks()
     fp8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
-    attn_tflops = fl / (attn_ms / 1e3) / 1e12
+    keep_frac = None
+    if w["sparse"]:
+        pk = step()
+        torch.cuda.synchronize()
+        keep_frac = float(pk.keep.float().mean())
+        del pk
+    # executed work of the attention kernel: dense tiles, or the kept tiles
+    # plus the block-mean proxy of the skipped ones (2*N*NB*D per head each way)
+    fl_exec = fl if keep_frac is None else (keep_frac * fl + 4.0 * G * NT * (NT // w["block_rows"]) * D)
+    attn_tflops = fl_exec / (attn_ms / 1e3) / 1e12
     traffic = None   # DRAM bytes per attention launch from the committed ncu summary
     tpath = os.path.join(ROOT, "profiles", "attn_tc_c1.md")
     if os.path.exists(tpath):
@@ -379,11 +536,15 @@ def main() -> int:
         "config": {"workload": w["desc"], "B": B, "H": H, "N": NT, "D": D, "block_rows": w["block_rows"],
                    "kmeans_k": res.k, "expcast": w["expcast"], "sparse": w["sparse"],
                    "parallelism": f"(batch, head) units x{world} ranks, independent, no collective",
-                   "l2": "inputs larger than L2 (Q/K/V 235 MB each)"},
+                   "l2": "inputs larger than L2 (Q/K/V 235 MB each)",
+                   "keep_fraction": keep_frac,
+                   "block_skip_ratio": None if keep_frac is None else 1.0 - keep_frac},
         "ms_prepare": prep_ms, "ms_attention": attn_ms, "kmeans_ms": kmeans_ms, "psnr_db": psnr,
         "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": fp8_peak, "unit": "TFLOP/s",
                      "frac": attn_tflops / fp8_peak, "traffic": traffic,
-                     "kernel": "attn_tc_kernel (tcgen05)",
+                     "kernel": ("attn_sparse_kernel (mma.sync, tau-routed)" if w["sparse"]
+                                else "attn_tc_kernel (tcgen05)"),
+                     "flops": ("executed (kept tiles + proxy)" if w["sparse"] else "dense"),
                      "peak_note": f"dense FP8 = 2 x {peak_kind} bf16 burst ({peaks.get('bf16_tflops')} TF/s)"},
         "prepare_roofline": {"bound": "hbm", "achieved": prep_bytes / (prep_ms / 1e3) / 1e9,
                              "peak": float(peaks.get("hbm_gbs", 6650.0)), "unit": "GB/s",
