@@ -50,6 +50,12 @@ WORKLOADS = {
                   spatial=None),
     "c3": dict(desc="dense FP8 VC-Attention, B1 H56 N65536 D128, ExpCast on, V-Smooth k=512",
                B=1, H=56, N=65536, D=128, expcast=True, sparse=False, k=512, block_rows=128, spatial=None),
+    "c3nv": dict(desc="configs[3]: NVFP4 QK^T (E2M1, E4M3 per-16 scales, fp32 tensor scale per head) + FP8 PV, "
+                      "B1 H56 N65536 D128, ExpCast on, V-Smooth k=512", B=1, H=56, N=65536, D=128, expcast=True,
+                 sparse=False, k=512, block_rows=128, spatial=None, qk_fp4=True),
+    "c1nv": dict(desc="NVFP4 QK^T + FP8 PV at the configs[1] shape: B1 H56 N16384 D128, ExpCast on, V-Smooth k=64",
+                 B=1, H=56, N=16384, D=128, expcast=True, sparse=False, k=64, block_rows=128, spatial=None,
+                 qk_fp4=True),
     "c4": dict(desc="configs[4]: dense FP8 VC-Attention, B2 (CFG pair) H56 N65536 D128, (batch, head) units "
                     "sharded over the ranks, NCCL all-gather of the bf16 output, ExpCast on, V-Smooth k=512",
                B=2, H=56, N=65536, D=128, expcast=True, sparse=False, k=512, block_rows=128, spatial=None,
@@ -410,7 +416,7 @@ def main() -> int:
     kmeans_ms = e0.elapsed_time(e1)
     perm = res.perm
     cfg = TritonConfig(block_n=w["block_rows"], enable_expcast=w["expcast"], sparse=w["sparse"],
-                       tau=w.get("tau", 1.3))
+                       tau=w.get("tau", 1.3), qk_fp4=w.get("qk_fp4", False))
     scale = D ** -0.5
     out = torch.empty_like(q)
 
@@ -420,7 +426,7 @@ def main() -> int:
         p = prepare(q, k, v, perm, block_rows=w["block_rows"], hadamard=True, smooth_k=True,
                     sparse=cfg.sparse, tau=cfg.tau, q_block=cfg.block_m, scale=scale,
                     want_v=not cfg.sparse, want_v_t=cfg.sparse, local_blocks=cfg.local_blocks,
-                    sink_blocks=cfg.sink_blocks)
+                    sink_blocks=cfg.sink_blocks, qk_fp4=cfg.qk_fp4, v_mma_order=not cfg.qk_fp4)
         if evs is not None:
             evs[1].record()
         attention_prepared(p, NT, out, scale, cfg)
@@ -543,6 +549,7 @@ def main() -> int:
         "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": fp8_peak, "unit": "TFLOP/s",
                      "frac": attn_tflops / fp8_peak, "traffic": traffic,
                      "kernel": ("attn_sparse_kernel (mma.sync, tau-routed)" if w["sparse"]
+                                else "attn_tc_kernel<NVFP4 QK> (tcgen05 mxf4nvf4 + f8f6f4)" if w.get("qk_fp4")
                                 else "attn_tc_kernel (tcgen05)"),
                      "flops": ("executed (kept tiles + proxy)" if w["sparse"] else "dense"),
                      "peak_note": f"dense FP8 = 2 x {peak_kind} bf16 burst ({peaks.get('bf16_tflops')} TF/s)"},

@@ -202,6 +202,35 @@ int vcattn_prepare_fp8(const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_
   return cuda_status(launch_prepare(p, static_cast<cudaStream_t>(stream)), "vcattn_prepare_fp8");
 }
 
+int vcattn_prepare_nvfp4(const vcattn_bhnd* q, const vcattn_bhnd* k, int dtype, int B, int H, int N, int D,
+                         const int32_t* perm, int perm_rows, int block_rows, int flags, uint8_t* q4,
+                         uint8_t* q4_scale, float* q4_g, uint8_t* k4, uint8_t* k4_scale, float* k4_g,
+                         uint8_t* q4_sf_mma, uint8_t* k4_sf_mma, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_prepare_nvfp4")) return fail(VCATTN_ERR_INJECTED, "vcattn_prepare_nvfp4: injected fault");
+  VC_CHECK(dtype_ok(dtype), "vcattn_prepare_nvfp4: unsupported dtype");
+  VC_CHECK(D == 64 || D == 128, "vcattn_prepare_nvfp4: D must be 64 or 128");
+  VC_CHECK(B > 0 && H > 0 && N > 0, "vcattn_prepare_nvfp4: empty shape");
+  VC_CHECK(block_rows == 64 || block_rows == 128, "vcattn_prepare_nvfp4: block_rows must be 64 or 128");
+  VC_CHECK(view_ok(q, dtype) && view_ok(k, dtype),
+           "vcattn_prepare_nvfp4: q/k must be 16-byte aligned with 16-byte multiple strides");
+  VC_CHECK(perm == nullptr || perm_rows == 1 || perm_rows == B * H, "vcattn_prepare_nvfp4: perm_rows must be 1 or G");
+  VC_CHECK(q4 && q4_scale && q4_g && k4 && k4_scale && k4_g, "vcattn_prepare_nvfp4: null output");
+  const int G = B * H;
+  const size_t need = prepare_workspace_bytes(G, N, D);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(VCATTN_ERR_WORKSPACE, "vcattn_prepare_nvfp4: workspace too small (need " + std::to_string(need) + " bytes)");
+  NvfpParams p{};
+  p.q = q; p.k = k; p.dtype = dtype; p.B = B; p.H = H; p.N = N; p.D = D;
+  p.n_pad = (N + block_rows - 1) / block_rows * block_rows;
+  p.block_rows = block_rows; p.flags = flags; p.perm = perm; p.perm_rows = perm ? perm_rows : 0;
+  p.q4 = q4; p.q4_scale = q4_scale; p.q4_g = q4_g; p.k4 = k4; p.k4_scale = k4_scale; p.k4_g = k4_g;
+  p.q4_sf_mma = q4_sf_mma; p.k4_sf_mma = k4_sf_mma;
+  p.workspace = workspace;
+  return cuda_status(launch_prepare_nvfp4(p, static_cast<cudaStream_t>(stream)), "vcattn_prepare_nvfp4");
+}
+
 int vcattn_route_mask(const vcattn_route_stats* route, int G, int N, int n_pad, int D, int block_rows, float tau,
                       int local_blocks, int sink_blocks, float sm_scale, uint8_t* keep, float* thresh,
                       void* stream) {
@@ -282,7 +311,45 @@ int vcattn_attn_status(int* code, int* where, int* block, int reset) {
   VC_CHECK(code && where && block, "vcattn_attn_status: null output");
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_status(e, "vcattn_attn_status");
-  return cuda_status(attn_tc_status(code, where, block, reset != 0), "vcattn_attn_status");
+  int c2 = 0, w2 = 0, b2 = 0;
+  e = attn_tc_status(code, where, block, reset != 0);
+  if (e == cudaSuccess) e = attn_nvfp4_status(&c2, &w2, &b2, reset != 0);
+  if (e == cudaSuccess && *code == 0 && c2 != 0) {
+    *code = c2;
+    *where = 100 + w2;   // waits of the NVFP4 kernel are reported as 100 + site
+    *block = b2;
+  }
+  return cuda_status(e, "vcattn_attn_status");
+}
+
+int vcattn_attn_nvfp4(const uint8_t* q4, const uint8_t* q4_sf_mma, const float* q4_g, const uint8_t* k4,
+                      const uint8_t* k4_sf_mma, const float* k4_g, const uint8_t* v8, const float* v_scale,
+                      const float* mu, int B, int H, int N, int n_pad, int D, int block_rows, float sm_scale,
+                      int flags, double expcast_beta, void* out, int out_dtype, int64_t out_sb, int64_t out_sh,
+                      int64_t out_sn, void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_attn_nvfp4")) return fail(VCATTN_ERR_INJECTED, "vcattn_attn_nvfp4: injected fault");
+  VC_CHECK(q4 && q4_sf_mma && q4_g && k4 && k4_sf_mma && k4_g && v8 && v_scale && mu && out,
+           "vcattn_attn_nvfp4: null pointer");
+  VC_CHECK(D == 128 && block_rows == 128, "vcattn_attn_nvfp4: needs D = 128 and block_rows = 128");
+  VC_CHECK(B > 0 && H > 0 && N > 0, "vcattn_attn_nvfp4: empty shape");
+  VC_CHECK(n_pad >= N && n_pad % 128 == 0 && n_pad - N < 128, "vcattn_attn_nvfp4: n_pad inconsistent with N");
+  VC_CHECK(dtype_ok(out_dtype), "vcattn_attn_nvfp4: unsupported output dtype");
+  VC_CHECK(aligned16(q4) && aligned16(k4) && aligned16(v8) && aligned16(q4_sf_mma) && aligned16(k4_sf_mma) &&
+               aligned16(v_scale) && aligned16(mu),
+           "vcattn_attn_nvfp4: operand buffers must be 16-byte aligned");
+  VC_CHECK(aligned16(out) && (out_sn % 8) == 0 && (out_sh % 8) == 0 && (out_sb % 8) == 0,
+           "vcattn_attn_nvfp4: out must be 16-byte aligned with 8-element multiple strides");
+  AttnParams p{};
+  p.q4 = q4; p.k4 = k4; p.q4_sf = q4_sf_mma; p.k4_sf = k4_sf_mma; p.q4_g = q4_g; p.k4_g = k4_g;
+  p.v8 = v8; p.v_scale = v_scale; p.mu = mu;
+  p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
+  p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
+  p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
+  const cudaError_t e = launch_attn_nvfp4(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(VCATTN_ERR_CUDA, std::string("vcattn_attn_nvfp4: ") + cudaGetErrorString(e) + " [" + attn_nvfp4_diag() + "]");
+  return VCATTN_OK;
 }
 
 int vcattn_attn_fp8_sparse(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,

@@ -16,6 +16,19 @@ struct PrepareParams {
   void* workspace;
 };
 
+// NVFP4 Q / K (no V): the kernels reuse the prepare workspace (K mean,
+// per-head maxima).
+struct NvfpParams {
+  const vcattn_bhnd *q, *k;
+  int dtype, B, H, N, D, n_pad, block_rows, flags;
+  const int32_t* perm;
+  int perm_rows;
+  uint8_t *q4, *q4_scale, *k4, *k4_scale;
+  uint8_t *q4_sf_mma, *k4_sf_mma;   // scale-factor atoms of the block-scaled MMA, or nullptr
+  float *q4_g, *k4_g;
+  void* workspace;
+};
+
 struct RouteParams {
   const float *k_mean, *q_cent, *q_bar;
   int G, N, n_pad, D, block_rows, q_block;
@@ -44,6 +57,9 @@ struct AttnParams {
   const float *k_mean, *v_mean;
   const uint8_t* keep;
   int q_block, group;
+  // NVFP4 QK^T (nullptr for the FP8 kernels)
+  const uint8_t *q4, *k4, *q4_sf, *k4_sf;
+  const float *q4_g, *k4_g;
   int B, H, N, n_pad, D, block_rows;
   float sm_scale;
   double beta;
@@ -57,10 +73,14 @@ size_t prepare_workspace_bytes(int G, int N, int D);
 size_t kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys);
 
 cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t st);
+cudaError_t launch_prepare_nvfp4(const NvfpParams& p, cudaStream_t st);
 cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st);
 cudaError_t launch_kmeans(const KMeansParams& p, cudaStream_t st);
 cudaError_t launch_attn_mma(const AttnParams& p, cudaStream_t st);
 cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t st);
+cudaError_t launch_attn_nvfp4(const AttnParams& p, cudaStream_t st);
+cudaError_t attn_nvfp4_status(int* code, int* where, int* block, bool reset);
+const char* attn_nvfp4_diag();
 cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset);
 const char* attn_tc_diag();
 cudaError_t launch_attn_sparse_mma(const AttnParams& p, cudaStream_t st);

@@ -426,9 +426,158 @@ __global__ void route_mask_kernel(const float* __restrict__ k_mean, const float*
 // ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// NVFP4 Q / K (quant.py:172-204 applied to each (b, h) slab of the rotated,
+// smoothed rows): one fp32 tensor scale g per head, an E4M3 micro scale per
+// 16 consecutive elements along D and E2M1 codes packed two per byte (low
+// nibble = even element).  Pass A takes the head's |x| max (integer atomicMax
+// on the float bits of non-negative values); pass B quantises.  Lanes own
+// four consecutive elements, so a 16-element block spans four lanes.
+// ---------------------------------------------------------------------------
+struct NvArgs {
+  vcattn_bhnd x;
+  int H, N, n_pad, flags;
+  const int32_t* perm;   // K only
+  int perm_rows;
+  const float* kmean;    // (G, D) or nullptr
+  unsigned* amax;        // (G) float bits
+  uint8_t* codes;        // (G, NP, D/2)
+  uint8_t* micro;        // (G, NP, D/16)
+  uint8_t* micro_mma;    // (G, ceil(NP/128), D/64, 512) scale-factor atoms of the block-scaled MMA, or nullptr
+  float* gout;           // (G)
+  int rows;              // rows per CTA
+};
+
+template <int DT, int D, bool QUANT>
+__global__ void __launch_bounds__(256) nvfp4_rows_kernel(NvArgs a) {
+  using RM = RowMap<D>;
+  const int g = blockIdx.y;
+  const int b = g / a.H, h = g % a.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * a.rows;
+  float km[4] = {0.f, 0.f, 0.f, 0.f};
+  if (a.kmean != nullptr) {
+    const float4 t = *reinterpret_cast<const float4*>(a.kmean + g * D + RM::col(lane));
+    km[0] = t.x; km[1] = t.y; km[2] = t.z; km[3] = t.w;
+  }
+  float gs = 0.f;
+  if constexpr (QUANT) {
+    gs = fmaxf(__fdiv_rn(fmaxf(__uint_as_float(a.amax[g]), kTiny), 6.0f * kE4M3Max), kTiny);
+    if (blockIdx.x == 0 && threadIdx.x == 0) a.gout[g] = gs;
+  }
+  float mx = 0.f;
+  const int nwarps = blockDim.x >> 5;
+  constexpr int kBatch = 8;
+  const int step = nwarps * RM::kRowsPerWarp;
+  for (int base0 = warp * RM::kRowsPerWarp; base0 < a.rows; base0 += kBatch * step) {
+    float vb[kBatch][4];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int t = r0 + base0 + u * step + RM::sub(lane);
+      vb[u][0] = vb[u][1] = vb[u][2] = vb[u][3] = 0.f;
+      if (base0 + u * step < a.rows && t < a.N) {
+        const int src = source_row(a.perm, a.perm_rows, g, a.N, t);
+        const float4 x = load4<DT>(a.x.data, b * a.x.sb + h * a.x.sh + static_cast<int64_t>(src) * a.x.sn + RM::col(lane));
+        vb[u][0] = x.x; vb[u][1] = x.y; vb[u][2] = x.z; vb[u][3] = x.w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      if (base0 + u * step >= a.rows) break;
+      const int t = r0 + base0 + u * step + RM::sub(lane);
+      float* v = vb[u];
+      const bool real = t < a.N;
+      if (a.flags & VCATTN_HADAMARD) RM::fwht(v, lane);
+      if (!real) { v[0] = v[1] = v[2] = v[3] = 0.f; }
+      else if (a.kmean != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __fsub_rn(v[i], km[i]);
+      }
+      float bm = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+      if constexpr (!QUANT) {
+        mx = fmaxf(mx, bm);
+      } else {
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));
+        bm = fmaxf(bm, kTiny);
+        const float micro = __fdiv_rn(__fdiv_rn(bm, 6.0f), gs);
+        const uint32_t mcode = e4m3x2(fminf(micro, kE4M3Max), 0.f) & 0xffu;
+        const float denom = fmaxf(__fmul_rn(gs, e4m3_to_float(mcode)), kTiny);
+        if (t < a.n_pad) {
+          const int64_t row = static_cast<int64_t>(g) * a.n_pad + t;
+          const uint32_t lo = e2m1x2(__fdiv_rn(v[0], denom), __fdiv_rn(v[1], denom));
+          const uint32_t hi = e2m1x2(__fdiv_rn(v[2], denom), __fdiv_rn(v[3], denom));
+          *reinterpret_cast<uint16_t*>(a.codes + row * (D / 2) + RM::col(lane) / 2) =
+              static_cast<uint16_t>(lo | (hi << 8));
+          if ((lane & 3) == 0) {
+            const int kb = RM::col(lane) / 16;
+            a.micro[row * (D / 16) + kb] = static_cast<uint8_t>(mcode);
+            if (a.micro_mma != nullptr) {
+              // 128-row tile, 512-byte atom per 4 scales: byte 16 (m%32) + 4 (m/32) + kb%4
+              const int m = t & 127;
+              const int64_t tiles = (a.n_pad + 127) / 128;
+              const int64_t atom = ((static_cast<int64_t>(g) * tiles + (t >> 7)) * (D / 64) + (kb >> 2)) * 512;
+              a.micro_mma[atom + (m & 31) * 16 + (m >> 5) * 4 + (kb & 3)] = static_cast<uint8_t>(mcode);
+            }
+          }
+        }
+      }
+    }
+  }
+  if constexpr (!QUANT) {
+    mx = warp_max(mx);
+    if (lane == 0) atomicMax(a.amax + g, __float_as_uint(mx));
+  }
+}
+
+template <int DT, int D>
+static cudaError_t prepare_nvfp4_impl(const NvfpParams& p, cudaStream_t st) {
+  const int G = p.B * p.H;
+  float* kmean = nullptr;
+  const int nchunks = (p.N + kChunkRows - 1) / kChunkRows;
+  double* partial = reinterpret_cast<double*>(p.workspace);
+  unsigned* amax = reinterpret_cast<unsigned*>(reinterpret_cast<float*>(partial + static_cast<size_t>(G) * nchunks * D) +
+                                               static_cast<size_t>(G) * D);
+  if (p.flags & VCATTN_SMOOTH_K) {
+    kmean = reinterpret_cast<float*>(partial + static_cast<size_t>(G) * nchunks * D);
+    kmean_partial_kernel<DT, D><<<dim3(nchunks, G), 256, 0, st>>>(*p.k, p.H, p.N, p.flags, partial);
+    kmean_final_kernel<D><<<G, D, 0, st>>>(partial, nchunks, p.N, kmean);
+  }
+  cudaMemsetAsync(amax, 0, 2 * static_cast<size_t>(G) * sizeof(unsigned), st);
+  const int rows = 128;
+  const dim3 grid((p.n_pad + rows - 1) / rows, G);
+  NvArgs aq{};
+  aq.x = *p.q; aq.H = p.H; aq.N = p.N; aq.n_pad = p.n_pad; aq.flags = p.flags;
+  aq.amax = amax; aq.codes = p.q4; aq.micro = p.q4_scale; aq.micro_mma = p.q4_sf_mma; aq.gout = p.q4_g; aq.rows = rows;
+  NvArgs ak = aq;
+  ak.x = *p.k; ak.perm = p.perm; ak.perm_rows = p.perm_rows; ak.kmean = kmean;
+  ak.amax = amax + G; ak.codes = p.k4; ak.micro = p.k4_scale; ak.micro_mma = p.k4_sf_mma; ak.gout = p.k4_g;
+  nvfp4_rows_kernel<DT, D, false><<<grid, 256, 0, st>>>(aq);
+  nvfp4_rows_kernel<DT, D, false><<<grid, 256, 0, st>>>(ak);
+  nvfp4_rows_kernel<DT, D, true><<<grid, 256, 0, st>>>(aq);
+  nvfp4_rows_kernel<DT, D, true><<<grid, 256, 0, st>>>(ak);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prepare_nvfp4(const NvfpParams& p, cudaStream_t st) {
+  if (p.D == 128) {
+    switch (p.dtype) {
+      case VCATTN_DTYPE_BF16: return prepare_nvfp4_impl<VCATTN_DTYPE_BF16, 128>(p, st);
+      case VCATTN_DTYPE_F16: return prepare_nvfp4_impl<VCATTN_DTYPE_F16, 128>(p, st);
+      default: return prepare_nvfp4_impl<VCATTN_DTYPE_F32, 128>(p, st);
+    }
+  }
+  switch (p.dtype) {
+    case VCATTN_DTYPE_BF16: return prepare_nvfp4_impl<VCATTN_DTYPE_BF16, 64>(p, st);
+    case VCATTN_DTYPE_F16: return prepare_nvfp4_impl<VCATTN_DTYPE_F16, 64>(p, st);
+    default: return prepare_nvfp4_impl<VCATTN_DTYPE_F32, 64>(p, st);
+  }
+}
+
 size_t prepare_workspace_bytes(int G, int N, int D) {
   const size_t nchunks = (N + kChunkRows - 1) / kChunkRows;
-  return static_cast<size_t>(G) * nchunks * D * sizeof(double) + static_cast<size_t>(G) * D * sizeof(float) + 256;
+  return static_cast<size_t>(G) * nchunks * D * sizeof(double) + static_cast<size_t>(G) * D * sizeof(float) +
+         2 * static_cast<size_t>(G) * sizeof(unsigned) + 256;
 }
 
 template <int DT, int D>

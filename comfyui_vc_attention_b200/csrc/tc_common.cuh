@@ -309,6 +309,52 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) { return smem_de
 // 1024 bytes apart (one MN block, so the leading offset is unused).
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr) { return smem_desc(saddr, 16, 1024); }
 
+// 64-byte swizzle K-major operand (rows of 64 bytes, e.g. 128 E2M1 values):
+// 8-row groups 512 bytes apart; the K slice is selected by the start address.
+constexpr uint64_t kLayoutSW64 = 4;
+__device__ __forceinline__ uint64_t desc_kmajor64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1) << 16;                    // leading offset unused (16 B)
+  d |= static_cast<uint64_t>((512u >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= kLayoutSW64 << 61;
+  return d;
+}
+// Scale-factor atom in shared memory (32 rows x 16 bytes, no swizzle): the
+// source of tcgen05.cp .32x128b.
+__device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1) << 16;                    // 16 B
+  d |= static_cast<uint64_t>((128u >> 4) & 0x3FFFu) << 32;  // 8-row groups 128 B apart
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;
+}
+// Copy one scale-factor atom (128 rows x 4 scales, 512 bytes laid out as 32
+// lines of 16 bytes: row m, scale k at 16 (m % 32) + 4 (m / 32) + k) into 4
+// TMEM columns, replicated to the four lane quarters.
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// Instruction descriptor of kind::mxf4nvf4: E2M1 A and B (format 1), UE4M3
+// scales per 16 elements, K-major, f32 accumulate, scale-factor ids 0.
+__host__ __device__ constexpr uint32_t idesc_nvfp4(int M, int N) {
+  return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+// D[tmem] (+)= (A . SFA) (B . SFB)^T, K = 64 E2M1 values per instruction;
+// the scale factors of this K slice start at TMEM columns sfa and sfb.
+__device__ __forceinline__ void mma_nvfp4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa,
+                                          uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
 // Instruction descriptor, kind::f8f6f4 with E4M3 operands and f32 accumulate.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N, bool b_mn_major) {
   return (1u << 4)                                   // D format f32

@@ -74,6 +74,13 @@ _SIGNATURES = {
                                    c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                    c_void_p, c_void_p, POINTER(RouteStats), c_void_p, c_size_t,
                                    c_void_p]),
+    "vcattn_attn_nvfp4": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
+                                  c_int, c_double, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p]),
+    "vcattn_prepare_nvfp4": (c_int, [POINTER(BHND), POINTER(BHND), c_int, c_int, c_int, c_int, c_int,
+                                     c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                     c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     c_size_t, c_void_p]),
     "vcattn_prepare_fp8_noalloc": (c_int, [POINTER(BHND), POINTER(BHND), POINTER(BHND), c_int, c_int,
                                            c_int, c_int, c_int, c_void_p, c_int, c_int, c_int,
                                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

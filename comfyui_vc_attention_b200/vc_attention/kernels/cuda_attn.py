@@ -69,10 +69,10 @@ class Prepared(NamedTuple):
     v_scale: torch.Tensor      # (B, H, NB, D) fp32
     mu: torch.Tensor           # (B, H, NB, D) fp32 block mean / v_scale
     n_pad: int
-    q4: Optional[torch.Tensor] = None
-    q4_scale: Optional[torch.Tensor] = None
-    k4: Optional[torch.Tensor] = None
-    k4_scale: Optional[torch.Tensor] = None
+    q4: Optional[torch.Tensor] = None        # (B, H, NP, D/2) uint8 E2M1 pairs, low nibble first
+    q4_scale: Optional[torch.Tensor] = None  # (B, H, NP, D/16) uint8 E4M3 micro scales
+    k4: Optional[torch.Tensor] = None        # (B, H, NP, D/2) token-major (the reference: K-first)
+    k4_scale: Optional[torch.Tensor] = None  # (B, H, NP, D/16)
     k_mean: Optional[torch.Tensor] = None   # (B, H, NB, D) fp32
     v_mean: Optional[torch.Tensor] = None   # (B, H, NB, D) fp32
     thresh: Optional[torch.Tensor] = None   # (B, H, NQB) fp32
@@ -84,6 +84,10 @@ class Prepared(NamedTuple):
     keep: Optional[torch.Tensor] = None     # (G, NQB, NB) uint8 routing mask
     block_rows: int = 128
     v_mma_order: bool = False               # v rows in the tcgen05 kernel's key order
+    q4_g: Optional[torch.Tensor] = None     # (G,) fp32 NVFP4 tensor scale per head
+    k4_g: Optional[torch.Tensor] = None
+    q4_sf_mma: Optional[torch.Tensor] = None  # (G, NP/128, D/64, 512) micro scales in MMA atom order
+    k4_sf_mma: Optional[torch.Tensor] = None
 
 
 def has_kernel() -> bool:
@@ -119,13 +123,15 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
             block_rows: int = 128, hadamard: bool = True, smooth_k: bool = True, *,
             sparse: bool = False, tau: float = 1.3, q_block: int = 64,
             scale: Optional[float] = None, want_v: bool = True, want_v_t: bool = False,
-            local_blocks: int = 1, sink_blocks: int = 0, v_mma_order: bool = True) -> Prepared:
+            local_blocks: int = 1, sink_blocks: int = 0, v_mma_order: bool = True,
+            qk_fp4: bool = False) -> Prepared:
     """Quantise and permute Q/K/V into the kernel layout (triton_attn.py:504-579).
 
     Byte-identical to the reference's portable ``prepare`` on the codes; the
     scales that depend on a token/block mean differ from it only in the last
     bits (the mean is rounded once here).  With ``sparse=True`` the routing
-    statistics and the block mask are produced as well.
+    statistics and the block mask are produced as well; with ``qk_fp4=True``
+    the NVFP4 Q/K of quant.py:172-204 (one tensor scale per head) too.
     """
     _check_qkv(q, k, v)
     lib = N.lib()
@@ -179,6 +185,21 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
         qv, kv, vv, dt, b, h, n, d, _ptr(perm_t), perm_rows, block_rows, flags,
         q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), _ptr(v8), vs.data_ptr(),
         mu.data_ptr(), _ptr(v8t), route, ws.data_ptr(), ws_bytes, _stream(q)))
+    q4 = q4s = k4 = k4s = q4g = k4g = q4sf = k4sf = None
+    if qk_fp4:
+        q4 = torch.empty((g, n_pad, d // 2), dtype=u8, device=dev)
+        k4 = torch.empty((g, n_pad, d // 2), dtype=u8, device=dev)
+        q4s = torch.empty((g, n_pad, d // 16), dtype=u8, device=dev)
+        k4s = torch.empty((g, n_pad, d // 16), dtype=u8, device=dev)
+        q4g = torch.empty((g,), dtype=torch.float32, device=dev)
+        k4g = torch.empty((g,), dtype=torch.float32, device=dev)
+        tiles = -(-n_pad // 128)
+        q4sf = torch.empty((g, tiles, d // 64, 512), dtype=u8, device=dev)
+        k4sf = torch.empty((g, tiles, d // 64, 512), dtype=u8, device=dev)
+        N.check("vcattn_prepare_nvfp4", lib.vcattn_prepare_nvfp4(
+            qv, kv, dt, b, h, n, d, _ptr(perm_t), perm_rows, block_rows, flags & ~N.V_MMA_ORDER,
+            q4.data_ptr(), q4s.data_ptr(), q4g.data_ptr(), k4.data_ptr(), k4s.data_ptr(), k4g.data_ptr(),
+            q4sf.data_ptr(), k4sf.data_ptr(), ws.data_ptr(), ws_bytes, _stream(q)))
     keep = thresh = None
     nqb = 0
     if sparse:
@@ -194,7 +215,12 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
         k_mean=None if k_mean is None else k_mean.view(b, h, nb, d),
         v_mean=None if v_mean is None else v_mean.view(b, h, nb, d),
         thresh=None if thresh is None else thresh.view(b, h, nqb), n_qblk=nqb,
-        v_t=v8t, q_cent=q_cent, q_bar=q_bar, keep=keep, block_rows=block_rows, v_mma_order=v_mma_order)
+        v_t=v8t, q_cent=q_cent, q_bar=q_bar, keep=keep, block_rows=block_rows, v_mma_order=v_mma_order,
+        q4=None if q4 is None else q4.view(b, h, n_pad, d // 2),
+        q4_scale=None if q4s is None else q4s.view(b, h, n_pad, d // 16),
+        k4=None if k4 is None else k4.view(b, h, n_pad, d // 2),
+        k4_scale=None if k4s is None else k4s.view(b, h, n_pad, d // 16), q4_g=q4g, k4_g=k4g,
+        q4_sf_mma=q4sf, k4_sf_mma=k4sf)
 
 
 def route_mask(route: "N.RouteStats", g: int, n: int, n_pad: int, d: int, block_rows: int, tau: float,
@@ -264,14 +290,16 @@ def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         scale = d ** -0.5
     if cfg.qk_fp4 and cfg.sparse:
         cfg = TritonConfig(**{**cfg.__dict__, "qk_fp4": False})
-    if cfg.qk_fp4:
-        raise NotImplementedError("NVFP4 QK^T kernel is not built in this version")
     br = cfg.block_n
     sparse = bool(cfg.sparse)
+    fp4 = bool(cfg.qk_fp4)
+    if fp4 and (d != 128 or br != 128):
+        raise ValueError("the NVFP4 QK kernel needs D = 128 and block_n = 128")
     use_tc = d == 128 and not sparse
     p = prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
                 tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=use_tc, want_v_t=not use_tc,
-                local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks)
+                local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks, v_mma_order=not fp4,
+                qk_fp4=fp4)
     out = _out_view(q, q.dtype)
     return attention_prepared(p, n, out, scale, cfg)
 
@@ -291,6 +319,15 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
     q8 = p.q.view(torch.uint8)
     k8 = p.k.view(torch.uint8)
     st = _stream(out)
+    if cfg.qk_fp4 and not cfg.sparse:
+        if p.q4 is None or p.v is None or p.v_mma_order:
+            raise ValueError("the NVFP4 kernel needs prepare(qk_fp4=True, want_v=True, v_mma_order=False)")
+        N.check("vcattn_attn_nvfp4", lib.vcattn_attn_nvfp4(
+            p.q4.data_ptr(), p.q4_sf_mma.data_ptr(), p.q4_g.data_ptr(), p.k4.data_ptr(), p.k4_sf_mma.data_ptr(),
+            p.k4_g.data_ptr(), p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(),
+            b, h, n, n_pad, d, p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
+            out.stride(0), out.stride(1), out.stride(2), st))
+        return out
     if cfg.sparse:
         if p.v_t is None:
             raise ValueError("the sparse kernel needs the block-transposed V codes (want_v_t=True)")

@@ -126,6 +126,29 @@ VCATTN_API int vcattn_prepare_fp8(const vcattn_bhnd* q, const vcattn_bhnd* k, co
                        const vcattn_route_stats* route,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- NVFP4 Q / K: quant.py:172-204 per (b, h) slab; replaces the NVFP4 half
+ * of triton_attn.py:693-702 (nvfp4_pack, whose Triton path has no tensor
+ * scale) with the tensor-scaled form of configs[3].
+ * Quantises the same rotated (VCATTN_HADAMARD) and, for K, smoothed
+ * (VCATTN_SMOOTH_K, over the N real rows) and perm-gathered rows as
+ * vcattn_prepare_fp8, zero-padded to NP = ceil(N / block_rows) * block_rows:
+ *    q4, k4 (G,NP,D/2): E2M1 codes, two per byte, low nibble = even element
+ *       (token-major for both; the reference stores K transposed);
+ *    q4_scale, k4_scale (G,NP,D/16): E4M3 micro scale per 16 elements;
+ *    q4_g, k4_g (G): fp32 tensor scale g = max(amax, 1e-30) / 2688 per head.
+ * x = fp4(x / max(g * micro, 1e-30)) * micro * g.
+ * q4_sf_mma, k4_sf_mma: NULL, or the same micro scales again in the layout
+ *    the block-scaled tcgen05 MMA reads (G, ceil(NP/128), D/64, 512): per
+ *    128-row tile and 4 scales one 512-byte atom, row m / scale kb at byte
+ *    16 (m % 32) + 4 (m / 32) + kb % 4.
+ * The workspace is the one of vcattn_prepare_workspace_bytes (always needed
+ * here). */
+VCATTN_API int vcattn_prepare_nvfp4(const vcattn_bhnd* q, const vcattn_bhnd* k, int dtype, int B, int H, int N,
+                                    int D, const int32_t* perm, int perm_rows, int block_rows, int flags,
+                                    uint8_t* q4, uint8_t* q4_scale, float* q4_g, uint8_t* k4, uint8_t* k4_scale,
+                                    float* k4_g, uint8_t* q4_sf_mma, uint8_t* k4_sf_mma, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
 /* ---- prepare without a workspace (no counterpart in the reference) ------
  * Same inputs, outputs and results as vcattn_prepare_fp8, for callers that
  * cannot allocate device memory: a host that owns every device byte through
@@ -150,6 +173,21 @@ VCATTN_API int vcattn_prepare_fp8_noalloc(const vcattn_bhnd* q, const vcattn_bhn
 VCATTN_API int vcattn_route_mask(const vcattn_route_stats* route, int G, int N, int n_pad, int D,
                       int block_rows, float tau, int local_blocks, int sink_blocks,
                       float sm_scale, uint8_t* keep, float* thresh, void* stream);
+
+/* ---- fused attention with NVFP4 QK^T: the QK_FP4 branch of
+ * triton_attn.py:227-239, 263-271 (+ launch :831-844), tensor-scaled NVFP4.
+ * q4, k4 (G,NP,D/2), the scale-factor atoms q4_sf_mma, k4_sf_mma and the
+ * tensor scales q4_g, k4_g from vcattn_prepare_nvfp4; v8, v_scale, mu from
+ * vcattn_prepare_fp8 WITHOUT VCATTN_V_MMA_ORDER (token-order V rows).
+ * s = dot_blockscaled(q4, k4) * g_q * g_k * sm_scale; P, V as in
+ * vcattn_attn_fp8.  D = 128, block_rows = 128.  Bounded waits report through
+ * vcattn_attn_status() (site numbers offset by 100). */
+VCATTN_API int vcattn_attn_nvfp4(const uint8_t* q4, const uint8_t* q4_sf_mma, const float* q4_g,
+                                 const uint8_t* k4, const uint8_t* k4_sf_mma, const float* k4_g,
+                                 const uint8_t* v8, const float* v_scale, const float* mu, int B, int H, int N,
+                                 int n_pad, int D, int block_rows, float sm_scale, int flags,
+                                 double expcast_beta, void* out, int out_dtype, int64_t out_sb,
+                                 int64_t out_sh, int64_t out_sn, void* stream);
 
 /* ---- fused dense FP8 attention: triton_attn.py:203-322 (+ launch :831-844)
  * The tcgen05 kernel (D = 128, block_rows 64 or 128).  Consumes the prepare

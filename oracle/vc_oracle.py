@@ -575,6 +575,12 @@ def _exact_tile(q8s, qs_rows, k8_blk, ks_blk, v8_blk, vs_row, mu_row, valid, sm_
     s_dot = np.matmul(q8s, k8_blk.T).astype(np.float32)
     s = (s_dot * (qs_rows[:, None] * ks_blk[None, :]).astype(np.float32)).astype(np.float32)
     s = (s * F32(sm_scale)).astype(np.float32)
+    return _tile_from_scores(s, v8_blk, vs_row, mu_row, valid, m_i, l_i, acc, expcast, beta)
+
+
+def _tile_from_scores(s, v8_blk, vs_row, mu_row, valid, m_i, l_i, acc, expcast, beta):
+    """The part of the exact tile after the scores: online max, P bytes, row
+    sum and the V-Smooth accumulation (triton_attn.py:272-318)."""
     s = np.where(valid[None, :], s, F32(-1e30))
     m_new = np.maximum(m_i, s.max(-1))
     m_new = np.where(np.isneginf(m_new), F32(0), m_new).astype(np.float32)
@@ -622,6 +628,45 @@ def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_
                     q8[gi, sm:em], qs[gi, sm:em], k8[gi, js:je], ks[gi, js:je], v8[gi, js:je],
                     vs[gi, j], mu[gi, j], np.arange(js, je) < n, sm_scale, m_i, l_i, acc,
                     expcast, beta)
+            out[gi, sm:em] = acc / l_i[:, None]
+    return out
+
+
+def attention_codes_nvfp4(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_m: int,
+                          sm_scale: float, expcast: bool = False, beta: float = -0.35) -> np.ndarray:
+    """NVFP4-QK variant of attention_codes (triton_attn.py:227-239, 263-271 with
+    the tensor-scaled NVFP4 of quant.py:172-204): Q and K are the NVFP4 codes
+    of the rotated (and smoothed) rows with one tensor scale per head,
+    s = dot(q4 * micro_q, k4 * micro_k) * fp32(fp32(g_q * g_k) * sm_scale)
+    (the block-scaled MMA's product, then one scale for the whole head); P and
+    V stay FP8 exactly as in attention_codes.  Returns (G, N, D) float32.
+    """
+    def deq(x_t):
+        packed, micro, gs = nvfp4_per_head(x_t)
+        g_, np_, dh = packed.shape
+        codes = np.stack([packed & 0xF, packed >> 4], axis=-1).reshape(g_, np_, dh * 2)
+        vals = fp4_decode(codes).astype(np.float32) * np.repeat(e4m3_decode(micro).astype(np.float32), 16, axis=-1)
+        return vals.astype(np.float32), gs
+    q4, gq = deq(prep["q_t"])
+    k4, gk = deq(prep["k_t"])
+    v8 = e4m3_decode(prep["v"])
+    vs, mu = prep["v_scale"], prep["mu"]
+    g, n_pad, d = q4.shape
+    nb = n_pad // block_rows
+    out = np.zeros((g, n, d), np.float32)
+    for gi in range(g):
+        c = F32(F32(gq[gi] * gk[gi]) * F32(sm_scale))
+        for sm in range(0, n, block_m):
+            em = min(n, sm + block_m)
+            rows = em - sm
+            m_i = np.full(rows, -np.inf, np.float32)
+            l_i = np.zeros(rows, np.float32)
+            acc = np.zeros((rows, d), np.float32)
+            for j in range(nb):
+                js, je = j * block_rows, (j + 1) * block_rows
+                s = (np.matmul(q4[gi, sm:em], k4[gi, js:je].T).astype(np.float32) * c).astype(np.float32)
+                m_i, l_i, acc = _tile_from_scores(s, v8[gi, js:je], vs[gi, j], mu[gi, j], np.arange(js, je) < n,
+                                                  m_i, l_i, acc, expcast, beta)
             out[gi, sm:em] = acc / l_i[:, None]
     return out
 

@@ -423,3 +423,61 @@ def test_sparse_ragged_and_multi_group(dev):
     assert np.array_equal(keep, keep_o)
     ref = O.attention_sparse_codes(prep, st, keep, n, 128, 64, 128 ** -0.5, group=16)
     assert O.rel_l2(got, ref) <= REL_L2_CODES
+
+
+# ------------------------------------------------------------ NVFP4 Q / K ----
+
+@pytest.mark.parametrize("n,d,br", [(1024, 128, 128), (1000, 128, 128), (700, 64, 64)])
+def test_prepare_nvfp4_bit_exact(dev, n, d, br):
+    """E2M1 codes, E4M3 micro scales and the per-head tensor scale equal the
+    oracle's quant.py:172-204 on each head's rotated (and smoothed) slab."""
+    h = 2
+    q, k, v = make_qkv(1, h, n, d, seed=7)
+    perm = np.stack([np.random.default_rng(i).permutation(n) for i in range(h)]).astype(np.int32)
+    p = _prep_gpu(q, k, v, perm, br, dev, qk_fp4=True)
+    ref = O.prepare(q.reshape(h, n, d), k.reshape(h, n, d), v.reshape(h, n, d), perm, block_rows=br)
+    n_pad = p.n_pad
+    for name, pk, ps, pg in (("q_t", p.q4, p.q4_scale, p.q4_g), ("k_t", p.k4, p.k4_scale, p.k4_g)):
+        packed, micro, gs = O.nvfp4_per_head(ref[name])
+        np.testing.assert_array_equal(pk.reshape(h, n_pad, d // 2).cpu().numpy(), packed, err_msg=name)
+        np.testing.assert_array_equal(ps.reshape(h, n_pad, d // 16).cpu().numpy(), micro, err_msg=name)
+        np.testing.assert_array_equal(pg.cpu().numpy(), gs, err_msg=name)
+
+
+@pytest.mark.parametrize("n,expcast", [(1024, False), (1024, True), (1000, True)])
+def test_attention_nvfp4_matches_oracle(dev, n, expcast):
+    """NVFP4 QK^T (block-scaled tcgen05 MMA) + FP8 PV against the oracle of
+    the same arithmetic (Q/K dequantised from NVFP4, P/V FP8)."""
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
+                                                                          attention_status)
+    h = 2
+    q, k, v = make_qkv(1, h, n, 128, seed=11)
+    perm = np.stack([np.random.default_rng(i).permutation(n) for i in range(h)]).astype(np.int32)
+    p = _prep_gpu(q, k, v, perm, 128, dev, qk_fp4=True, want_v=True, v_mma_order=False)
+    out = torch.empty((1, h, n, 128), dtype=torch.float32, device=dev)
+    cfg = TritonConfig(block_n=128, enable_expcast=expcast, qk_fp4=True)
+    attention_prepared(p, n, out, 128 ** -0.5, cfg)
+    torch.cuda.synchronize()
+    assert attention_status() == (0, 0, 0)
+    got = out.cpu().numpy().reshape(h, n, 128)
+    qg, kg, vg = (a.reshape(h, n, 128) for a in (q, k, v))
+    prep = O.prepare(qg, kg, vg, perm, block_rows=128)
+    ref = O.attention_codes_nvfp4(prep, n, 128, 128, 128 ** -0.5, expcast=expcast)
+    assert O.rel_l2(got, ref) <= REL_L2_CODES
+    assert O.psnr(got, O.sdpa_f32(qg, kg, vg)) > 20.0
+
+
+def test_vc_attention_cuda_nvfp4_entry_point(dev):
+    """The public entry point with TritonConfig(qk_fp4=True), bf16 in / out."""
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import TritonConfig, vc_attention_cuda
+    h, n = 2, 1024
+    q, k, v = make_qkv(1, h, n, 128, seed=12)
+    perm = np.stack([np.random.default_rng(10 + i).permutation(n) for i in range(h)]).astype(np.int32)
+    out = vc_attention_cuda(_bf16(q, dev), _bf16(k, dev), _bf16(v, dev), _t(perm, dev),
+                            TritonConfig(block_n=128, enable_expcast=True, qk_fp4=True))
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy().reshape(h, n, 128)
+    qg, kg, vg = (a.reshape(h, n, 128) for a in (q, k, v))
+    ref = O.attention_codes_nvfp4(O.prepare(qg, kg, vg, perm, block_rows=128), n, 128, 128, 128 ** -0.5,
+                                  expcast=True)
+    assert O.rel_l2(got, ref) <= 5e-3      # bf16 output rounding

@@ -205,3 +205,21 @@ def test_sparse_oracle_keep_all_equals_dense(c0):
     dense = O.attention_codes(prep, 1024, 64, 64, 128 ** -0.5)
     sparse = O.attention_sparse_codes(prep, st, keep, 1024, 64, 64, 128 ** -0.5)
     assert np.array_equal(dense, sparse)
+
+
+def test_attention_codes_nvfp4_close_to_float64():
+    """The NVFP4-QK restatement equals a float64 evaluation of the same
+    definition (dequantised NVFP4 Q/K, FP8 P and V) to fp32 rounding, and
+    stays close to exact attention on small inputs."""
+    import numpy as np
+    from oracle.inputs import make_qkv
+    q, k, v = make_qkv(1, 1, 256, 128, seed=3)
+    perm = np.arange(256, dtype=np.int32)[None]
+    prep = O.prepare(q.reshape(1, 256, 128), k.reshape(1, 256, 128), v.reshape(1, 256, 128), perm, block_rows=128)
+    out = O.attention_codes_nvfp4(prep, 256, 128, 128, 128 ** -0.5)
+    fp8 = O.attention_codes(prep, 256, 128, 128, 128 ** -0.5)
+    sd = O.sdpa_f32(q.reshape(1, 256, 128), k.reshape(1, 256, 128), v.reshape(1, 256, 128))
+    assert np.isfinite(out).all()
+    assert O.rel_l2(out, sd) < 0.1
+    assert O.rel_l2(out, fp8) < 0.1
+    assert O.psnr(out, sd) > 20.0
