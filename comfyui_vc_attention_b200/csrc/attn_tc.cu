@@ -91,8 +91,9 @@ struct TcSmem {
   alignas(8) uint64_t s_full[2];
   alignas(8) uint64_t p_full[2];
   alignas(8) uint64_t t_full[2];
-  alignas(8) uint64_t tr_free[2];  // T buffer b holds nothing unread (T_{i-1} done, R_i read)
-  alignas(8) uint64_t q0_free;     // first quarter of T_i read: R_{i+1} may land there
+  // Correction of tile i has read R_i and the first quarter of T_i (and all
+  // of T_{i-1}): PV_{i+1} / R_{i+1} may write T_{(i+1)&1} and T_i[0,16).
+  alignas(8) uint64_t t_rel;
   alignas(8) uint64_t a_full[kRing];
   alignas(8) uint64_t a_free[kRing];
   alignas(8) uint64_t f_full[kRing];
@@ -204,9 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.s_full[b], 1);
       mbar_init(&sm.p_full[b], 8);
       mbar_init(&sm.t_full[b], 1);
-      mbar_init(&sm.tr_free[b], 4);
     }
-    mbar_init(&sm.q0_free, 4);
+    mbar_init(&sm.t_rel, 4);
     for (int r = 0; r < kRing; ++r) {
       mbar_init(&sm.a_full[r], 8);
       mbar_init(&sm.a_free[r], 4);
@@ -267,7 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    {
+      const uint32_t leader = elect_one();
       const uint32_t id_qk = idesc_e4m3(kBM, BR, false);
       const uint32_t id_pv = idesc_e4m3(kBM, kD, true);
       const uint32_t id_r = idesc_e4m3(kBM, 16, false);
@@ -285,34 +286,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t k_addr = smem_u32(sm.k[s]);
 #pragma unroll
           for (int kk = 0; kk < kD / 32; ++kk)
-            mma_f8(tbase + kColS + b * 128, desc_kmajor(q_addr + kk * 32), desc_kmajor(k_addr + kk * 32), id_qk,
-                   kk > 0);
-          tc_commit(&sm.s_full[b]);
+            mma_f8_if(tbase + kColS + b * 128, desc_kmajor(q_addr + kk * 32), desc_kmajor(k_addr + kk * 32), id_qk,
+                   kk > 0, leader);
+          tc_commit_if(&sm.s_full[b], leader);
         }
         if (j >= 1) {
           const int i = j - 1, bi = i & 1, si = i % kStages;
-          ok = mbar_wait(&sm.p_full[bi], (i >> 1) & 1, abort, status, 5);
-          // T_bi last held T_{i-2} and R_{i-1}: both read (signalled at tile i-1).
-          if (ok && i >= 1) ok = mbar_wait(&sm.tr_free[bi], ((i - 1) >> 1) & 1, abort, status, 6);
-          // R_i goes over the first quarter of T_{i-1}, already read.
-          if (ok && i >= 1) ok = mbar_wait(&sm.q0_free, (i - 1) & 1, abort, status, 9);
+          // T_bi last held T_{i-2} and R_{i-1}; R_i goes over the first
+          // quarter of T_{i-1}: all three read once tile i-1 is released.
+          ok = i >= 1 ? mbar_wait2(&sm.p_full[bi], (i >> 1) & 1, &sm.t_rel, (i - 1) & 1, abort, status, 5)
+                      : mbar_wait(&sm.p_full[bi], (i >> 1) & 1, abort, status, 5);
           if (!ok) break;
           tc_fence_after();
           const uint32_t v_addr = smem_u32(sm.v[si]);
           const uint32_t p_t = tbase + kColS + bi * 128;   // A positions [32kk, 32kk+32) at columns 8kk..8kk+7
 #pragma unroll
           for (int kk = 0; kk < BR / 32; ++kk)
-            mma_f8_ts(tbase + kColT + bi * 128, p_t + 8 * kk, desc_mnmajor(v_addr + kk * 32 * 128), id_pv,
-                      kk > 0);
+            mma_f8_ts_if(tbase + kColT + bi * 128, p_t + 8 * kk, desc_mnmajor(v_addr + kk * 32 * 128), id_pv,
+                      kk > 0, leader);
 #pragma unroll
           for (int kk = 0; kk < BR / 32; ++kk)
-            mma_f8_ts(tbase + kColT + (bi ^ 1) * 128, p_t + 8 * kk, desc_kmajor(ones_addr + kk * 32), id_r, kk > 0);
-          tc_commit(&sm.t_full[bi]);
-          tc_commit(&sm.kv_empty[si]);
+            mma_f8_ts_if(tbase + kColT + (bi ^ 1) * 128, p_t + 8 * kk, desc_kmajor(ones_addr + kk * 32), id_r, kk > 0, leader);
+          tc_commit_if(&sm.t_full[bi], leader);
+          tc_commit_if(&sm.kv_empty[si], leader);
         }
       }
       // Every MMA issued must finish before TMEM is released.
-      tc_commit(&sm.drain);
+      tc_commit_if(&sm.drain, leader);
       const long long t0 = clock64();
       while (!mbar_try_wait(&sm.drain, 0) && clock64() - t0 < kWaitCycles) {
       }
@@ -461,9 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int i = 0; i < nb; ++i) {
       const int ring = i % kRing, tb = i & 1;
-      ok = mbar_wait(&sm.t_full[tb], (i >> 1) & 1, abort, status, 11) &&
-           mbar_wait(&sm.a_full[ring], (i / kRing) & 1, abort, status, 12) &&
-           mbar_wait(&sm.f_full[ring], (i / kRing) & 1, abort, status, 15);
+      ok = mbar_wait(&sm.t_full[tb], (i >> 1) & 1, abort, status, 11);
       if (!ok) break;
       tc_fence_after();
       const uint32_t tcol = kColT + tb * 128;
@@ -472,15 +470,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_16x256b_x1(lb1 + kColT + (tb ^ 1) * 128, r1);
       tmem_ld_16x256b_x4(lb0 + tcol, t0a);
       tmem_ld_16x256b_x4(lb1 + tcol, t0b);
-      const float4 al4 = *reinterpret_cast<const float4*>(&sm.alpha[ring][wq * 32 + 4 * rl]);
       tmem_ld_wait();
       reg_fence4(r0);
       reg_fence4(r1);
       reg_fence16(t0a);
       reg_fence16(t0b);
       tc_fence_before();
-      warp_arrive(&sm.tr_free[tb ^ 1], lane); // T_{i-1} done and R_i read: PV_{i+1} may write that buffer
-      warp_arrive(&sm.q0_free, lane);        // first quarter of T_i read: R_{i+1} may land there
+      warp_arrive(&sm.t_rel, lane);   // PV_{i+1} may write T_{(i+1)&1}, R_{i+1} the first quarter of T_i
+      ok = mbar_wait2(&sm.a_full[ring], (i / kRing) & 1, &sm.f_full[ring], (i / kRing) & 1, abort, status, 12);
+      if (!ok) break;
+      const float4 al4 = *reinterpret_cast<const float4*>(&sm.alpha[ring][wq * 32 + 4 * rl]);
       warp_arrive(&sm.a_free[ring], lane);
       const float al[4] = {al4.x, al4.y, al4.z, al4.w};
       const bool rescale =

@@ -75,6 +75,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait on two barriers at once: both probes are in flight together,
+// so an already-complete pair costs one shared-memory round trip.
+__device__ __forceinline__ bool mbar_wait2(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb, volatile int* abort,
+                                           DevStatus* status, int where) {
+  bool da = mbar_try_wait(a, pa);
+  bool db = mbar_try_wait(b, pb);
+  if (da && db) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (!da) da = mbar_try_wait(a, pa);
+    if (!db) db = mbar_try_wait(b, pb);
+    if (da && db) return true;
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort = 1;
+      if (status != nullptr && atomicCAS(&status->code, 0, 1) == 0) {
+        status->where = where;
+        status->block = blockIdx.x + gridDim.x * blockIdx.y;
+      }
+      return false;
+    }
+  }
+}
+
 // ------------------------------------------------------------------- TMA --
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -282,6 +306,46 @@ __device__ __forceinline__ void mma_f8_ts(uint32_t tmem_d, uint32_t tmem_a, uint
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Warp-wide issue: every lane runs the issuing loop (so addresses and
+// descriptors stay warp-uniform) and only the lane elected here issues.
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(pred));
+  return pred;
+}
+__device__ __forceinline__ void tc_commit_if(uint64_t* bar, uint32_t leader) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %1, 0;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(smem_u32(bar)),
+      "r"(leader)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f8_if(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate, uint32_t leader) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.ne.b32 e, %5, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(leader)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f8_ts_if(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate, uint32_t leader) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.ne.b32 e, %5, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(leader)
       : "memory");
 }
 

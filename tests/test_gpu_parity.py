@@ -263,7 +263,8 @@ def test_attention_config0(dev, expcast, kernel):
 
 
 @pytest.mark.parametrize("n,br,d,h", [(200, 128, 128, 2), (1000, 64, 128, 2), (700, 128, 64, 3),
-                                      (64, 64, 128, 1), (2048, 128, 128, 2)])
+                                      (64, 64, 128, 1), (2048, 128, 128, 2), (300, 128, 128, 2),
+                                      (600, 128, 128, 1)])
 @pytest.mark.parametrize("kernel", ["tc", "mma"])
 def test_attention_shapes(dev, n, br, d, h, kernel):
     """Ragged N, head_dim 64, single tile.  For N not a multiple of the block,
