@@ -398,7 +398,7 @@ def main() -> int:
     from comfyui_vc_attention_b200.vc_attention import _native as N
     from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
     from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
-                                                                          prepare, vc_attention_cuda)
+                                                                          prepare, vc_attention_cuda, sparse_tc_applies)
     N.lib()
 
     q, k, v = make_inputs_gpu(w, 1234 + rank, dev)
@@ -419,13 +419,17 @@ def main() -> int:
                        tau=w.get("tau", 1.3), qk_fp4=w.get("qk_fp4", False))
     scale = D ** -0.5
     out = torch.empty_like(q)
+    # tcgen05 kernels read V in their key order; the register-MMA sparse
+    # kernel (other shapes) reads the block-transposed copy.
+    sparse_tc = cfg.sparse and sparse_tc_applies(D, w["block_rows"], cfg.block_m, cfg.group, NT)
+    want_v = (not cfg.sparse) or sparse_tc
 
     def step(evs=None):
         if evs is not None:
             evs[0].record()
         p = prepare(q, k, v, perm, block_rows=w["block_rows"], hadamard=True, smooth_k=True,
                     sparse=cfg.sparse, tau=cfg.tau, q_block=cfg.block_m, scale=scale,
-                    want_v=not cfg.sparse, want_v_t=cfg.sparse, local_blocks=cfg.local_blocks,
+                    want_v=want_v, want_v_t=not want_v, local_blocks=cfg.local_blocks,
                     sink_blocks=cfg.sink_blocks, qk_fp4=cfg.qk_fp4, v_mma_order=not cfg.qk_fp4)
         if evs is not None:
             evs[1].record()
@@ -548,7 +552,8 @@ def main() -> int:
         "ms_prepare": prep_ms, "ms_attention": attn_ms, "kmeans_ms": kmeans_ms, "psnr_db": psnr,
         "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": fp8_peak, "unit": "TFLOP/s",
                      "frac": attn_tflops / fp8_peak, "traffic": traffic,
-                     "kernel": ("attn_sparse_kernel (mma.sync, tau-routed)" if w["sparse"]
+                     "kernel": ("attn_tc_sparse_kernel (tcgen05, tau-routed)" if sparse_tc
+                                else "attn_sparse_kernel (mma.sync, tau-routed)" if w["sparse"]
                                 else "attn_tc_kernel<NVFP4 QK> (tcgen05 mxf4nvf4 + f8f6f4)" if w.get("qk_fp4")
                                 else "attn_tc_kernel (tcgen05)"),
                      "flops": ("executed (kept tiles + proxy)" if w["sparse"] else "dense"),

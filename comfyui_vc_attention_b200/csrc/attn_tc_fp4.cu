@@ -30,6 +30,7 @@
 
 #include "kernels.cuh"
 #include "tc_common.cuh"
+#include "tc_math.cuh"
 
 namespace vcattn {
 
@@ -51,13 +52,6 @@ constexpr uint32_t kColS = 0, kColT = 256, kColR = 384, kColSFA = 400, kColSFB =
 // groups' float4 reads fall in different banks.
 constexpr int kCmStride = 36;
 __host__ __device__ constexpr int cm_index(int c) { return ((c & 7) >> 1) * kCmStride + (c >> 3) * 2 + (c & 1); }
-
-// One arrival per warp: the lanes' earlier shared-memory and tensor-memory
-// work is ordered before lane 0's (release) arrive by __syncwarp.
-__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
-  __syncwarp();
-  if (lane == 0) mbar_arrive(bar);
-}
 
 template <int BR>
 struct TcSmem {
@@ -101,53 +95,6 @@ struct TcArgs {
   void* out;
   int64_t osb, osh, osn;
 };
-
-// ---- packed fp32 helpers ---------------------------------------------------
-__device__ __forceinline__ void mul2(float& a, float& b, float x, float y) {
-  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
-      "mov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
-      "mul.rn.f32x2 rc, ra, rb;\n\tmov.b64 {%0, %1}, rc;\n\t}\n"
-      : "+f"(a), "+f"(b)
-      : "f"(x), "f"(y));
-}
-// (a, b) = (x0, x1) * (y0, y1) + (a, b)
-__device__ __forceinline__ void fma2(float& a, float& b, float x0, float x1, float y0, float y1) {
-  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%0, %1};\n\t"
-      "fma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}\n"
-      : "+f"(a), "+f"(b)
-      : "f"(x0), "f"(x1), "f"(y0), "f"(y1));
-}
-__device__ __forceinline__ void add2(float& a, float& b, float x, float y) {
-  asm("{\n\t.reg .b64 ra, rb;\n\t"
-      "mov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
-      "add.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}\n"
-      : "+f"(a), "+f"(b)
-      : "f"(x), "f"(y));
-}
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-__device__ __forceinline__ float fma_sat(float a, float b, float c) {
-  float d;
-  asm("fma.rn.sat.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// Two adjacent output values of one row, converted and written to the
-// staging tile (row stride RS bytes).
-template <int ODT>
-__device__ __forceinline__ void stage2(uint8_t* base, float v0, float v1) {
-  if constexpr (ODT == VCATTN_DTYPE_BF16) {
-    *reinterpret_cast<__nv_bfloat162*>(base) = __floats2bfloat162_rn(v0, v1);
-  } else if constexpr (ODT == VCATTN_DTYPE_F16) {
-    *reinterpret_cast<__half2*>(base) = __floats2half2_rn(v0, v1);
-  } else {
-    *reinterpret_cast<float2*>(base) = make_float2(v0, v1);
-  }
-}
 
 template <int BR, bool EXPCAST, int ODT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -239,7 +186,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop; the elected lane issues.
+    {
+      const uint32_t leader = elect_one();
       const uint32_t id_qk = idesc_nvfp4(kBM, BR);
       const uint32_t id_pv = idesc_e4m3(kBM, kD, true);
       const uint32_t id_r = idesc_e4m3(kBM, 16, false);
@@ -248,7 +197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(&sm.q_full, 0, abort, status, 2);
       if (ok) {
         tc_fence_after();
-        for (int at = 0; at < 2; ++at) tmem_cp_sf(tbase + kColSFA + 4 * at, desc_sf(smem_u32(sm.sfa + 512 * at)));
+        for (int at = 0; at < 2; ++at)
+          tmem_cp_sf_if(tbase + kColSFA + 4 * at, desc_sf(smem_u32(sm.sfa + 512 * at)), leader);
       }
       for (int j = 0; ok && j <= nb; ++j) {
         if (j < nb) {
@@ -262,33 +212,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           // K scale atoms of tile j into SFB_b; SFB_b was last read by QK_{j-2},
           // complete before PV_{j-2} was issued (p_full(j-2) follows s_full(j-2)).
           const uint32_t sfb = tbase + kColSFB + 8 * b;
-          for (int at = 0; at < 2; ++at) tmem_cp_sf(sfb + 4 * at, desc_sf(smem_u32(sm.sfb[s] + 512 * at)));
+          for (int at = 0; at < 2; ++at) tmem_cp_sf_if(sfb + 4 * at, desc_sf(smem_u32(sm.sfb[s] + 512 * at)), leader);
 #pragma unroll
           for (int kk = 0; kk < 2; ++kk)
-            mma_nvfp4(tbase + kColS + b * 128, desc_kmajor64(q_addr + kk * 32), desc_kmajor64(k_addr + kk * 32),
-                      id_qk, tbase + kColSFA + 4 * kk, sfb + 4 * kk, kk > 0);
-          tc_commit(&sm.s_full[b]);
+            mma_nvfp4_if(tbase + kColS + b * 128, desc_kmajor64(q_addr + kk * 32), desc_kmajor64(k_addr + kk * 32),
+                         id_qk, tbase + kColSFA + 4 * kk, sfb + 4 * kk, kk > 0, leader);
+          tc_commit_if(&sm.s_full[b], leader);
         }
         if (j >= 1) {
           const int i = j - 1, bi = i & 1, si = i % kStages;
-          ok = mbar_wait(&sm.p_full[bi], (i >> 1) & 1, abort, status, 5);
-          if (ok && i >= 1) ok = mbar_wait(&sm.t_free, (i - 1) & 1, abort, status, 6);
+          ok = i >= 1 ? mbar_wait2(&sm.p_full[bi], (i >> 1) & 1, &sm.t_free, (i - 1) & 1, abort, status, 5)
+                      : mbar_wait(&sm.p_full[bi], (i >> 1) & 1, abort, status, 5);
           if (!ok) break;
           tc_fence_after();
           const uint32_t v_addr = smem_u32(sm.v[si]);
           const uint32_t p_t = tbase + kColS + bi * 128;   // keys [32kk, 32kk+32) at columns 8kk..8kk+7
 #pragma unroll
           for (int kk = 0; kk < BR / 32; ++kk)
-            mma_f8_ts(tbase + kColT, p_t + 8 * kk, desc_mnmajor(v_addr + kk * 32 * 128), id_pv, kk > 0);
+            mma_f8_ts_if(tbase + kColT, p_t + 8 * kk, desc_mnmajor(v_addr + kk * 32 * 128), id_pv, kk > 0, leader);
 #pragma unroll
           for (int kk = 0; kk < BR / 32; ++kk)
-            mma_f8_ts(tbase + kColR, p_t + 8 * kk, desc_kmajor(ones_addr + kk * 32), id_r, kk > 0);
-          tc_commit(&sm.t_full);
-          tc_commit(&sm.kv_empty[si]);
+            mma_f8_ts_if(tbase + kColR, p_t + 8 * kk, desc_kmajor(ones_addr + kk * 32), id_r, kk > 0, leader);
+          tc_commit_if(&sm.t_full, leader);
+          tc_commit_if(&sm.kv_empty[si], leader);
         }
       }
       // Every MMA issued must finish before TMEM is released.
-      tc_commit(&sm.drain);
+      tc_commit_if(&sm.drain, leader);
       const long long t0 = clock64();
       while (!mbar_try_wait(&sm.drain, 0) && clock64() - t0 < kWaitCycles) {
       }

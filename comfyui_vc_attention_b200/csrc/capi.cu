@@ -319,6 +319,13 @@ int vcattn_attn_status(int* code, int* where, int* block, int reset) {
     *where = 100 + w2;   // waits of the NVFP4 kernel are reported as 100 + site
     *block = b2;
   }
+  int c3 = 0, w3 = 0, b3 = 0;
+  if (e == cudaSuccess) e = attn_sparse_tc_status(&c3, &w3, &b3, reset != 0);
+  if (e == cudaSuccess && *code == 0 && c3 != 0) {
+    *code = c3;
+    *where = 200 + w3;   // and those of the tcgen05 sparse kernel as 200 + site
+    *block = b3;
+  }
   return cuda_status(e, "vcattn_attn_status");
 }
 
@@ -373,6 +380,37 @@ int vcattn_attn_fp8_sparse(const uint8_t* q8, const float* q_scale, const uint8_
   p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
   p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
   return cuda_status(launch_attn_sparse_mma(p, static_cast<cudaStream_t>(stream)), "vcattn_attn_fp8_sparse");
+}
+
+int vcattn_attn_fp8_sparse_tc(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
+                              const uint8_t* v8, const float* v_scale, const float* mu, const float* k_mean,
+                              const float* v_mean, const uint8_t* keep, int q_block, int group, int B, int H,
+                              int N, int n_pad, int D, int block_rows, float sm_scale, int flags,
+                              double expcast_beta, void* out, int out_dtype, int64_t out_sb, int64_t out_sh,
+                              int64_t out_sn, void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_attn_fp8_sparse_tc"))
+    return fail(VCATTN_ERR_INJECTED, "vcattn_attn_fp8_sparse_tc: injected fault");
+  const int rc = attn_common_checks("vcattn_attn_fp8_sparse_tc", q8, q_scale, k8, k_scale, v8, v_scale, mu, B, H, N,
+                                    n_pad, D, block_rows, out, out_dtype);
+  if (rc != VCATTN_OK) return rc;
+  VC_CHECK(k_mean && v_mean && keep, "vcattn_attn_fp8_sparse_tc: missing routing inputs");
+  VC_CHECK(aligned16(k_mean) && aligned16(v_mean), "vcattn_attn_fp8_sparse_tc: k_mean / v_mean must be 16-byte aligned");
+  VC_CHECK(aligned16(out) && (out_sn % 8) == 0 && (out_sh % 8) == 0 && (out_sb % 8) == 0,
+           "vcattn_attn_fp8_sparse_tc: out must be 16-byte aligned with 8-element multiple strides");
+  AttnParams p{};
+  p.q8 = q8; p.k8 = k8; p.v8 = v8; p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
+  p.k_mean = k_mean; p.v_mean = v_mean; p.keep = keep; p.q_block = q_block; p.group = group;
+  p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
+  p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
+  p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
+  VC_CHECK(attn_sparse_tc_supported(p),
+           "vcattn_attn_fp8_sparse_tc: needs D = 128, block_rows = 128, q_block = 64, group = 16 and N <= 131072");
+  const cudaError_t e = launch_attn_sparse_tc(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(VCATTN_ERR_CUDA,
+                std::string("vcattn_attn_fp8_sparse_tc: ") + cudaGetErrorString(e) + " [" + attn_sparse_tc_diag() + "]");
+  return VCATTN_OK;
 }
 
 int vcattn_e4m3_encode(const float* x, int64_t n, uint8_t* out, void* stream) {

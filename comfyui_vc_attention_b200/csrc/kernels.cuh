@@ -84,6 +84,10 @@ const char* attn_nvfp4_diag();
 cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset);
 const char* attn_tc_diag();
 cudaError_t launch_attn_sparse_mma(const AttnParams& p, cudaStream_t st);
+bool attn_sparse_tc_supported(const AttnParams& p);
+cudaError_t launch_attn_sparse_tc(const AttnParams& p, cudaStream_t st);
+cudaError_t attn_sparse_tc_status(int* code, int* where, int* block, bool reset);
+const char* attn_sparse_tc_diag();
 cudaError_t launch_codecs_e4m3(const float* x, int64_t n, uint8_t* out, cudaStream_t st);
 cudaError_t launch_codecs_fp4(const float* x, int64_t n, uint8_t* out, cudaStream_t st);
 cudaError_t launch_expcast(const float* s, const float* m, int rows, int cols, double beta, int mode,

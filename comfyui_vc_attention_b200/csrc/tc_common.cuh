@@ -419,6 +419,26 @@ __device__ __forceinline__ void mma_nvfp4(uint32_t tmem_d, uint64_t adesc, uint6
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_cp_sf_if(uint32_t taddr, uint64_t sdesc, uint32_t leader) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %2, 0;\n\t"
+      "@e tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n\t}\n" ::"r"(taddr),
+      "l"(sdesc), "r"(leader)
+      : "memory");
+}
+__device__ __forceinline__ void mma_nvfp4_if(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t sfa, uint32_t sfb, uint32_t accumulate, uint32_t leader) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.ne.b32 e, %7, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb), "r"(leader)
+      : "memory");
+}
+
 // Instruction descriptor, kind::f8f6f4 with E4M3 operands and f32 accumulate.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N, bool b_mn_major) {
   return (1u << 4)                                   // D format f32

@@ -100,6 +100,11 @@ _SIGNATURES = {
                                        c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int,
                                        c_double, c_void_p, c_int, c_int64, c_int64, c_int64,
                                        c_void_p]),
+    "vcattn_attn_fp8_sparse_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                          c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int,
+                                          c_double, c_void_p, c_int, c_int64, c_int64, c_int64,
+                                          c_void_p]),
     "vcattn_e4m3_encode": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
     "vcattn_fp4_encode": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
     "vcattn_expcast_codes": (c_int, [c_void_p, c_void_p, c_int, c_int, c_double, c_int, c_void_p,

@@ -295,7 +295,7 @@ def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     fp4 = bool(cfg.qk_fp4)
     if fp4 and (d != 128 or br != 128):
         raise ValueError("the NVFP4 QK kernel needs D = 128 and block_n = 128")
-    use_tc = d == 128 and not sparse
+    use_tc = d == 128 and (not sparse or sparse_tc_applies(d, br, cfg.block_m, cfg.group, n))
     p = prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
                 tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=use_tc, want_v_t=not use_tc,
                 local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks, v_mma_order=not fp4,
@@ -309,8 +309,8 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
     """Run the attention kernel on prepared operands, writing into ``out``.
 
     kernel: "tc" (tcgen05, D = 128, needs ``p.v``), "mma" (register MMA,
-    needs ``p.v_t``) or "auto" (tcgen05 whenever it applies).  The sparse
-    path always runs on the register-MMA kernel.
+    needs ``p.v_t``) or "auto" (tcgen05 whenever it applies), for the dense
+    and the sparse path alike.
     """
     lib = N.lib()
     b, h, n_pad, d = p.q.shape
@@ -329,6 +329,20 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
             out.stride(0), out.stride(1), out.stride(2), st))
         return out
     if cfg.sparse:
+        if kernel == "auto":
+            kernel = "tc" if (p.v is not None and p.v_mma_order and
+                              sparse_tc_applies(d, p.block_rows, cfg.block_m, cfg.group, n_pad)) else "mma"
+        if kernel == "tc":
+            if p.v is None or not p.v_mma_order:
+                raise ValueError("the tcgen05 sparse kernel reads V codes in its key order "
+                                 "(want_v=True, v_mma_order=True)")
+            N.check("vcattn_attn_fp8_sparse_tc", lib.vcattn_attn_fp8_sparse_tc(
+                q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
+                p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), p.k_mean.data_ptr(),
+                p.v_mean.data_ptr(), p.keep.data_ptr(), cfg.block_m, cfg.group, b, h, n, n_pad, d,
+                p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
+                out.stride(0), out.stride(1), out.stride(2), st))
+            return out
         if p.v_t is None:
             raise ValueError("the sparse kernel needs the block-transposed V codes (want_v_t=True)")
         N.check("vcattn_attn_fp8_sparse", lib.vcattn_attn_fp8_sparse(
@@ -357,6 +371,13 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
             p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
             out.stride(0), out.stride(1), out.stride(2), st))
     return out
+
+
+def sparse_tc_applies(d: int, block_rows: int, q_block: int, group: int, n: int) -> bool:
+    """Whether the tcgen05 sparse kernel takes this shape (two 64-row routing
+    blocks per CTA, 128-key tiles, groups of 16, at most 1024 KV tiles)."""
+    nb = -(-n // block_rows)
+    return d == 128 and block_rows == 128 and q_block == 64 and group == 16 and nb + -(-nb // 16) <= 1088
 
 
 def attention_status(reset: bool = True):

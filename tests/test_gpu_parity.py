@@ -371,24 +371,29 @@ def test_route_mask_bit_exact(dev, tau, local, sink):
     assert 0.0 < keep.mean() < 1.0, "routing must be non-trivial on the spatial inputs"
 
 
-def _sparse_gpu(q, k, v, perm, dev, tau, local=1, sink=0, expcast=False, out_dtype=torch.float32):
-    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import TritonConfig, attention_prepared
+def _sparse_gpu(q, k, v, perm, dev, tau, local=1, sink=0, expcast=False, out_dtype=torch.float32, kernel="mma"):
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
+                                                                           attention_status)
     b, h, n, d = q.shape
-    p = _prep_gpu(q, k, v, perm, 128, dev, sparse=True, tau=tau, q_block=64, want_v_t=True,
+    tc = kernel == "tc"
+    p = _prep_gpu(q, k, v, perm, 128, dev, sparse=True, tau=tau, q_block=64, want_v_t=not tc, want_v=tc,
                   local_blocks=local, sink_blocks=sink)
     out = torch.empty((b, h, n, d), dtype=out_dtype, device=dev)
     cfg = TritonConfig(block_m=64, block_n=128, sparse=True, tau=tau, local_blocks=local, sink_blocks=sink,
                        enable_expcast=expcast)
-    attention_prepared(p, n, out, d ** -0.5, cfg)
+    attention_prepared(p, n, out, d ** -0.5, cfg, kernel=kernel)
     torch.cuda.synchronize()
+    if tc:
+        assert attention_status() == (0, 0, 0), "a bounded wait of the tcgen05 sparse kernel expired"
     return out.float().cpu().numpy().reshape(b * h, n, d), p
 
 
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
 @pytest.mark.parametrize("expcast", [False, True])
-def test_sparse_attention_matches_oracle(dev, expcast):
+def test_sparse_attention_matches_oracle(dev, expcast, kernel):
     n, h = 1024, 2
     q, k, v, perm = _sparse_case(n, h)
-    got, p = _sparse_gpu(q, k, v, perm, dev, tau=1.3, expcast=expcast)
+    got, p = _sparse_gpu(q, k, v, perm, dev, tau=1.3, expcast=expcast, kernel=kernel)
     qg, kg, vg = (a.reshape(h, n, 128) for a in (q, k, v))
     prep = O.prepare(qg, kg, vg, perm, block_rows=128)
     st = O.route_stats(prep, 128, 64, 1.3, 128 ** -0.5)
@@ -399,23 +404,25 @@ def test_sparse_attention_matches_oracle(dev, expcast):
     assert O.psnr(got, sd) > 20.0
 
 
-def test_sparse_keep_all_equals_dense(dev):
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
+def test_sparse_keep_all_equals_dense(dev, kernel):
     """tau -> -inf keeps every block: the sparse kernel must reproduce the
-    dense register-MMA kernel bit for bit (exact tiles, same order)."""
+    dense kernel of the same family bit for bit (exact tiles, same order)."""
     n, h = 1024, 2
     q, k, v, perm = _sparse_case(n, h)
-    sparse, p = _sparse_gpu(q, k, v, perm, dev, tau=-1000.0)
+    sparse, p = _sparse_gpu(q, k, v, perm, dev, tau=-1000.0, kernel=kernel)
     assert p.keep.bool().all()
-    dense = _attn_gpu(q, k, v, perm, 128, dev, kernel="mma")
+    dense = _attn_gpu(q, k, v, perm, 128, dev, kernel=kernel)
     assert np.array_equal(sparse, dense)
 
 
-def test_sparse_ragged_and_multi_group(dev):
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
+def test_sparse_ragged_and_multi_group(dev, kernel):
     """N not a multiple of the block, more than one 16-block group."""
     n, h = 2500, 2
     q, k, v = make_qkv(1, h, n, 128, seed=12)
     perm = np.stack([np.random.default_rng(i).permutation(n) for i in range(h)]).astype(np.int32)
-    got, p = _sparse_gpu(q, k, v, perm, dev, tau=0.8, local=0)
+    got, p = _sparse_gpu(q, k, v, perm, dev, tau=0.8, local=0, kernel=kernel)
     qg, kg, vg = (a.reshape(h, n, 128) for a in (q, k, v))
     prep = O.prepare(qg, kg, vg, perm, block_rows=128)
     st = O.route_stats(prep, 128, 64, 0.8, 128 ** -0.5)
