@@ -519,11 +519,17 @@ def main() -> int:
     peaks, peak_kind = measured_peaks()
     fp8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
     keep_frac = None
+    sparse_stats = None
     if w["sparse"]:
         pk = step()
         torch.cuda.synchronize()
         keep_frac = float(pk.keep.float().mean())
-        del pk
+        kp = pk.keep.view(G, -1, 2, pk.keep.shape[-1]).bool()
+        union = kp[:, :, 0] | kp[:, :, 1]           # tiles run by the tcgen05 CTA of two query blocks
+        appx = (~kp).view(G, kp.shape[1], 2, -1, 16).any(-1).any(2)   # groups with a proxy fold
+        sparse_stats = {"union_fraction": float(union.float().mean()),
+                        "proxy_groups_per_cta": float(appx.float().sum(-1).mean())}
+        del pk, kp, union, appx
     # executed work of the attention kernel: dense tiles, or the kept tiles
     # plus the block-mean proxy of the skipped ones (2*N*NB*D per head each way)
     fl_exec = fl if keep_frac is None else (keep_frac * fl + 4.0 * G * NT * (NT // w["block_rows"]) * D)
@@ -548,7 +554,8 @@ def main() -> int:
                    "parallelism": f"(batch, head) units x{world} ranks, independent, no collective",
                    "l2": "inputs larger than L2 (Q/K/V 235 MB each)",
                    "keep_fraction": keep_frac,
-                   "block_skip_ratio": None if keep_frac is None else 1.0 - keep_frac},
+                   "block_skip_ratio": None if keep_frac is None else 1.0 - keep_frac,
+                   "sparse_cta_work": sparse_stats},
         "ms_prepare": prep_ms, "ms_attention": attn_ms, "kmeans_ms": kmeans_ms, "psnr_db": psnr,
         "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": fp8_peak, "unit": "TFLOP/s",
                      "frac": attn_tflops / fp8_peak, "traffic": traffic,

@@ -357,68 +357,94 @@ __global__ void __launch_bounds__(256) quant_v_kernel(VArgs a) {
 
 // ---------------------------------------------------------------------------
 // Routing threshold + keep mask (triton_attn.py:449-459 and :716-735).
-// One CTA per (head, routing query block); thread j handles KV block j.
+// One CTA per (head, routing query block).  Warp w takes KV blocks w, w+8, ..;
+// its lanes read one k_mean row (coalesced) and form both float64 dots of
+// that row: the threshold proxy fp32(q_cent . k_mean_j) * scale and the
+// routing score fp32(q_bar . bf16(k_mean_j)) / q_block.  Each dot is summed
+// in float64 and rounded once, so its fp32 value does not depend on the
+// order of the partial sums.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Sum of one double per thread over the CTA (blockDim.x = 256); every thread
+// gets the total.
+__device__ __forceinline__ double block_sum_f64(double v, double* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  v = warp_sum_f64(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = lane < (blockDim.x >> 5) ? red[lane] : 0.0;
+  return warp_sum_f64(t);
+}
+
 template <int D>
-__global__ void route_mask_kernel(const float* __restrict__ k_mean, const float* __restrict__ q_cent,
-                                  const float* __restrict__ q_bar, int nqb, int nb, int q_block,
-                                  int br, float tau, int local_blocks, int sink_blocks,
-                                  float sm_scale, uint8_t* __restrict__ keep,
-                                  float* __restrict__ thresh_out) {
-  extern __shared__ float rsm[];           // proxy[nb]
-  __shared__ float qc[D], qb[D];
-  __shared__ double red[256];
+__global__ void __launch_bounds__(256) route_mask_kernel(const float* __restrict__ k_mean,
+                                                         const float* __restrict__ q_cent,
+                                                         const float* __restrict__ q_bar, int nqb, int nb, int q_block,
+                                                         int br, float tau, int local_blocks, int sink_blocks,
+                                                         float sm_scale, uint8_t* __restrict__ keep,
+                                                         float* __restrict__ thresh_out) {
+  constexpr int E = D / 32;                 // channels per lane
+  extern __shared__ float rsm[];            // proxy[nb], score[nb]
+  __shared__ double red[8];
+  float* proxy = rsm;
+  float* score = rsm + nb;
   const int g = blockIdx.y, i = blockIdx.x;
-  const int tid = threadIdx.x;
-  if (tid < D) {
-    qc[tid] = q_cent[(static_cast<int64_t>(g) * nqb + i) * D + tid];
-    qb[tid] = q_bar[(static_cast<int64_t>(g) * nqb + i) * D + tid];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float qc[E], qb[E];
+  {
+    const float* qcr = q_cent + (static_cast<int64_t>(g) * nqb + i) * D + E * lane;
+    const float* qbr = q_bar + (static_cast<int64_t>(g) * nqb + i) * D + E * lane;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      qc[e] = qcr[e];
+      qb[e] = qbr[e];
+    }
+  }
+  const float inv_q = static_cast<float>(q_block);
+  for (int j = warp; j < nb; j += 8) {
+    const float* km = k_mean + (static_cast<int64_t>(g) * nb + j) * D + E * lane;
+    float kv[E];
+    if constexpr (E == 4) {
+      const float4 t = *reinterpret_cast<const float4*>(km);
+      kv[0] = t.x; kv[1] = t.y; kv[2] = t.z; kv[3] = t.w;
+    } else {
+      const float2 t = *reinterpret_cast<const float2*>(km);
+      kv[0] = t.x; kv[1] = t.y;
+    }
+    double d1 = 0.0, d2 = 0.0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      d1 = fma(static_cast<double>(qc[e]), static_cast<double>(kv[e]), d1);
+      d2 = fma(static_cast<double>(qb[e]), static_cast<double>(bf16_round(kv[e])), d2);
+    }
+    d1 = warp_sum_f64(d1);
+    d2 = warp_sum_f64(d2);
+    if (lane == 0) {
+      proxy[j] = __fmul_rn(__double2float_rn(d1), sm_scale);
+      score[j] = __fdiv_rn(__double2float_rn(d2), inv_q);
+    }
   }
   __syncthreads();
-  // proxy_h[j] = fp32(q_cent . k_mean_j) * scale ; mean over j
   double part = 0.0;
-  for (int j = tid; j < nb; j += blockDim.x) {
-    const float* km = k_mean + (static_cast<int64_t>(g) * nb + j) * D;
-    double dot = 0.0;
-    for (int d = 0; d < D; ++d) dot += static_cast<double>(qc[d]) * static_cast<double>(km[d]);
-    const float p = __fmul_rn(__double2float_rn(dot), sm_scale);
-    rsm[j] = p;
-    part += static_cast<double>(p);
-  }
-  red[tid] = part;
-  __syncthreads();
-  if (tid == 0) {
-    double tot = 0.0;
-    for (int t = 0; t < blockDim.x; ++t) tot += red[t];
-    red[0] = tot;
-  }
-  __syncthreads();
-  const float mean = __fdiv_rn(__double2float_rn(red[0]), static_cast<float>(nb));
-  __syncthreads();
+  for (int j = tid; j < nb; j += blockDim.x) part += static_cast<double>(proxy[j]);
+  const float mean = __fdiv_rn(__double2float_rn(block_sum_f64(part, red)), static_cast<float>(nb));
   part = 0.0;
   for (int j = tid; j < nb; j += blockDim.x) {
-    const float dv = __fsub_rn(rsm[j], mean);
+    const float dv = __fsub_rn(proxy[j], mean);
     part += static_cast<double>(__fmul_rn(dv, dv));
   }
-  red[tid] = part;
-  __syncthreads();
-  if (tid == 0) {
-    double tot = 0.0;
-    for (int t = 0; t < blockDim.x; ++t) tot += red[t];
-    red[0] = tot;
-  }
-  __syncthreads();
-  const float var = __fdiv_rn(__double2float_rn(red[0]), static_cast<float>(nb));
+  const float var = __fdiv_rn(__double2float_rn(block_sum_f64(part, red)), static_cast<float>(nb));
   const float thr = __fadd_rn(mean, __fmul_rn(tau, __fsqrt_rn(var)));
   if (tid == 0 && thresh_out) thresh_out[static_cast<int64_t>(g) * nqb + i] = thr;
-  // score_j = fp32(qbar . bf16(k_mean_j)) / q_block
   const int qb_kv = (i * q_block) / br;
   for (int j = tid; j < nb; j += blockDim.x) {
-    const float* km = k_mean + (static_cast<int64_t>(g) * nb + j) * D;
-    double dot = 0.0;
-    for (int d = 0; d < D; ++d) dot += static_cast<double>(qb[d]) * static_cast<double>(bf16_round(km[d]));
-    const float score = __fdiv_rn(__double2float_rn(dot), static_cast<float>(q_block));
-    const bool k = (score > thr) || (abs(qb_kv - j) <= local_blocks) || (j < sink_blocks);
+    const bool k = (score[j] > thr) || (abs(qb_kv - j) <= local_blocks) || (j < sink_blocks);
     keep[(static_cast<int64_t>(g) * nqb + i) * nb + j] = k ? 1 : 0;
   }
 }
@@ -648,7 +674,7 @@ cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t st) {
 cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st) {
   const int nqb = p.n_pad / p.q_block;
   const int nb = p.n_pad / p.block_rows;
-  const size_t smem = static_cast<size_t>(nb) * sizeof(float);
+  const size_t smem = 2 * static_cast<size_t>(nb) * sizeof(float);
   if (p.D == 128) {
     route_mask_kernel<128><<<dim3(nqb, p.G), 256, smem, st>>>(
         p.k_mean, p.q_cent, p.q_bar, nqb, nb, p.q_block, p.block_rows, p.tau, p.local_blocks,
