@@ -526,9 +526,13 @@ def main() -> int:
         keep_frac = float(pk.keep.float().mean())
         kp = pk.keep.view(G, -1, 2, pk.keep.shape[-1]).bool()
         union = kp[:, :, 0] | kp[:, :, 1]           # tiles run by the tcgen05 CTA of two query blocks
-        appx = (~kp).view(G, kp.shape[1], 2, -1, 16).any(-1).any(2)   # groups with a proxy fold
+        nbk = kp.shape[-1]
+        pad = (-nbk) % 16                            # blocks past the end are never approximated
+        kpp = torch.nn.functional.pad(kp.to(torch.uint8), (0, pad), value=1).bool()
+        appx = (~kpp).view(G, kp.shape[1], 2, -1, 16).any(-1).any(2)   # groups with a proxy fold
         sparse_stats = {"union_fraction": float(union.float().mean()),
                         "proxy_groups_per_cta": float(appx.float().sum(-1).mean())}
+        del kpp
         del pk, kp, union, appx
     # executed work of the attention kernel: dense tiles, or the kept tiles
     # plus the block-mean proxy of the skipped ones (2*N*NB*D per head each way)
