@@ -25,9 +25,10 @@
 //   PV slot:  T_b = P_ap @ V_mean(bf16)                   tcgen05.mma kind::f16,
 //             A from tensor memory, two N = 64 halves
 //   correction: acc = alpha acc + T_b ; l = alpha l + sum p_ap
-// The factor warps convert the group's k_mean / v_mean rows (fp32, staged
-// by the producer) to bf16 operand tiles, and Q to bf16 once per CTA.
-// Every wait is bounded.
+// The group's bf16 k_mean / v_mean operand tiles come prepared (route tiles
+// of prepare.cu, already in the swizzled layout) and are bulk-copied into the
+// step's K / V stage; the softmax warps convert Q to bf16 once per CTA when
+// the CTA has a proxy step.  Every wait is bounded.
 #include <cuda.h>
 #include <cuda_fp8.h>
 #include <cstdio>
@@ -82,11 +83,9 @@ __device__ __forceinline__ int step_ap_ord(const Step& s) { return static_cast<i
 
 struct SpSmem {
   alignas(1024) uint8_t q[kBM * 128];
-  alignas(1024) uint8_t k[kStages][kBR * 128];   // exact: K codes; approx: k_mean fp32 rows
-  alignas(1024) uint8_t v[kStages][kBR * 128];   // exact: V codes; approx: v_mean fp32 rows
+  alignas(1024) uint8_t k[kStages][kBR * 128];   // exact: K codes; proxy: bf16 k_mean tile (4 KB)
+  alignas(1024) uint8_t v[kStages][kBR * 128];   // exact: V codes; proxy: bf16 v_mean tile (4 KB)
   alignas(1024) uint8_t qb[2][kBM * 128];         // Q as bf16, two 64-element K atoms
-  alignas(1024) uint8_t kmb[2][2][kGroup * 128];  // [buffer][K atom] k_mean bf16, 16 rows
-  alignas(1024) uint8_t vmb[2][2][kGroup * 128];  // [buffer][N half] v_mean bf16, 16 K rows
   alignas(1024) uint8_t ones[16 * 128];
   alignas(16) float ks[kStages][kBR];
   alignas(16) float vs[kStages][kD];
@@ -97,6 +96,7 @@ struct SpSmem {
   alignas(16) float lsum[kRing][kBM];    // approximation steps: sum p_ap, same order
   Step steps[kMaxSteps];
   int nsteps;
+  int has_ap;
   alignas(8) uint64_t q_full;
   alignas(8) uint64_t qb_full;
   alignas(8) uint64_t kv_full[kStages];
@@ -105,7 +105,6 @@ struct SpSmem {
   alignas(8) uint64_t p_full[2];
   alignas(8) uint64_t t_full[2];
   alignas(8) uint64_t t_rel;
-  alignas(8) uint64_t ap_free[2];
   alignas(8) uint64_t a_full[kRing];
   alignas(8) uint64_t a_free[kRing];
   alignas(8) uint64_t f_full[kRing];
@@ -122,10 +121,9 @@ struct SpArgs {
   const float* k_scale;
   const float* v_scale;
   const float* mu;
-  const float* k_mean;
-  const float* v_mean;
+  const uint8_t* ap_tiles;
   const uint8_t* keep;
-  int H, N, n_pad, nb, nqb;
+  int H, N, n_pad, nb, nqb, ngroups;
   float sm_scale;
   float c120;
   void* out;
@@ -192,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     sm.abort = 0;
     mbar_init(&sm.q_full, 1);
-    mbar_init(&sm.qb_full, 2);
+    mbar_init(&sm.qb_full, 8);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1 + 2);
@@ -201,7 +199,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.s_full[b], 1);
       mbar_init(&sm.p_full[b], 8);
       mbar_init(&sm.t_full[b], 1);
-      mbar_init(&sm.ap_free[b], 1);
     }
     mbar_init(&sm.t_rel, 4);
     for (int r = 0; r < kRing; ++r) {
@@ -246,7 +243,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++n;
       }
     }
-    if (lane == 0) sm.nsteps = n;
+    if (lane == 0) {
+      sm.nsteps = n;
+      sm.has_ap = ap_ord > 0;
+    }
   }
   fence_proxy_async_smem();
   if (warp == 1) {
@@ -285,13 +285,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, status, 1)) break;
         const Step st = sm.steps[j];
         if (step_is_ap(st)) {
-          const int g0 = step_index(st) * kGroup;
-          const int cnt = min(kGroup, nb - g0);
-          const uint32_t bytes = static_cast<uint32_t>(cnt) * kD * 4u;
-          mbar_expect_tx(&sm.kv_full[s], 2u * bytes);
-          const int64_t mo = (static_cast<int64_t>(g) * nb + g0) * kD;
-          bulk_load(sm.k[s], a.k_mean + mo, bytes, &sm.kv_full[s]);
-          bulk_load(sm.v[s], a.v_mean + mo, bytes, &sm.kv_full[s]);
+          const uint8_t* tile = a.ap_tiles + (static_cast<int64_t>(g) * a.ngroups + step_index(st)) * 8192;
+          mbar_expect_tx(&sm.kv_full[s], 8192u);
+          bulk_load(sm.k[s], tile, 4096, &sm.kv_full[s]);
+          bulk_load(sm.v[s], tile + 4096, 4096, &sm.kv_full[s]);
         } else {
           const int blk = step_index(st);
           mbar_expect_tx(&sm.kv_full[s], tile_bytes);
@@ -330,17 +327,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool qb_ready = false;
       for (int j = 0; ok && j <= nst; ++j) {
         if (j < nst) {
-          const int s = j % kStages, b = j & 1, ring = j % kRing;
+          const int s = j % kStages, b = j & 1;
           const Step st = sm.steps[j];
           ok = mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 3);
           if (!ok) break;
           if (step_is_ap(st)) {
-            // k_mean tile converted by the factor warps; Q in bf16 once.
-            ok = mbar_wait(&sm.f_full[ring], (j / kRing) & 1, abort, status, 17);
-            if (ok && !qb_ready) ok = qb_ready = mbar_wait(&sm.qb_full, 0, abort, status, 18);
+            // bf16 k_mean tile in stage s; Q in bf16 once per CTA.
+            if (!qb_ready) ok = qb_ready = mbar_wait(&sm.qb_full, 0, abort, status, 18);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t kmb_addr = smem_u32(sm.kmb[step_ap_ord(st) & 1][0]);
+            const uint32_t kmb_addr = smem_u32(sm.k[s]);
 #pragma unroll
             for (int kk = 0; kk < kD / 16; ++kk)
               mma_bf16_if(tbase + kColS + b * 128, desc_kmajor(qb_addr + (kk >> 2) * (kBM * 128) + (kk & 3) * 32),
@@ -365,12 +361,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t p_t = tbase + kColS + bi * 128;
           if (step_is_ap(st)) {
-            const int x = step_ap_ord(st) & 1;
+            const uint32_t vmb_addr = smem_u32(sm.v[si]);
 #pragma unroll
             for (int h = 0; h < 2; ++h)
-              mma_bf16_ts_if(tbase + kColT + bi * 128 + 64 * h, p_t, desc_mnmajor(smem_u32(sm.vmb[x][h])), id_pva, 0,
+              mma_bf16_ts_if(tbase + kColT + bi * 128 + 64 * h, p_t, desc_mnmajor(vmb_addr + 2048 * h), id_pva, 0,
                              leader);
-            tc_commit_if(&sm.ap_free[x], leader);
           } else {
             const uint32_t v_addr = smem_u32(sm.v[si]);
 #pragma unroll
@@ -393,48 +388,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ factors and bf16 operand tiles
+    // ------------------------------------------------------------ per-tile factors
     const int c2 = tid - 64;   // 0..63
-    // Q codes -> bf16, K-major 128-byte swizzle, two K atoms of 64 elements.
-    if (mbar_wait(&sm.q_full, 0, abort, status, 19)) {
-      for (int e = c2; e < kBM * 64; e += 64) {   // pairs of elements
-        const int r = e >> 6, k = (e & 63) * 2;
-        const uint32_t two = *reinterpret_cast<const uint16_t*>(sm.q + sw128(r, k));
-        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-        const int atom = k >> 6, c = (k & 63) * 2;
-        *reinterpret_cast<uint32_t*>(sm.qb[atom] + sw128(r, c)) = pack_bf16x2(f.x, f.y);
-      }
-      fence_proxy_async_smem();
-      warp_arrive(&sm.qb_full, lane);
-    }
     for (int j = 0; j < nst; ++j) {
       const int s = j % kStages, ring = j % kRing;
       if (!mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 13)) break;
       if (j >= kRing && !mbar_wait(&sm.f_free[ring], ((j / kRing) + 1) & 1, abort, status, 14)) break;
       const Step st = sm.steps[j];
-      if (step_is_ap(st)) {
-        const int ord = step_ap_ord(st), x = ord & 1;
-        if (ord >= 2 && !mbar_wait(&sm.ap_free[x], ((ord - 2) >> 1) & 1, abort, status, 20)) break;
-        const int cnt = min(kGroup, nb - step_index(st) * kGroup);
-        const float* kmf = reinterpret_cast<const float*>(sm.k[s]);
-        const float* vmf = reinterpret_cast<const float*>(sm.v[s]);
-        // k_mean: B operand of the proxy MMA, 16 rows (blocks) x 128, K-major.
-        for (int e = c2; e < kGroup * 64; e += 64) {
-          const int n = e >> 6, k = (e & 63) * 2;
-          const float v0 = n < cnt ? kmf[n * kD + k] : 0.f, v1 = n < cnt ? kmf[n * kD + k + 1] : 0.f;
-          *reinterpret_cast<uint32_t*>(sm.kmb[x][k >> 6] + sw128(n, (k & 63) * 2)) = pack_bf16x2(v0, v1);
-        }
-        // v_mean: B operand of the approximation PV, K = 16 positions (rows,
-        // block ap_block_of_pos(k)) x N = 128 channels, MN-major, two halves.
-        for (int e = c2; e < kGroup * 64; e += 64) {
-          const int kpos = e >> 6, c = (e & 63) * 2;
-          const int n = ap_block_of_pos(kpos);
-          const float v0 = n < cnt ? vmf[n * kD + c] : 0.f, v1 = n < cnt ? vmf[n * kD + c + 1] : 0.f;
-          *reinterpret_cast<uint32_t*>(sm.vmb[x][c >> 6] + sw128(kpos, (c & 63) * 2)) = pack_bf16x2(v0, v1);
-        }
-        fence_proxy_async_smem();
-      } else {
+      if (!step_is_ap(st)) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int c = c2 + 64 * h;
@@ -464,8 +425,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float As_a = __fmul_rn(8.0f * kLog2e, qsm_a) * (1.0f / 128.0f);
     const float As_b = __fmul_rn(8.0f * kLog2e, qsm_b) * (1.0f / 128.0f);
     const float Ae_a = __fmul_rn(qsm_a, kLog2e), Ae_b = __fmul_rn(qsm_b, kLog2e);
+    bool run = true;
+    if (sm.has_ap) {
+      // Q codes -> bf16 operand of the proxy MMA (K-major, 128-byte swizzle,
+      // two 64-element atoms): each thread converts four 16-byte chunks.
+      run = mbar_wait(&sm.q_full, 0, abort, status, 19);
+      const int t = run ? tid - 128 : kBM * 8;
+      for (int ci = t; ci < kBM * 8; ci += 256) {
+        const int r = ci >> 3, c = ci & 7;
+        const uint4 raw = *reinterpret_cast<const uint4*>(sm.q + sw128(r, 16 * c));
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        uint32_t o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t two = (w[i >> 1] >> (16 * (i & 1))) & 0xffffu;
+          const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+          o[i] = pack_bf16x2(f.x, f.y);
+        }
+        uint8_t* dst = sm.qb[c >> 2];
+        const int cb = (c & 3) * 32;
+        *reinterpret_cast<uint4*>(dst + sw128(r, cb)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(dst + sw128(r, cb + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+      fence_proxy_async_smem();
+      if (run) warp_arrive(&sm.qb_full, lane);
+    }
     float m_a = -INFINITY, m_b = -INFINITY;
-    for (int j = 0; j < nst; ++j) {
+    for (int j = 0; run && j < nst; ++j) {
       const int b = j & 1, ring = j % kRing;
       if (!mbar_wait(&sm.s_full[b], (j >> 1) & 1, abort, status, 7)) break;
       if (!mbar_wait(&sm.f_full[ring], (j / kRing) & 1, abort, status, 8)) break;
@@ -799,8 +786,9 @@ cudaError_t launch_sp(const AttnParams& p, cudaStream_t st) {
     return cudaErrorInvalidValue;
   SpArgs a{};
   a.q_scale = p.q_scale; a.k_scale = p.k_scale; a.v_scale = p.v_scale; a.mu = p.mu;
-  a.k_mean = p.k_mean; a.v_mean = p.v_mean; a.keep = p.keep;
+  a.ap_tiles = p.ap_tiles; a.keep = p.keep;
   a.H = p.H; a.N = p.N; a.n_pad = p.n_pad; a.nb = p.n_pad / kBR; a.nqb = p.n_pad / kQBlock;
+  a.ngroups = (a.nb + kGroup - 1) / kGroup;
   a.sm_scale = p.sm_scale;
   a.c120 = static_cast<float>(64.0 + 56.0 + p.beta);
   a.out = p.out; a.osb = p.osb; a.osh = p.osh; a.osn = p.osn;

@@ -250,6 +250,17 @@ int vcattn_route_mask(const vcattn_route_stats* route, int G, int N, int n_pad, 
   return cuda_status(launch_route_mask(p, static_cast<cudaStream_t>(stream)), "vcattn_route_mask");
 }
 
+int vcattn_route_tiles(const float* k_mean, const float* v_mean, int G, int n_pad, int D, int block_rows,
+                       uint8_t* tiles, void* stream) {
+  g_last_error.clear();
+  VC_CHECK(k_mean && v_mean && tiles, "vcattn_route_tiles: null pointer");
+  VC_CHECK(D == 128 && block_rows == 128, "vcattn_route_tiles: needs D = 128 and block_rows = 128");
+  VC_CHECK(G > 0 && n_pad > 0 && n_pad % block_rows == 0, "vcattn_route_tiles: bad shape");
+  VC_CHECK(aligned16(tiles), "vcattn_route_tiles: tiles must be 16-byte aligned");
+  return cuda_status(launch_route_tiles(k_mean, v_mean, G, n_pad / block_rows, tiles, static_cast<cudaStream_t>(stream)),
+                     "vcattn_route_tiles");
+}
+
 static int attn_common_checks(const char* name, const uint8_t* q8, const float* q_scale, const uint8_t* k8,
                               const float* k_scale, const uint8_t* v8t, const float* v_scale, const float* mu,
                               int B, int H, int N, int n_pad, int D, int block_rows, void* out, int out_dtype) {
@@ -383,8 +394,8 @@ int vcattn_attn_fp8_sparse(const uint8_t* q8, const float* q_scale, const uint8_
 }
 
 int vcattn_attn_fp8_sparse_tc(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
-                              const uint8_t* v8, const float* v_scale, const float* mu, const float* k_mean,
-                              const float* v_mean, const uint8_t* keep, int q_block, int group, int B, int H,
+                              const uint8_t* v8, const float* v_scale, const float* mu, const uint8_t* ap_tiles,
+                              const uint8_t* keep, int q_block, int group, int B, int H,
                               int N, int n_pad, int D, int block_rows, float sm_scale, int flags,
                               double expcast_beta, void* out, int out_dtype, int64_t out_sb, int64_t out_sh,
                               int64_t out_sn, void* stream) {
@@ -394,13 +405,13 @@ int vcattn_attn_fp8_sparse_tc(const uint8_t* q8, const float* q_scale, const uin
   const int rc = attn_common_checks("vcattn_attn_fp8_sparse_tc", q8, q_scale, k8, k_scale, v8, v_scale, mu, B, H, N,
                                     n_pad, D, block_rows, out, out_dtype);
   if (rc != VCATTN_OK) return rc;
-  VC_CHECK(k_mean && v_mean && keep, "vcattn_attn_fp8_sparse_tc: missing routing inputs");
-  VC_CHECK(aligned16(k_mean) && aligned16(v_mean), "vcattn_attn_fp8_sparse_tc: k_mean / v_mean must be 16-byte aligned");
+  VC_CHECK(ap_tiles && keep, "vcattn_attn_fp8_sparse_tc: missing routing inputs");
+  VC_CHECK(aligned16(ap_tiles), "vcattn_attn_fp8_sparse_tc: ap_tiles must be 16-byte aligned");
   VC_CHECK(aligned16(out) && (out_sn % 8) == 0 && (out_sh % 8) == 0 && (out_sb % 8) == 0,
            "vcattn_attn_fp8_sparse_tc: out must be 16-byte aligned with 8-element multiple strides");
   AttnParams p{};
   p.q8 = q8; p.k8 = k8; p.v8 = v8; p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
-  p.k_mean = k_mean; p.v_mean = v_mean; p.keep = keep; p.q_block = q_block; p.group = group;
+  p.ap_tiles = ap_tiles; p.keep = keep; p.q_block = q_block; p.group = group;
   p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
   p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
   p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;

@@ -56,6 +56,7 @@ struct AttnParams {
   // block-sparse extras (nullptr for the dense kernel)
   const float *k_mean, *v_mean;
   const uint8_t* keep;
+  const uint8_t* ap_tiles;   // bf16 proxy tiles (vcattn_route_tiles) of the tcgen05 sparse kernel
   int q_block, group;
   // NVFP4 QK^T (nullptr for the FP8 kernels)
   const uint8_t *q4, *k4, *q4_sf, *k4_sf;
@@ -75,6 +76,8 @@ size_t kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys);
 cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t st);
 cudaError_t launch_prepare_nvfp4(const NvfpParams& p, cudaStream_t st);
 cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st);
+cudaError_t launch_route_tiles(const float* k_mean, const float* v_mean, int G, int nb, uint8_t* tiles,
+                               cudaStream_t st);
 cudaError_t launch_kmeans(const KMeansParams& p, cudaStream_t st);
 cudaError_t launch_attn_mma(const AttnParams& p, cudaStream_t st);
 cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t st);

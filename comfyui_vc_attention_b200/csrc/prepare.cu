@@ -671,6 +671,55 @@ cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t st) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// bf16 operand tiles of the proxy fold of the tcgen05 sparse kernel, one
+// 8 KB tile per (head, group of 16 KV blocks), laid out so that a linear
+// copy into 1024-byte aligned shared memory gives the 128-byte swizzle:
+//   [0, 4096)    bf16(k_mean) K-major: atom a (channels 64a..64a+63) at 2048 a,
+//                row n = block g0+n, byte c at sw128(n, c)
+//   [4096, 8192) bf16(v_mean) MN-major: half h (channels 64h..) at 4096 + 2048 h,
+//                row k = block g0 + route_tile_block(k), byte c at sw128(k, c)
+// Blocks past the last one are zero.
+// ---------------------------------------------------------------------------
+__host__ __device__ constexpr int route_tile_block(int k) {
+  return ((k & 3) < 2) ? 2 * (k >> 2) + (k & 3) : 8 + 2 * (k >> 2) + (k & 3) - 2;
+}
+__host__ __device__ constexpr int tile_sw128(int r, int c) {
+  return r * 128 + ((((c >> 4) ^ (r & 7)) & 7) << 4) + (c & 15);
+}
+
+__global__ void __launch_bounds__(256) route_tiles_kernel(const float* __restrict__ k_mean,
+                                                          const float* __restrict__ v_mean, int nb, int ngroups,
+                                                          uint8_t* __restrict__ tiles) {
+  const int grp = blockIdx.x, g = blockIdx.y;
+  const int g0 = grp * 16;
+  uint8_t* t = tiles + (static_cast<int64_t>(g) * ngroups + grp) * 8192;
+  // 16 rows x 64 channel pairs for each of k_mean and v_mean
+  for (int e = threadIdx.x; e < 2 * 16 * 64; e += blockDim.x) {
+    const int which = e >> 10, r = (e >> 6) & 15, pair = e & 63;
+    const int ch = 2 * pair;                       // channel of the low half
+    const int blk = g0 + (which == 0 ? r : route_tile_block(r));
+    float v0 = 0.f, v1 = 0.f;
+    if (blk < nb) {
+      const float* src = (which == 0 ? k_mean : v_mean) + (static_cast<int64_t>(g) * nb + blk) * 128 + ch;
+      v0 = src[0];
+      v1 = src[1];
+    }
+    const uint32_t word = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v0))) |
+                          (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v1))) << 16);
+    const int half = ch >> 6, c = (ch & 63) * 2;
+    *reinterpret_cast<uint32_t*>(t + which * 4096 + half * 2048 + tile_sw128(r, c)) = word;
+  }
+}
+
+cudaError_t launch_route_tiles(const float* k_mean, const float* v_mean, int G, int nb, uint8_t* tiles,
+                               cudaStream_t st) {
+  const int ngroups = (nb + 15) / 16;
+  if (G <= 0 || ngroups <= 0) return cudaSuccess;
+  route_tiles_kernel<<<dim3(ngroups, G), 256, 0, st>>>(k_mean, v_mean, nb, ngroups, tiles);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st) {
   const int nqb = p.n_pad / p.q_block;
   const int nb = p.n_pad / p.block_rows;

@@ -100,8 +100,9 @@ _SIGNATURES = {
                                        c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int,
                                        c_double, c_void_p, c_int, c_int64, c_int64, c_int64,
                                        c_void_p]),
+    "vcattn_route_tiles": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "vcattn_attn_fp8_sparse_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                                          c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                          c_void_p, c_void_p, c_void_p, c_int, c_int,
                                           c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int,
                                           c_double, c_void_p, c_int, c_int64, c_int64, c_int64,
                                           c_void_p]),

@@ -79,6 +79,7 @@ class Prepared(NamedTuple):
     n_qblk: int = 0
     # build-specific operands
     v_t: Optional[torch.Tensor] = None      # (G, NB, D, block_rows) uint8 V codes, block-transposed
+    ap_tiles: Optional[torch.Tensor] = None  # (G, ceil(NB/16), 8192) uint8 bf16 proxy tiles (tcgen05 sparse)
     q_cent: Optional[torch.Tensor] = None   # (G, NQB, D) fp32
     q_bar: Optional[torch.Tensor] = None    # (G, NQB, D) fp32
     keep: Optional[torch.Tensor] = None     # (G, NQB, NB) uint8 routing mask
@@ -200,12 +201,16 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
             qv, kv, dt, b, h, n, d, _ptr(perm_t), perm_rows, block_rows, flags & ~N.V_MMA_ORDER,
             q4.data_ptr(), q4s.data_ptr(), q4g.data_ptr(), k4.data_ptr(), k4s.data_ptr(), k4g.data_ptr(),
             q4sf.data_ptr(), k4sf.data_ptr(), ws.data_ptr(), ws_bytes, _stream(q)))
-    keep = thresh = None
+    keep = thresh = ap_tiles = None
     nqb = 0
     if sparse:
         nqb = n_pad // q_block
         keep, thresh = route_mask(route, g, n, n_pad, d, block_rows, tau, local_blocks, sink_blocks,
                                   sc, dev, q)
+        if d == 128 and block_rows == 128:
+            ap_tiles = torch.empty((g, -(-nb // 16), 8192), dtype=u8, device=dev)
+            N.check("vcattn_route_tiles", lib.vcattn_route_tiles(
+                k_mean.data_ptr(), v_mean.data_ptr(), g, n_pad, d, block_rows, ap_tiles.data_ptr(), _stream(q)))
     f8 = torch.float8_e4m3fn
     return Prepared(
         q=q8.view(f8).view(b, h, n_pad, d), q_scale=qs.view(b, h, n_pad),
@@ -216,6 +221,7 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
         v_mean=None if v_mean is None else v_mean.view(b, h, nb, d),
         thresh=None if thresh is None else thresh.view(b, h, nqb), n_qblk=nqb,
         v_t=v8t, q_cent=q_cent, q_bar=q_bar, keep=keep, block_rows=block_rows, v_mma_order=v_mma_order,
+        ap_tiles=ap_tiles,
         q4=None if q4 is None else q4.view(b, h, n_pad, d // 2),
         q4_scale=None if q4s is None else q4s.view(b, h, n_pad, d // 16),
         k4=None if k4 is None else k4.view(b, h, n_pad, d // 2),
@@ -330,16 +336,16 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
         return out
     if cfg.sparse:
         if kernel == "auto":
-            kernel = "tc" if (p.v is not None and p.v_mma_order and
+            kernel = "tc" if (p.v is not None and p.v_mma_order and p.ap_tiles is not None and
                               sparse_tc_applies(d, p.block_rows, cfg.block_m, cfg.group, n_pad)) else "mma"
         if kernel == "tc":
-            if p.v is None or not p.v_mma_order:
-                raise ValueError("the tcgen05 sparse kernel reads V codes in its key order "
-                                 "(want_v=True, v_mma_order=True)")
+            if p.v is None or not p.v_mma_order or p.ap_tiles is None:
+                raise ValueError("the tcgen05 sparse kernel reads V codes in its key order and the proxy "
+                                 "tiles (want_v=True, v_mma_order=True, D = block_rows = 128)")
             N.check("vcattn_attn_fp8_sparse_tc", lib.vcattn_attn_fp8_sparse_tc(
                 q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
-                p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), p.k_mean.data_ptr(),
-                p.v_mean.data_ptr(), p.keep.data_ptr(), cfg.block_m, cfg.group, b, h, n, n_pad, d,
+                p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), p.ap_tiles.data_ptr(),
+                p.keep.data_ptr(), cfg.block_m, cfg.group, b, h, n, n_pad, d,
                 p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
                 out.stride(0), out.stride(1), out.stride(2), st))
             return out

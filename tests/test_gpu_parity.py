@@ -388,6 +388,50 @@ def _sparse_gpu(q, k, v, perm, dev, tau, local=1, sink=0, expcast=False, out_dty
     return out.float().cpu().numpy().reshape(b * h, n, d), p
 
 
+def _route_tiles_np(k_mean, v_mean):
+    """Expected bytes of vcattn_route_tiles: per (head, group of 16 blocks) an
+    8 KB tile, bf16(k_mean) K-major then bf16(v_mean) MN-major with rows in
+    the proxy MMA's key order, both in the 128-byte swizzle."""
+    g, nb, d = k_mean.shape
+    ng = -(-nb // 16)
+    out = np.zeros((g, ng, 8192), np.uint8)
+    kb = O.f32_to_bf16_bits(k_mean).astype(np.uint16)
+    vb = O.f32_to_bf16_bits(v_mean).astype(np.uint16)
+
+    def sw(r, c):
+        return r * 128 + ((((c >> 4) ^ (r & 7)) & 7) << 4) + (c & 15)
+
+    def blk_of(kpos):
+        return 2 * (kpos >> 2) + (kpos & 3) if (kpos & 3) < 2 else 8 + 2 * (kpos >> 2) + (kpos & 3) - 2
+
+    for gi in range(g):
+        for gr in range(ng):
+            t = out[gi, gr]
+            for which, src in ((0, kb), (1, vb)):
+                for r in range(16):
+                    blk = gr * 16 + (r if which == 0 else blk_of(r))
+                    if blk >= nb:
+                        continue
+                    for ch in range(d):
+                        half, c = ch // 64, (ch % 64) * 2
+                        off = which * 4096 + half * 2048 + sw(r, c)
+                        val = int(src[gi, blk, ch])
+                        t[off] = val & 0xFF
+                        t[off + 1] = val >> 8
+    return out
+
+
+def test_route_tiles_layout(dev):
+    n, h = 2500, 2     # 20 blocks: a full and a partial group
+    q, k, v = make_qkv(1, h, n, 128, seed=5)
+    perm = np.stack([np.random.default_rng(i).permutation(n) for i in range(h)]).astype(np.int32)
+    p = _prep_gpu(q, k, v, perm, 128, dev, sparse=True, tau=1.3, q_block=64, want_v=True)
+    assert p.ap_tiles is not None
+    nb = p.k_mean.shape[-2]
+    want = _route_tiles_np(p.k_mean.reshape(h, nb, 128).cpu().numpy(), p.v_mean.reshape(h, nb, 128).cpu().numpy())
+    np.testing.assert_array_equal(p.ap_tiles.cpu().numpy(), want)
+
+
 @pytest.mark.parametrize("kernel", ["tc", "mma"])
 @pytest.mark.parametrize("expcast", [False, True])
 def test_sparse_attention_matches_oracle(dev, expcast, kernel):
