@@ -153,9 +153,27 @@ __device__ __forceinline__ void fwht128_warp(float v[4], int lane) {
       v[t] = __fmaf_rn(sg, v[t], p);
     }
   }
-  const float r = 11.313708498984761f;   // fp32(sqrt(128))
+  // IEEE division by r = fp32(sqrt(128)) = 0x1.6a09e6p+3.  Markstein's
+  // correction from y = RN(1/r) = 0x1.6a09e6p-4 equals __fdiv_rn(x, r) for
+  // every fp32 x with 2^-100 <= |x| <= 2^100: an exhaustive run over all 2^32
+  // inputs on B200 found 1 595 509 differences, all with |x| <= 2.2e-32 (the
+  // residual leaves the normal range) or x = -0 (sign of zero).  A row holding
+  // any value outside that range takes the division itself.
+  const float r = 11.313708498984761f;
+  const float y = 0.0883883461356163f;
+  bool slow = false;
 #pragma unroll
-  for (int t = 0; t < 4; ++t) v[t] = __fdiv_rn(v[t], r);
+  for (int t = 0; t < 4; ++t) slow |= !(fabsf(v[t]) >= 0x1p-100f && fabsf(v[t]) <= 0x1p+100f);
+  if (__any_sync(0xffffffffu, slow)) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) v[t] = __fdiv_rn(v[t], r);
+  } else {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float q0 = __fmul_rn(v[t], y);
+      v[t] = __fmaf_rn(__fmaf_rn(-q0, r, v[t]), y, q0);
+    }
+  }
 }
 
 // 64-wide variant: lanes 0..15 hold a row (4 elements each), lanes 16..31 a
@@ -174,9 +192,9 @@ __device__ __forceinline__ void fwht64_halfwarp(float v[4], int lane) {
       v[t] = __fmaf_rn(sg, v[t], p);
     }
   }
-  const float r = 8.0f;   // fp32(sqrt(64))
+  // division by fp32(sqrt(64)) = 8: the scaling by 2^-3 is the same rounding
 #pragma unroll
-  for (int t = 0; t < 4; ++t) v[t] = __fdiv_rn(v[t], r);
+  for (int t = 0; t < 4; ++t) v[t] = __fmul_rn(v[t], 0.125f);
 }
 
 }  // namespace vcattn
