@@ -53,14 +53,17 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
   return d;
 }
 // Four ExpCast codes (fma.sat to [0,1] in units of 128 codes, then + 98304
-// rounds to an integer in the low byte) packed into one word.
+// rounds to an integer in the low byte) packed into one word.  The word of
+// c = 98304 + code / 128 is 0x47c00000 + code, so a + (b << 8) holds
+// code_a | code_b << 8 in its low half (no carry out of the low byte); one
+// byte permute joins the halves.
 __device__ __forceinline__ uint32_t expcast4(float x0, float x1, float x2, float x3, float As, float Bs) {
   float c0 = fma_sat(x0, As, Bs), c1 = fma_sat(x1, As, Bs);
   float c2 = fma_sat(x2, As, Bs), c3 = fma_sat(x3, As, Bs);
   add2(c0, c1, 98304.0f, 98304.0f);
   add2(c2, c3, 98304.0f, 98304.0f);
-  const uint32_t lo = __byte_perm(__float_as_uint(c0), __float_as_uint(c1), 0x0040);
-  const uint32_t hi = __byte_perm(__float_as_uint(c2), __float_as_uint(c3), 0x0040);
+  const uint32_t lo = __float_as_uint(c0) + (__float_as_uint(c1) << 8);
+  const uint32_t hi = __float_as_uint(c2) + (__float_as_uint(c3) << 8);
   return __byte_perm(lo, hi, 0x5410);
 }
 // Four E4M3(exp2(x * Ae + Be)) bytes packed into one word.
