@@ -542,12 +542,13 @@ def main() -> int:
     fl_exec = fl if keep_frac is None else (keep_frac * fl + 4.0 * G * NT * (NT // w["block_rows"]) * D)
     attn_tflops = fl_exec / (attn_ms / 1e3) / 1e12
     traffic = None   # DRAM bytes per attention launch from the committed ncu summary
-    tpath = os.path.join(ROOT, "profiles", "attn_tc_c1.md")
-    if os.path.exists(tpath):
-        with open(tpath) as f:
-            for ln in f:
-                if ln.startswith(f"traffic_bytes_per_launch {args.workload}:"):
-                    traffic = int(ln.split(":")[1])
+    for tname in ("attn_tc_c1.md", "attn_tc_sparse_c2.md"):
+        tpath = os.path.join(ROOT, "profiles", tname)
+        if os.path.exists(tpath):
+            with open(tpath) as f:
+                for ln in f:
+                    if ln.startswith(f"traffic_bytes_per_launch {args.workload}:"):
+                        traffic = int(ln.split(":")[1])
     prep_bytes = (6 * G * NT * D + 3 * G * NT * D + 8 * G * NT + 8 * G * (NT // w["block_rows"]) * D
                   + 4 * G * NT)
     launches_per_step = 5 + 1
