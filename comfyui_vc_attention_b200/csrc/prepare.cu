@@ -136,15 +136,18 @@ struct QKArgs {
   float sm_scale;
 };
 
-template <int DT, int D>
-__global__ void __launch_bounds__(256) quant_rows_kernel(QKArgs a) {
+// STATS: the routing block statistics are requested (blk_mean / blk_qbar);
+// without them the kernel keeps no float64 accumulators and fits three CTAs
+// per SM (79 registers) instead of two.
+template <int DT, int D, bool STATS>
+__global__ void __launch_bounds__(256, STATS ? 2 : 3) quant_rows_kernel(QKArgs a) {
   using RM = RowMap<D>;
   const int g = blockIdx.y;
   const int b = g / a.H, h = g % a.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * a.rows;
-  const bool want_mean = a.blk_mean != nullptr;
-  const bool want_qbar = a.blk_qbar != nullptr;
+  const bool want_mean = STATS && a.blk_mean != nullptr;
+  const bool want_qbar = STATS && a.blk_qbar != nullptr;
   double msum[4] = {0.0, 0.0, 0.0, 0.0};
   double qsum[4] = {0.0, 0.0, 0.0, 0.0};
   float km[4] = {0.f, 0.f, 0.f, 0.f};
@@ -209,6 +212,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(QKArgs a) {
     }
   }
   }
+  if constexpr (!STATS) return;
   if (!want_mean && !want_qbar) return;
   __shared__ double red_m[8][32][4];
   __shared__ double red_q[8][32][4];
@@ -630,7 +634,8 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
     a.blk_qbar = route ? p.route->q_bar : nullptr;
     a.sm_scale = route ? p.route->sm_scale : 0.f;
     const int grid_x = (p.n_pad + a.rows - 1) / a.rows;
-    quant_rows_kernel<DT, D><<<dim3(grid_x, G), 256, 0, st>>>(a);
+    if (route) quant_rows_kernel<DT, D, true><<<dim3(grid_x, G), 256, 0, st>>>(a);
+    else quant_rows_kernel<DT, D, false><<<dim3(grid_x, G), 256, 0, st>>>(a);
   }
   // K rows (gathered by perm)
   {
@@ -641,7 +646,8 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
     a.rows = p.block_rows;
     a.blk_mean = route ? p.route->k_mean : nullptr;
     a.blk_qbar = nullptr;
-    quant_rows_kernel<DT, D><<<dim3(nb, G), 256, 0, st>>>(a);
+    if (route) quant_rows_kernel<DT, D, true><<<dim3(nb, G), 256, 0, st>>>(a);
+    else quant_rows_kernel<DT, D, false><<<dim3(nb, G), 256, 0, st>>>(a);
   }
   // V blocks
   {
