@@ -263,9 +263,9 @@ __host__ __device__ __forceinline__ int mma_key_slot(int r) {
 // XOR-swizzled by row / 4, which keeps both its row-major writes and its
 // column reads free of bank conflicts.
 template <int DT, int D, int BR>
-__global__ void __launch_bounds__(256) quant_v_kernel(VArgs a) {
+__global__ void __launch_bounds__(512, 2) quant_v_kernel(VArgs a) {
   using RM = RowMap<D>;
-  constexpr int kWarps = 8;
+  constexpr int kWarps = 16;   // 16 warps, two CTAs per SM: 32 row-holding warps
   constexpr int kSteps = BR / (kWarps * RM::kRowsPerWarp);   // rows per lane
   constexpr int kWords = D / 4;                              // 4-byte code words per row
   __shared__ double red[kWarps][32][4];
@@ -656,8 +656,8 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
     a.perm = p.perm; a.perm_rows = p.perm_rows;
     a.codes = p.v8; a.codes_t = p.v8t; a.scale = p.v_scale; a.mu = p.mu; a.mean = p.v_mean;
     a.mma_order = (p.flags & VCATTN_V_MMA_ORDER) != 0;
-    if (p.block_rows == 128) quant_v_kernel<DT, D, 128><<<dim3(nb, G), 256, 0, st>>>(a);
-    else quant_v_kernel<DT, D, 64><<<dim3(nb, G), 256, 0, st>>>(a);
+    if (p.block_rows == 128) quant_v_kernel<DT, D, 128><<<dim3(nb, G), 512, 0, st>>>(a);
+    else quant_v_kernel<DT, D, 64><<<dim3(nb, G), 512, 0, st>>>(a);
   }
   return cudaGetLastError();
 }
