@@ -64,7 +64,7 @@ __device__ __forceinline__ double reduce_lanes(double (*red)[32][4], int nwarps,
 }
 
 template <int DT, int D>
-__global__ void __launch_bounds__(256) kmean_partial_kernel(
+__global__ void __launch_bounds__(256, 3) kmean_partial_kernel(
     vcattn_bhnd k, int H, int N, int flags, double* __restrict__ partial) {
   using RM = RowMap<D>;
   __shared__ double red[8][32][4];
@@ -140,7 +140,7 @@ struct QKArgs {
 // without them the kernel keeps no float64 accumulators and fits three CTAs
 // per SM (79 registers) instead of two.
 template <int DT, int D, bool STATS>
-__global__ void __launch_bounds__(256, STATS ? 2 : 3) quant_rows_kernel(QKArgs a) {
+__global__ void __launch_bounds__(256, STATS ? 2 : 4) quant_rows_kernel(QKArgs a) {
   using RM = RowMap<D>;
   const int g = blockIdx.y;
   const int b = g / a.H, h = g % a.H;
@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(256, STATS ? 2 : 3) quant_rows_kernel(QKArgs a
   const int nwarps = blockDim.x >> 5;
   // kBatch rows per warp are loaded before any is used (memory-level
   // parallelism); rows = 64 or 128 gives 8 or 16 rows per warp.
-  constexpr int kBatch = 8;
+  constexpr int kBatch = STATS ? 8 : 4;
   const int step = nwarps * RM::kRowsPerWarp;
   for (int base0 = warp * RM::kRowsPerWarp; base0 < a.rows; base0 += kBatch * step) {
   float vb[kBatch][4];
