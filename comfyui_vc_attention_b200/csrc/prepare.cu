@@ -137,10 +137,10 @@ struct QKArgs {
 };
 
 // STATS: the routing block statistics are requested (blk_mean / blk_qbar);
-// without them the kernel keeps no float64 accumulators and fits three CTAs
-// per SM (79 registers) instead of two.
+// without them the kernel keeps no float64 accumulators and fits four CTAs
+// per SM (64 registers), with them three (72 registers).
 template <int DT, int D, bool STATS>
-__global__ void __launch_bounds__(256, STATS ? 2 : 4) quant_rows_kernel(QKArgs a) {
+__global__ void __launch_bounds__(256, STATS ? 3 : 4) quant_rows_kernel(QKArgs a) {
   using RM = RowMap<D>;
   const int g = blockIdx.y;
   const int b = g / a.H, h = g % a.H;
@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(256, STATS ? 2 : 4) quant_rows_kernel(QKArgs a
   const int nwarps = blockDim.x >> 5;
   // kBatch rows per warp are loaded before any is used (memory-level
   // parallelism); rows = 64 or 128 gives 8 or 16 rows per warp.
-  constexpr int kBatch = STATS ? 8 : 4;
+  constexpr int kBatch = 4;
   const int step = nwarps * RM::kRowsPerWarp;
   for (int base0 = warp * RM::kRowsPerWarp; base0 < a.rows; base0 += kBatch * step) {
   float vb[kBatch][4];
