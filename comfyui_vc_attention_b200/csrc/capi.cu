@@ -180,8 +180,14 @@ int vcattn_prepare_fp8(const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_
   VC_CHECK(view_ok(q, dtype) && view_ok(k, dtype) && view_ok(v, dtype),
            "vcattn_prepare_fp8: q/k/v must be 16-byte aligned with 16-byte multiple strides");
   VC_CHECK(perm == nullptr || perm_rows == 1 || perm_rows == B * H, "vcattn_prepare_fp8: perm_rows must be 1 or G");
-  VC_CHECK(q8 && q_scale && k8 && k_scale && v_scale && mu && (v8 || v8t), "vcattn_prepare_fp8: null output");
-  VC_CHECK(aligned16(q8) && aligned16(k8) && (v8 == nullptr || aligned16(v8)) && (v8t == nullptr || aligned16(v8t)),
+  // Q (or K) codes are skipped when both their code and scale buffers are
+  // null (the NVFP4 path only needs V here); routing needs both.
+  VC_CHECK((q8 == nullptr) == (q_scale == nullptr) && (k8 == nullptr) == (k_scale == nullptr),
+           "vcattn_prepare_fp8: q8/q_scale and k8/k_scale must be given (or left out) together");
+  VC_CHECK(v_scale && mu && (v8 || v8t), "vcattn_prepare_fp8: null output");
+  VC_CHECK(route == nullptr || (q8 && k8), "vcattn_prepare_fp8: routing statistics need the Q and K codes");
+  VC_CHECK((q8 == nullptr || aligned16(q8)) && (k8 == nullptr || aligned16(k8)) && (v8 == nullptr || aligned16(v8)) &&
+               (v8t == nullptr || aligned16(v8t)),
            "vcattn_prepare_fp8: code buffers must be 16-byte aligned");
   const int G = B * H;
   const int n_pad = (N + block_rows - 1) / block_rows * block_rows;
@@ -190,7 +196,7 @@ int vcattn_prepare_fp8(const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_
     VC_CHECK(n_pad % route->q_block == 0, "vcattn_prepare_fp8: n_pad must be a multiple of q_block");
   }
   const size_t need = prepare_workspace_bytes(G, N, D);
-  if ((flags & VCATTN_SMOOTH_K) && (workspace == nullptr || workspace_bytes < need))
+  if ((flags & VCATTN_SMOOTH_K) && k8 != nullptr && (workspace == nullptr || workspace_bytes < need))
     return fail(VCATTN_ERR_WORKSPACE, "vcattn_prepare_fp8: workspace too small (need " + std::to_string(need) + " bytes)");
   PrepareParams p{};
   p.q = q; p.k = k; p.v = v; p.dtype = dtype; p.B = B; p.H = H; p.N = N; p.D = D; p.n_pad = n_pad;

@@ -479,7 +479,7 @@ struct NvArgs {
 };
 
 template <int DT, int D, bool QUANT>
-__global__ void __launch_bounds__(256) nvfp4_rows_kernel(NvArgs a) {
+__global__ void __launch_bounds__(256, 4) nvfp4_rows_kernel(NvArgs a) {
   using RM = RowMap<D>;
   const int g = blockIdx.y;
   const int b = g / a.H, h = g % a.H;
@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(256) nvfp4_rows_kernel(NvArgs a) {
   }
   float mx = 0.f;
   const int nwarps = blockDim.x >> 5;
-  constexpr int kBatch = 8;
+  constexpr int kBatch = 4;
   const int step = nwarps * RM::kRowsPerWarp;
   for (int base0 = warp * RM::kRowsPerWarp; base0 < a.rows; base0 += kBatch * step) {
     float vb[kBatch][4];
@@ -615,7 +615,7 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
   const int G = p.B * p.H;
   const int nb = p.n_pad / p.block_rows;
   float* kmean = nullptr;
-  if (p.flags & VCATTN_SMOOTH_K) {
+  if ((p.flags & VCATTN_SMOOTH_K) && p.k8 != nullptr) {
     const int nchunks = (p.N + kChunkRows - 1) / kChunkRows;
     double* partial = reinterpret_cast<double*>(p.workspace);
     kmean = reinterpret_cast<float*>(partial + static_cast<size_t>(G) * nchunks * D);
@@ -624,7 +624,7 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
   }
   const bool route = p.route != nullptr;
   // Q rows
-  {
+  if (p.q8 != nullptr) {
     QKArgs a{};
     a.x = *p.q; a.H = p.H; a.N = p.N; a.n_pad = p.n_pad; a.flags = p.flags;
     a.perm = nullptr; a.perm_rows = 0; a.kmean = nullptr;
@@ -638,7 +638,7 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
     else quant_rows_kernel<DT, D, false><<<dim3(grid_x, G), 256, 0, st>>>(a);
   }
   // K rows (gathered by perm)
-  {
+  if (p.k8 != nullptr) {
     QKArgs a{};
     a.x = *p.k; a.H = p.H; a.N = p.N; a.n_pad = p.n_pad; a.flags = p.flags;
     a.perm = p.perm; a.perm_rows = p.perm_rows; a.kmean = kmean;

@@ -125,14 +125,15 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
             sparse: bool = False, tau: float = 1.3, q_block: int = 64,
             scale: Optional[float] = None, want_v: bool = True, want_v_t: bool = False,
             local_blocks: int = 1, sink_blocks: int = 0, v_mma_order: bool = True,
-            qk_fp4: bool = False) -> Prepared:
+            qk_fp4: bool = False, fp8_qk: bool = True) -> Prepared:
     """Quantise and permute Q/K/V into the kernel layout (triton_attn.py:504-579).
 
     Byte-identical to the reference's portable ``prepare`` on the codes; the
     scales that depend on a token/block mean differ from it only in the last
     bits (the mean is rounded once here).  With ``sparse=True`` the routing
     statistics and the block mask are produced as well; with ``qk_fp4=True``
-    the NVFP4 Q/K of quant.py:172-204 (one tensor scale per head) too.
+    the NVFP4 Q/K of quant.py:172-204 (one tensor scale per head) too, and
+    ``fp8_qk=False`` then leaves out the E4M3 Q/K codes (``q``, ``k`` None).
     """
     _check_qkv(q, k, v)
     lib = N.lib()
@@ -155,12 +156,14 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
             raise ValueError(f"perm must be (G, N) or (1, N), got {tuple(perm_t.shape)}")
         perm_rows = perm_t.shape[0]
     u8 = torch.uint8
-    q8 = torch.empty((g, n_pad, d), dtype=u8, device=dev)
-    k8 = torch.empty((g, n_pad, d), dtype=u8, device=dev)
+    if not fp8_qk and (sparse or not qk_fp4):
+        raise ValueError("fp8_qk=False is only for the NVFP4 QK path (qk_fp4=True, dense)")
+    q8 = torch.empty((g, n_pad, d), dtype=u8, device=dev) if fp8_qk else None
+    k8 = torch.empty((g, n_pad, d), dtype=u8, device=dev) if fp8_qk else None
     v8 = torch.empty((g, n_pad, d), dtype=u8, device=dev) if want_v else None
     v8t = torch.empty((g, nb, d, block_rows), dtype=u8, device=dev) if want_v_t else None
-    qs = torch.empty((g, n_pad), dtype=torch.float32, device=dev)
-    ks = torch.empty((g, n_pad), dtype=torch.float32, device=dev)
+    qs = torch.empty((g, n_pad), dtype=torch.float32, device=dev) if fp8_qk else None
+    ks = torch.empty((g, n_pad), dtype=torch.float32, device=dev) if fp8_qk else None
     vs = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
     mu = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
     flags = (N.HADAMARD if hadamard else 0) | (N.SMOOTH_K if smooth_k else 0)
@@ -184,7 +187,7 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
     ws = torch.empty(ws_bytes, dtype=u8, device=dev)
     N.check("vcattn_prepare_fp8", lib.vcattn_prepare_fp8(
         qv, kv, vv, dt, b, h, n, d, _ptr(perm_t), perm_rows, block_rows, flags,
-        q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), _ptr(v8), vs.data_ptr(),
+        _ptr(q8), _ptr(qs), _ptr(k8), _ptr(ks), _ptr(v8), vs.data_ptr(),
         mu.data_ptr(), _ptr(v8t), route, ws.data_ptr(), ws_bytes, _stream(q)))
     q4 = q4s = k4 = k4s = q4g = k4g = q4sf = k4sf = None
     if qk_fp4:
@@ -213,8 +216,10 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
                 k_mean.data_ptr(), v_mean.data_ptr(), g, n_pad, d, block_rows, ap_tiles.data_ptr(), _stream(q)))
     f8 = torch.float8_e4m3fn
     return Prepared(
-        q=q8.view(f8).view(b, h, n_pad, d), q_scale=qs.view(b, h, n_pad),
-        k=k8.view(f8).view(b, h, n_pad, d), k_scale=ks.view(b, h, n_pad),
+        q=None if q8 is None else q8.view(f8).view(b, h, n_pad, d),
+        q_scale=None if qs is None else qs.view(b, h, n_pad),
+        k=None if k8 is None else k8.view(f8).view(b, h, n_pad, d),
+        k_scale=None if ks is None else ks.view(b, h, n_pad),
         v=None if v8 is None else v8.view(f8).view(b, h, n_pad, d),
         v_scale=vs.view(b, h, nb, d), mu=mu.view(b, h, nb, d), n_pad=n_pad,
         k_mean=None if k_mean is None else k_mean.view(b, h, nb, d),
@@ -305,7 +310,7 @@ def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     p = prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
                 tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=use_tc, want_v_t=not use_tc,
                 local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks, v_mma_order=not fp4,
-                qk_fp4=fp4)
+                qk_fp4=fp4, fp8_qk=not fp4)
     out = _out_view(q, q.dtype)
     return attention_prepared(p, n, out, scale, cfg)
 
@@ -319,11 +324,9 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
     and the sparse path alike.
     """
     lib = N.lib()
-    b, h, n_pad, d = p.q.shape
+    b, h, n_pad, d = (p.q if p.q is not None else p.v).shape
     flags = N.EXPCAST if cfg.enable_expcast else 0
     odt = _dtype_code(out)
-    q8 = p.q.view(torch.uint8)
-    k8 = p.k.view(torch.uint8)
     st = _stream(out)
     if cfg.qk_fp4 and not cfg.sparse:
         if p.q4 is None or p.v is None or p.v_mma_order:
@@ -334,6 +337,10 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
             b, h, n, n_pad, d, p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
             out.stride(0), out.stride(1), out.stride(2), st))
         return out
+    if p.q is None or p.k is None:
+        raise ValueError("the FP8 kernels need the E4M3 Q/K codes (prepare with fp8_qk=True)")
+    q8 = p.q.view(torch.uint8)
+    k8 = p.k.view(torch.uint8)
     if cfg.sparse:
         if kernel == "auto":
             kernel = "tc" if (p.v is not None and p.v_mma_order and p.ap_tiles is not None and

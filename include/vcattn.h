@@ -116,7 +116,10 @@ VCATTN_API int vcattn_kmeans(const vcattn_bhnd* v, int dtype, int B, int H, int 
  *    v8t: NULL, or the same V codes stored block-transposed (G,NB,D,block_rows)
  *    (the operand layout of the register-MMA attention kernels); v8 may be
  *    NULL when only v8t is wanted.
- * route: NULL, or routing statistics to fill (block-sparse path). */
+ *    q8 + q_scale (or k8 + k_scale) may both be NULL: those rows are then not
+ *    quantised (the NVFP4 QK path takes its Q / K from vcattn_prepare_nvfp4).
+ * route: NULL, or routing statistics to fill (block-sparse path; needs the
+ *    Q and K codes). */
 VCATTN_API size_t vcattn_prepare_workspace_bytes(int G, int N, int D);
 VCATTN_API int vcattn_prepare_fp8(const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_bhnd* v,
                        int dtype, int B, int H, int N, int D,
