@@ -63,6 +63,9 @@ WORKLOADS = {
     "c2h16": dict(desc="profiling slice of configs[2]: tau=1.3 block-sparse, B1 H16 N16384 D128, 16x32x32 grid",
                   B=1, H=16, N=16384, D=128, expcast=True, sparse=True, k=64, block_rows=128,
                   spatial=(16, 32, 32), tau=1.3),
+    "c2l": dict(desc="configs[2] at N=65536: block-sparse FP8 VC-Attention, tau=1.3, B1 H56 N65536 D128 on a "
+                     "64x32x32 grid, ExpCast on, V-Smooth k=512", B=1, H=56, N=65536, D=128, expcast=True,
+                sparse=True, k=512, block_rows=128, spatial=(64, 32, 32), tau=1.3),
     "c2": dict(desc="configs[2]: block-sparse FP8 VC-Attention, tau=1.3, B1 H56 N16384 D128 on a 16x32x32 "
                     "grid, ExpCast on, V-Smooth k=64", B=1, H=56, N=16384, D=128, expcast=True, sparse=True,
                k=64, block_rows=128, spatial=(16, 32, 32), tau=1.3),

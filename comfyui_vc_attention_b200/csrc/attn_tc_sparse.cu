@@ -211,41 +211,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
   }
   for (int i = tid; i < 16 * 128; i += kThreads) sm.ones[i] = 0x38;
-  // Step list (warp 0): lane l tests block g0 + l%16 of query block l/16.
+  // Step list (warp 0): lane l handles group gbase + l; its 16 keep bytes of
+  // each query block are independent loads, and a warp scan of the steps per
+  // group gives every lane its slot in the list.
   if (warp == 0) {
     const int qa = 2 * blockIdx.x, qbk = 2 * blockIdx.x + 1;
     const uint8_t* keep_a = a.keep + (static_cast<int64_t>(g) * a.nqb + qa) * nb;
     const uint8_t* keep_b = a.keep + (static_cast<int64_t>(g) * a.nqb + qbk) * nb;
     const bool has_b = qbk < a.nqb;
-    int n = 0, ap_ord = 0;
-    for (int g0 = 0; g0 < nb; g0 += kGroup) {
-      const int blk = g0 + (lane & 15);
-      const bool valid = blk < nb && (lane < 16 || has_b);
-      const bool kept = valid && (lane < 16 ? keep_a[blk] : keep_b[blk]) != 0;
-      const uint32_t km = __ballot_sync(0xffffffffu, kept);
-      const uint32_t vm = __ballot_sync(0xffffffffu, valid);
-      const uint32_t am = vm & ~km;   // approximated blocks, A in bits 0-15, B in 16-31
-      if (am != 0) {
-        if (lane == 0 && n < kMaxSteps) {
-          sm.steps[n].info = static_cast<uint32_t>(g0 / kGroup) | (static_cast<uint32_t>(ap_ord) << 16) | (1u << 31);
-          sm.steps[n].mask = am;
+    const int ngr = (nb + kGroup - 1) / kGroup;
+    int n_base = 0, ap_base = 0;
+    for (int gbase = 0; gbase < ngr; gbase += 32) {
+      const int gi = gbase + lane;
+      uint32_t km_a = 0, km_b = 0, vm = 0;
+      if (gi < ngr) {
+        const int b0 = gi * kGroup;
+#pragma unroll
+        for (int i = 0; i < kGroup; ++i) {
+          if (b0 + i < nb) {
+            vm |= 1u << i;
+            km_a |= static_cast<uint32_t>(keep_a[b0 + i] != 0) << i;
+            if (has_b) km_b |= static_cast<uint32_t>(keep_b[b0 + i] != 0) << i;
+          }
         }
-        ++n;
-        ++ap_ord;
       }
-      const uint32_t ku = (km | (km >> 16)) & 0xffffu;   // union of kept blocks
-      for (uint32_t rest = ku; rest != 0; rest &= rest - 1) {
-        const int bj = __ffs(rest) - 1;
-        if (lane == 0 && n < kMaxSteps) {
-          sm.steps[n].info = static_cast<uint32_t>(g0 + bj);
-          sm.steps[n].mask = ((km >> bj) & 1u) | (((km >> (16 + bj)) & 1u) << 1);
+      const uint32_t am = (vm & ~km_a) | (has_b ? (vm & ~km_b) << 16 : 0u);   // approximated: A 0-15, B 16-31
+      const uint32_t ku = km_a | km_b;                                        // union of kept blocks
+      const int has_ap = am != 0;
+      const int cnt = has_ap + __popc(ku);
+      int s_incl = cnt, a_incl = has_ap;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int ts = __shfl_up_sync(0xffffffffu, s_incl, o), ta = __shfl_up_sync(0xffffffffu, a_incl, o);
+        if (lane >= o) {
+          s_incl += ts;
+          a_incl += ta;
         }
-        ++n;
       }
+      int n = n_base + s_incl - cnt;
+      if (gi < ngr) {
+        if (has_ap) {
+          if (n < kMaxSteps) {
+            sm.steps[n].info = static_cast<uint32_t>(gi) |
+                               (static_cast<uint32_t>(ap_base + a_incl - has_ap) << 16) | (1u << 31);
+            sm.steps[n].mask = am;
+          }
+          ++n;
+        }
+        for (uint32_t rest = ku; rest != 0; rest &= rest - 1) {
+          const int bj = __ffs(rest) - 1;
+          if (n < kMaxSteps) {
+            sm.steps[n].info = static_cast<uint32_t>(gi * kGroup + bj);
+            sm.steps[n].mask = ((km_a >> bj) & 1u) | (((km_b >> bj) & 1u) << 1);
+          }
+          ++n;
+        }
+      }
+      n_base += __shfl_sync(0xffffffffu, s_incl, 31);
+      ap_base += __shfl_sync(0xffffffffu, a_incl, 31);
     }
     if (lane == 0) {
-      sm.nsteps = n;
-      sm.has_ap = ap_ord > 0;
+      sm.nsteps = n_base;
+      sm.has_ap = ap_base > 0;
     }
   }
   fence_proxy_async_smem();
