@@ -245,6 +245,7 @@ int vcattn_route_mask(const vcattn_route_stats* route, int G, int N, int n_pad, 
   VC_CHECK(route && route->k_mean && route->q_cent && route->q_bar, "vcattn_route_mask: missing statistics");
   VC_CHECK(D == 64 || D == 128, "vcattn_route_mask: D must be 64 or 128");
   VC_CHECK(block_rows == 64 || block_rows == 128, "vcattn_route_mask: block_rows must be 64 or 128");
+  VC_CHECK(n_pad / block_rows <= 2048, "vcattn_route_mask: at most 2048 KV blocks per head");
   VC_CHECK(route->q_block > 0 && n_pad % route->q_block == 0 && n_pad % block_rows == 0,
            "vcattn_route_mask: inconsistent padding");
   VC_CHECK(keep != nullptr, "vcattn_route_mask: null keep");

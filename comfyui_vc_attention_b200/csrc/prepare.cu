@@ -361,29 +361,24 @@ __global__ void __launch_bounds__(512, 2) quant_v_kernel(VArgs a) {
 
 // ---------------------------------------------------------------------------
 // Routing threshold + keep mask (triton_attn.py:449-459 and :716-735).
-// One CTA per (head, routing query block).  Warp w takes KV blocks w, w+8, ..;
-// its lanes read one k_mean row (coalesced) and form both float64 dots of
-// that row: the threshold proxy fp32(q_cent . k_mean_j) * scale and the
-// routing score fp32(q_bar . bf16(k_mean_j)) / q_block.  Each dot is summed
-// in float64 and rounded once, so its fp32 value does not depend on the
-// order of the partial sums.
+// One CTA per (head, kRouteQB routing query blocks); warp w owns query block
+// blockIdx.x * kRouteQB + w.  The head's k_mean rows stream through shared
+// memory 32 at a time (row stride D + 1 floats: lane r reading row r at a
+// common channel hits bank (r + d) % 32), next to their bf16 roundings, so
+// each row is read from L2 once per kRouteQB query blocks.  Lane r of warp w
+// forms both float64 dots of (query block w, KV block r): the threshold proxy
+// fp32(q_cent . k_mean_j) * scale and the routing score
+// fp32(q_bar . bf16(k_mean_j)) / q_block.  Each dot is summed in float64 and
+// rounded once, so its fp32 value does not depend on the order of the
+// partial sums.
 // ---------------------------------------------------------------------------
+constexpr int kRouteQB = 8;
+constexpr int kRouteRows = 32;
+
 __device__ __forceinline__ double warp_sum_f64(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
-}
-
-// Sum of one double per thread over the CTA (blockDim.x = 256); every thread
-// gets the total.
-__device__ __forceinline__ double block_sum_f64(double v, double* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  v = warp_sum_f64(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  double t = lane < (blockDim.x >> 5) ? red[lane] : 0.0;
-  return warp_sum_f64(t);
 }
 
 template <int D>
@@ -393,63 +388,72 @@ __global__ void __launch_bounds__(256) route_mask_kernel(const float* __restrict
                                                          int br, float tau, int local_blocks, int sink_blocks,
                                                          float sm_scale, uint8_t* __restrict__ keep,
                                                          float* __restrict__ thresh_out) {
-  constexpr int E = D / 32;                 // channels per lane
-  extern __shared__ float rsm[];            // proxy[nb], score[nb]
-  __shared__ double red[8];
-  float* proxy = rsm;
-  float* score = rsm + nb;
-  const int g = blockIdx.y, i = blockIdx.x;
+  constexpr int RS = D + 1;                      // padded row stride of the staged k_mean rows
+  extern __shared__ float rsm[];                 // kms, kbs [kRouteRows][RS]; proxy, score [kRouteQB][nb]
+  __shared__ float qcs[kRouteQB][D], qbs[kRouteQB][D];
+  float* kms = rsm;
+  float* kbs = rsm + kRouteRows * RS;
+  float* proxy = kbs + kRouteRows * RS;
+  float* score = proxy + kRouteQB * nb;
+  const int g = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float qc[E], qb[E];
-  {
-    const float* qcr = q_cent + (static_cast<int64_t>(g) * nqb + i) * D + E * lane;
-    const float* qbr = q_bar + (static_cast<int64_t>(g) * nqb + i) * D + E * lane;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      qc[e] = qcr[e];
-      qb[e] = qbr[e];
-    }
+  const int qi = blockIdx.x * kRouteQB + warp;   // this warp's routing query block
+  for (int e = tid; e < kRouteQB * D; e += blockDim.x) {
+    const int w = e / D, d = e % D, i = blockIdx.x * kRouteQB + w;
+    const bool ok = i < nqb;
+    qcs[w][d] = ok ? q_cent[(static_cast<int64_t>(g) * nqb + i) * D + d] : 0.f;
+    qbs[w][d] = ok ? q_bar[(static_cast<int64_t>(g) * nqb + i) * D + d] : 0.f;
   }
   const float inv_q = static_cast<float>(q_block);
-  for (int j = warp; j < nb; j += 8) {
-    const float* km = k_mean + (static_cast<int64_t>(g) * nb + j) * D + E * lane;
-    float kv[E];
-    if constexpr (E == 4) {
-      const float4 t = *reinterpret_cast<const float4*>(km);
-      kv[0] = t.x; kv[1] = t.y; kv[2] = t.z; kv[3] = t.w;
-    } else {
-      const float2 t = *reinterpret_cast<const float2*>(km);
-      kv[0] = t.x; kv[1] = t.y;
+  const float* km_head = k_mean + static_cast<int64_t>(g) * nb * D;
+  for (int j0 = 0; j0 < nb; j0 += kRouteRows) {
+    const int rows = min(kRouteRows, nb - j0);
+    __syncthreads();   // previous chunk consumed (and the q vectors staged)
+    for (int e = tid; e < rows * D; e += blockDim.x) {
+      const int r = e / D, d = e % D;
+      const float v = km_head[static_cast<int64_t>(j0 + r) * D + d];
+      kms[r * RS + d] = v;
+      kbs[r * RS + d] = bf16_round(v);
     }
-    double d1 = 0.0, d2 = 0.0;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      d1 = fma(static_cast<double>(qc[e]), static_cast<double>(kv[e]), d1);
-      d2 = fma(static_cast<double>(qb[e]), static_cast<double>(bf16_round(kv[e])), d2);
-    }
-    d1 = warp_sum_f64(d1);
-    d2 = warp_sum_f64(d2);
-    if (lane == 0) {
-      proxy[j] = __fmul_rn(__double2float_rn(d1), sm_scale);
-      score[j] = __fdiv_rn(__double2float_rn(d2), inv_q);
+    __syncthreads();
+    if (lane < rows) {
+      const float* kr = kms + lane * RS;
+      const float* br_ = kbs + lane * RS;
+      // two partial sums per dot (even / odd channels) keep two float64 FMA
+      // chains in flight; the sum stays one float64 value rounded once
+      double d1a = 0.0, d1b = 0.0, d2a = 0.0, d2b = 0.0;
+#pragma unroll 8
+      for (int d = 0; d < D; d += 2) {
+        d1a = fma(static_cast<double>(qcs[warp][d]), static_cast<double>(kr[d]), d1a);
+        d1b = fma(static_cast<double>(qcs[warp][d + 1]), static_cast<double>(kr[d + 1]), d1b);
+        d2a = fma(static_cast<double>(qbs[warp][d]), static_cast<double>(br_[d]), d2a);
+        d2b = fma(static_cast<double>(qbs[warp][d + 1]), static_cast<double>(br_[d + 1]), d2b);
+      }
+      proxy[warp * nb + j0 + lane] = __fmul_rn(__double2float_rn(d1a + d1b), sm_scale);
+      score[warp * nb + j0 + lane] = __fdiv_rn(__double2float_rn(d2a + d2b), inv_q);
     }
   }
-  __syncthreads();
+  __syncwarp();
+  if (qi >= nqb) return;
+  // threshold of this warp's query block: mean + tau * std of its proxies
+  const float* pr = proxy + warp * nb;
+  const float* sc = score + warp * nb;
   double part = 0.0;
-  for (int j = tid; j < nb; j += blockDim.x) part += static_cast<double>(proxy[j]);
-  const float mean = __fdiv_rn(__double2float_rn(block_sum_f64(part, red)), static_cast<float>(nb));
+  for (int j = lane; j < nb; j += 32) part += static_cast<double>(pr[j]);
+  const float mean = __fdiv_rn(__double2float_rn(warp_sum_f64(part)), static_cast<float>(nb));
   part = 0.0;
-  for (int j = tid; j < nb; j += blockDim.x) {
-    const float dv = __fsub_rn(proxy[j], mean);
+  for (int j = lane; j < nb; j += 32) {
+    const float dv = __fsub_rn(pr[j], mean);
     part += static_cast<double>(__fmul_rn(dv, dv));
   }
-  const float var = __fdiv_rn(__double2float_rn(block_sum_f64(part, red)), static_cast<float>(nb));
+  const float var = __fdiv_rn(__double2float_rn(warp_sum_f64(part)), static_cast<float>(nb));
   const float thr = __fadd_rn(mean, __fmul_rn(tau, __fsqrt_rn(var)));
-  if (tid == 0 && thresh_out) thresh_out[static_cast<int64_t>(g) * nqb + i] = thr;
-  const int qb_kv = (i * q_block) / br;
-  for (int j = tid; j < nb; j += blockDim.x) {
-    const bool k = (score[j] > thr) || (abs(qb_kv - j) <= local_blocks) || (j < sink_blocks);
-    keep[(static_cast<int64_t>(g) * nqb + i) * nb + j] = k ? 1 : 0;
+  if (lane == 0 && thresh_out) thresh_out[static_cast<int64_t>(g) * nqb + qi] = thr;
+  const int qb_kv = (qi * q_block) / br;
+  uint8_t* krow = keep + (static_cast<int64_t>(g) * nqb + qi) * nb;
+  for (int j = lane; j < nb; j += 32) {
+    const bool k = (sc[j] > thr) || (abs(qb_kv - j) <= local_blocks) || (j < sink_blocks);
+    krow[j] = k ? 1 : 0;
   }
 }
 
@@ -729,13 +733,22 @@ cudaError_t launch_route_tiles(const float* k_mean, const float* v_mean, int G, 
 cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st) {
   const int nqb = p.n_pad / p.q_block;
   const int nb = p.n_pad / p.block_rows;
-  const size_t smem = 2 * static_cast<size_t>(nb) * sizeof(float);
+  const dim3 grid((nqb + kRouteQB - 1) / kRouteQB, p.G);
+  const size_t smem = (2 * static_cast<size_t>(kRouteRows) * (p.D + 1) + 2 * static_cast<size_t>(kRouteQB) * nb) *
+                      sizeof(float);
+  // above 48 KB of dynamic shared memory from N = 32K tokens on
+  cudaError_t e = cudaFuncSetAttribute(route_mask_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(route_mask_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
   if (p.D == 128) {
-    route_mask_kernel<128><<<dim3(nqb, p.G), 256, smem, st>>>(
+    route_mask_kernel<128><<<grid, 256, smem, st>>>(
         p.k_mean, p.q_cent, p.q_bar, nqb, nb, p.q_block, p.block_rows, p.tau, p.local_blocks,
         p.sink_blocks, p.sm_scale, p.keep, p.thresh);
   } else {
-    route_mask_kernel<64><<<dim3(nqb, p.G), 256, smem, st>>>(
+    route_mask_kernel<64><<<grid, 256, smem, st>>>(
         p.k_mean, p.q_cent, p.q_bar, nqb, nb, p.q_block, p.block_rows, p.tau, p.local_blocks,
         p.sink_blocks, p.sm_scale, p.keep, p.thresh);
   }
