@@ -361,19 +361,16 @@ __global__ void __launch_bounds__(512, 2) quant_v_kernel(VArgs a) {
 
 // ---------------------------------------------------------------------------
 // Routing threshold + keep mask (triton_attn.py:449-459 and :716-735).
-// One CTA per (head, kRouteQB routing query blocks); warp w owns query block
-// blockIdx.x * kRouteQB + w.  The head's k_mean rows stream through shared
-// memory 32 at a time (row stride D + 1 floats: lane r reading row r at a
-// common channel hits bank (r + d) % 32), next to their bf16 roundings, so
-// each row is read from L2 once per kRouteQB query blocks.  Lane r of warp w
-// forms both float64 dots of (query block w, KV block r): the threshold proxy
-// fp32(q_cent . k_mean_j) * scale and the routing score
-// fp32(q_bar . bf16(k_mean_j)) / q_block.  Each dot is summed in float64 and
-// rounded once, so its fp32 value does not depend on the order of the
-// partial sums.
+// One CTA per (head, kRouteQB routing query blocks).  Thread t takes KV
+// blocks t, t + 256, ...: it reads its k_mean row once (16-byte loads, the
+// row's lines stay in L1 across the four-channel steps) and forms the float64
+// dots of that row with all kRouteQB query blocks (q vectors as shared-memory
+// broadcasts): the threshold proxy fp32(q_cent . k_mean_j) * scale and the
+// routing score fp32(q_bar . bf16(k_mean_j)) / q_block.  Each dot is summed
+// in float64 and rounded once, so its fp32 value does not depend on the order
+// of the partial sums.  Warp w then reduces the threshold of query block w.
 // ---------------------------------------------------------------------------
 constexpr int kRouteQB = 8;
-constexpr int kRouteRows = 32;
 
 __device__ __forceinline__ double warp_sum_f64(double v) {
 #pragma unroll
@@ -388,54 +385,53 @@ __global__ void __launch_bounds__(256) route_mask_kernel(const float* __restrict
                                                          int br, float tau, int local_blocks, int sink_blocks,
                                                          float sm_scale, uint8_t* __restrict__ keep,
                                                          float* __restrict__ thresh_out) {
-  constexpr int RS = D + 1;                      // padded row stride of the staged k_mean rows
-  extern __shared__ float rsm[];                 // kms, kbs [kRouteRows][RS]; proxy, score [kRouteQB][nb]
-  __shared__ float qcs[kRouteQB][D], qbs[kRouteQB][D];
-  float* kms = rsm;
-  float* kbs = rsm + kRouteRows * RS;
-  float* proxy = kbs + kRouteRows * RS;
-  float* score = proxy + kRouteQB * nb;
+  extern __shared__ float rsm[];                 // proxy, score [kRouteQB][nb]
+  __shared__ __align__(16) float qcs[kRouteQB][D];
+  __shared__ __align__(16) float qbs[kRouteQB][D];
+  float* proxy = rsm;
+  float* score = rsm + kRouteQB * nb;
   const int g = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qi = blockIdx.x * kRouteQB + warp;   // this warp's routing query block
   for (int e = tid; e < kRouteQB * D; e += blockDim.x) {
     const int w = e / D, d = e % D, i = blockIdx.x * kRouteQB + w;
     const bool ok = i < nqb;
     qcs[w][d] = ok ? q_cent[(static_cast<int64_t>(g) * nqb + i) * D + d] : 0.f;
     qbs[w][d] = ok ? q_bar[(static_cast<int64_t>(g) * nqb + i) * D + d] : 0.f;
   }
+  __syncthreads();
   const float inv_q = static_cast<float>(q_block);
-  const float* km_head = k_mean + static_cast<int64_t>(g) * nb * D;
-  for (int j0 = 0; j0 < nb; j0 += kRouteRows) {
-    const int rows = min(kRouteRows, nb - j0);
-    __syncthreads();   // previous chunk consumed (and the q vectors staged)
-    for (int e = tid; e < rows * D; e += blockDim.x) {
-      const int r = e / D, d = e % D;
-      const float v = km_head[static_cast<int64_t>(j0 + r) * D + d];
-      kms[r * RS + d] = v;
-      kbs[r * RS + d] = bf16_round(v);
-    }
-    __syncthreads();
-    if (lane < rows) {
-      const float* kr = kms + lane * RS;
-      const float* br_ = kbs + lane * RS;
-      // two partial sums per dot (even / odd channels) keep two float64 FMA
-      // chains in flight; the sum stays one float64 value rounded once
-      double d1a = 0.0, d1b = 0.0, d2a = 0.0, d2b = 0.0;
-#pragma unroll 8
-      for (int d = 0; d < D; d += 2) {
-        d1a = fma(static_cast<double>(qcs[warp][d]), static_cast<double>(kr[d]), d1a);
-        d1b = fma(static_cast<double>(qcs[warp][d + 1]), static_cast<double>(kr[d + 1]), d1b);
-        d2a = fma(static_cast<double>(qbs[warp][d]), static_cast<double>(br_[d]), d2a);
-        d2b = fma(static_cast<double>(qbs[warp][d + 1]), static_cast<double>(br_[d + 1]), d2b);
+  for (int j = tid; j < nb; j += blockDim.x) {
+    const float* km = k_mean + (static_cast<int64_t>(g) * nb + j) * D;
+    double d1[kRouteQB], d2[kRouteQB];
+#pragma unroll
+    for (int w = 0; w < kRouteQB; ++w) d1[w] = d2[w] = 0.0;
+#pragma unroll 2
+    for (int d = 0; d < D; d += 4) {
+      const float4 kv = *reinterpret_cast<const float4*>(km + d);
+      const float kf[4] = {kv.x, kv.y, kv.z, kv.w};
+      const float kb[4] = {bf16_round(kv.x), bf16_round(kv.y), bf16_round(kv.z), bf16_round(kv.w)};
+#pragma unroll
+      for (int w = 0; w < kRouteQB; ++w) {
+        const float4 c4 = *reinterpret_cast<const float4*>(&qcs[w][d]);
+        const float4 b4 = *reinterpret_cast<const float4*>(&qbs[w][d]);
+        const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          d1[w] = fma(static_cast<double>(cv[e]), static_cast<double>(kf[e]), d1[w]);
+          d2[w] = fma(static_cast<double>(bv[e]), static_cast<double>(kb[e]), d2[w]);
+        }
       }
-      proxy[warp * nb + j0 + lane] = __fmul_rn(__double2float_rn(d1a + d1b), sm_scale);
-      score[warp * nb + j0 + lane] = __fdiv_rn(__double2float_rn(d2a + d2b), inv_q);
+    }
+#pragma unroll
+    for (int w = 0; w < kRouteQB; ++w) {
+      proxy[w * nb + j] = __fmul_rn(__double2float_rn(d1[w]), sm_scale);
+      score[w * nb + j] = __fdiv_rn(__double2float_rn(d2[w]), inv_q);
     }
   }
-  __syncwarp();
+  __syncthreads();
+  const int qi = blockIdx.x * kRouteQB + warp;   // this warp's routing query block
   if (qi >= nqb) return;
-  // threshold of this warp's query block: mean + tau * std of its proxies
+  // threshold of the query block: mean + tau * std of its proxies
   const float* pr = proxy + warp * nb;
   const float* sc = score + warp * nb;
   double part = 0.0;
@@ -734,9 +730,8 @@ cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st) {
   const int nqb = p.n_pad / p.q_block;
   const int nb = p.n_pad / p.block_rows;
   const dim3 grid((nqb + kRouteQB - 1) / kRouteQB, p.G);
-  const size_t smem = (2 * static_cast<size_t>(kRouteRows) * (p.D + 1) + 2 * static_cast<size_t>(kRouteQB) * nb) *
-                      sizeof(float);
-  // above 48 KB of dynamic shared memory from N = 32K tokens on
+  const size_t smem = 2 * static_cast<size_t>(kRouteQB) * nb * sizeof(float);
+  // above 48 KB of dynamic shared memory from 768 KV blocks on
   cudaError_t e = cudaFuncSetAttribute(route_mask_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e == cudaSuccess)
