@@ -3,22 +3,32 @@
 Every stage of the path is independent per (b, h) unit: the V-Smooth
 permutation (grouping.py:160-186), the smooth-K mean (triton_attn.py:546),
 the block statistics and the kernel grid (triton_attn.py:804) are all per
-head.  Rank r of P therefore owns the contiguous unit range
-[r*ceil(U/P), min(U, (r+1)*ceil(U/P))) of the flattened B*H axis, computes it
-with the CUDA path, and, when the caller needs the whole tensor, one NCCL
-all-gather assembles the (B, H, N, D) output.  There is no other exchange.
+head.  So the units are dealt out to the ranks with no exchange, and only
+when the caller needs the whole tensor do NCCL all-gathers assemble the
+(B, H, N, D) output.
 
-The all-gather moves equal slabs of ceil(U/P) units per rank into a padded
-buffer; the padding units (when P does not divide U) are never read.
+Two layouts:
+
+* ``chunk=None``: rank r owns the contiguous range
+  [r*ceil(U/P), min(U, (r+1)*ceil(U/P))) of the flattened B*H axis and one
+  all-gather of equal padded slabs assembles the output after the compute.
+* ``chunk=c``: the units are dealt in rounds of P*c, rank r taking units
+  [i*P*c + r*c, i*P*c + (r+1)*c) of round i.  Round i's slabs then sit next to
+  each other in the output, so its all-gather writes them in place, and it is
+  issued asynchronously while round i+1 computes: the transfer overlaps the
+  remaining heads and only the last round's gather is exposed.
+
+Padding units (past U) are never computed; their output rows are zeros in
+the padded buffer and are never returned.
 """
 
 from __future__ import annotations
 
-from typing import Callable, Optional, Tuple
+from typing import Callable, List, Optional, Tuple
 
 import torch
 
-__all__ = ["shard_units", "vc_attention_sharded"]
+__all__ = ["shard_units", "rank_units", "vc_attention_sharded"]
 
 
 def shard_units(units: int, world: int, rank: int) -> Tuple[int, int]:
@@ -31,7 +41,28 @@ def shard_units(units: int, world: int, rank: int) -> Tuple[int, int]:
     return lo, min(units, lo + per)
 
 
-def _local_units(q, k, v, perm, lo, hi, compute):
+def rank_units(units: int, world: int, rank: int, chunk: Optional[int] = None) -> List[Tuple[int, int]]:
+    """Unit ranges [lo, hi) owned by ``rank``, in output order: one range for
+    ``chunk=None`` (:func:`shard_units`), else one per round of ``world * chunk``
+    units (empty ranges of a partial last round left out)."""
+    if chunk is None:
+        lo, hi = shard_units(units, world, rank)
+        return [(lo, hi)] if hi > lo else []
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    if chunk <= 0:
+        raise ValueError("chunk must be positive")
+    out = []
+    for base in range(0, units, world * chunk):
+        lo = min(units, base + rank * chunk)
+        hi = min(units, lo + chunk)
+        if hi > lo:
+            out.append((lo, hi))
+    return out
+
+
+def _compute_units(q, k, v, perm, lo, hi, compute, dst):
+    """Run ``compute`` on units [lo, hi) and write them to ``dst`` (hi - lo, N, D)."""
     b, h, n, d = q.shape
     g = b * h
     ql = q.reshape(g, n, d)[lo:hi].unsqueeze(0)
@@ -40,21 +71,25 @@ def _local_units(q, k, v, perm, lo, hi, compute):
     pl = None
     if perm is not None:
         pl = perm if perm.shape[0] == 1 else perm[lo:hi]
-    return compute(ql, kl, vl, pl).reshape(hi - lo, n, d)
+    dst.copy_(compute(ql, kl, vl, pl).reshape(hi - lo, n, d))
 
 
 def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                          perm: Optional[torch.Tensor] = None, cfg=None, scale: Optional[float] = None,
-                         group=None, gather: bool = True,
+                         group=None, gather: bool = True, chunk: Optional[int] = None,
                          compute: Optional[Callable] = None) -> torch.Tensor:
     """VC-Attention over this rank's (b, h) units, optionally all-gathered.
 
     q, k, v: (B, H, N, D), the same full tensors on every rank (views are
     sliced, not copied).  perm: (B*H, N) or (1, N) int32, or None.
+    chunk: None (one contiguous range per rank, one gather after the
+    compute) or units per rank per round (round-robin layout, each round's
+    gather overlapping the next round's compute).
     Returns the full (B, H, N, D) output on every rank when ``gather``, else
-    this rank's (hi - lo, N, D) slab (unit range from :func:`shard_units`).
-    ``compute`` (tests only) replaces the CUDA attention call; it receives
-    (1, units, N, D) tensors and the matching permutation rows.
+    this rank's units stacked in output order, (units, N, D), as listed by
+    :func:`rank_units`.  ``compute`` (tests only) replaces the CUDA
+    attention call; it receives (1, units, N, D) tensors and the matching
+    permutation rows.
     """
     import torch.distributed as dist
 
@@ -68,15 +103,40 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     b, h, n, d = q.shape
     units = b * h
-    lo, hi = shard_units(units, world, rank)
-    per = -(-units // world)
-    local = torch.zeros((per, n, d), dtype=q.dtype, device=q.device)
-    if hi > lo:
-        local[: hi - lo] = _local_units(q, k, v, perm, lo, hi, compute)
-    if not gather:
-        return local[: hi - lo]
     if world == 1:
-        return local[:units].reshape(b, h, n, d)
-    full = torch.empty((world * per, n, d), dtype=q.dtype, device=q.device)
-    dist.all_gather_into_tensor(full, local, group=group)
+        chunk = None
+    if chunk is None:
+        lo, hi = shard_units(units, world, rank)
+        per = -(-units // world)
+        local = torch.zeros((per, n, d), dtype=q.dtype, device=q.device)
+        if hi > lo:
+            _compute_units(q, k, v, perm, lo, hi, compute, local[: hi - lo])
+        if not gather:
+            return local[: hi - lo]
+        if world == 1:
+            return local[:units].reshape(b, h, n, d)
+        full = torch.empty((world * per, n, d), dtype=q.dtype, device=q.device)
+        dist.all_gather_into_tensor(full, local, group=group)
+        return full[:units].reshape(b, h, n, d)
+
+    rounds = -(-units // (world * chunk))
+    full = torch.empty((rounds * world * chunk, n, d), dtype=q.dtype, device=q.device) if gather else None
+    mine = []
+    works = []
+    for i in range(rounds):
+        base = i * world * chunk
+        lo = min(units, base + rank * chunk)
+        hi = min(units, lo + chunk)
+        slab = torch.zeros((chunk, n, d), dtype=q.dtype, device=q.device)
+        if hi > lo:
+            _compute_units(q, k, v, perm, lo, hi, compute, slab[: hi - lo])
+            mine.append(slab[: hi - lo])
+        if gather:
+            # every rank issues every round, in the same order, with equal slabs
+            works.append((dist.all_gather_into_tensor(full[base: base + world * chunk], slab, group=group,
+                                                      async_op=True), slab))
+    for w, _ in works:
+        w.wait()
+    if not gather:
+        return torch.cat(mine, 0) if mine else torch.zeros((0, n, d), dtype=q.dtype, device=q.device)
     return full[:units].reshape(b, h, n, d)

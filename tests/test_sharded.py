@@ -11,7 +11,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from comfyui_vc_attention_b200.vc_attention.sharded import shard_units, vc_attention_sharded
+from comfyui_vc_attention_b200.vc_attention.sharded import rank_units, shard_units, vc_attention_sharded
 
 
 def test_shard_units_cover_every_unit_once():
@@ -27,6 +27,21 @@ def test_shard_units_cover_every_unit_once():
         shard_units(4, 2, 2)
 
 
+def test_rank_units_rounds_cover_every_unit_once():
+    for units in (1, 7, 56, 112):
+        for world in (1, 2, 3, 8):
+            for chunk in (None, 1, 3, 14):
+                got = []
+                for r in range(world):
+                    for lo, hi in rank_units(units, world, r, chunk):
+                        assert 0 <= lo < hi <= units and (chunk is None or hi - lo <= chunk)
+                        got.extend(range(lo, hi))
+                assert sorted(got) == list(range(units))
+    # round-robin: round i of world*chunk units, rank r at offset r*chunk
+    assert rank_units(10, 2, 1, 2) == [(2, 4), (6, 8)]
+    assert rank_units(10, 2, 0, 2) == [(0, 2), (4, 6), (8, 10)]
+
+
 def _stand_in(ql, kl, vl, pl):
     # depends on the unit's own data only (and on perm when given)
     out = ql + 2.0 * kl - vl
@@ -35,7 +50,7 @@ def _stand_in(ql, kl, vl, pl):
     return out
 
 
-def _worker(rank, world, port, b, h, n, d, with_perm, ret):
+def _worker(rank, world, port, b, h, n, d, with_perm, ret, chunk=None):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -46,13 +61,15 @@ def _worker(rank, world, port, b, h, n, d, with_perm, ret):
         k = torch.randn(b, h, n, d, generator=g)
         v = torch.randn(b, h, n, d, generator=g)
         perm = torch.stack([torch.randperm(n, generator=g) for _ in range(b * h)]).int() if with_perm else None
-        full = vc_attention_sharded(q, k, v, perm, compute=_stand_in)
+        full = vc_attention_sharded(q, k, v, perm, compute=_stand_in, chunk=chunk)
         ref = _stand_in(q.reshape(1, b * h, n, d), k.reshape(1, b * h, n, d), v.reshape(1, b * h, n, d),
                         perm).reshape(b, h, n, d)
         ok = torch.equal(full, ref)
-        lo, hi = shard_units(b * h, world, rank)
-        part = vc_attention_sharded(q, k, v, perm, compute=_stand_in, gather=False)
-        ok = ok and part.shape[0] == hi - lo and torch.equal(part, ref.reshape(b * h, n, d)[lo:hi])
+        part = vc_attention_sharded(q, k, v, perm, compute=_stand_in, gather=False, chunk=chunk)
+        flat = ref.reshape(b * h, n, d)
+        mine = [flat[lo:hi] for lo, hi in rank_units(b * h, world, rank, chunk)]
+        want = torch.cat(mine, 0) if mine else flat[:0]
+        ok = ok and part.shape == want.shape and torch.equal(part, want)
         ret[rank] = int(ok)
     finally:
         dist.destroy_process_group()
@@ -66,13 +83,15 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("b,h,with_perm", [(2, 3, True), (1, 5, False), (2, 4, True)])
-def test_sharded_gather_matches_unsharded(b, h, with_perm):
+@pytest.mark.parametrize("b,h,with_perm,chunk", [(2, 3, True, None), (1, 5, False, None), (2, 4, True, None),
+                                                 (2, 3, True, 1), (1, 5, False, 2), (2, 4, True, 3)])
+def test_sharded_gather_matches_unsharded(b, h, with_perm, chunk):
     world = 2
     ctx = mp.get_context("spawn")
     ret = ctx.Array("i", [0] * world)
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, b, h, 16, 8, with_perm, ret)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, b, h, 16, 8, with_perm, ret, chunk))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
