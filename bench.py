@@ -411,7 +411,8 @@ def main() -> int:
     from comfyui_vc_attention_b200.vc_attention import _native as N
     from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
     from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
-                                                                          prepare, vc_attention_cuda, sparse_tc_applies)
+                                                                          prepare, vc_attention_cuda, sparse_tc_applies,
+                                                                          vc_attention_host)
     N.lib()
 
     q, k, v = make_inputs_gpu(w, 1234 + rank, dev)
@@ -489,18 +490,15 @@ def main() -> int:
         return 0
 
     # ---- end to end through the public entry point, host buffers ----------
+    # vc_attention_host streams head chunks: copy-in, prepare + attention and
+    # copy-out of consecutive chunks overlap on three streams.
     q_h = q.cpu().pin_memory()
     k_h = k.cpu().pin_memory()
     v_h = v.cpu().pin_memory()
     o_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
     def e2e_step():
-        qd.copy_(q_h, non_blocking=True)
-        kd.copy_(k_h, non_blocking=True)
-        vd.copy_(v_h, non_blocking=True)
-        o = vc_attention_cuda(qd, kd, vd, perm, cfg, scale)
-        o_h.copy_(o, non_blocking=True)
+        vc_attention_host(q_h, k_h, v_h, perm, cfg, scale, out=o_h)
 
     for _ in range(2):
         e2e_step()
@@ -521,7 +519,7 @@ def main() -> int:
         e2e_ms = float(t.item())
     h2d = 3 * q.numel() * q.element_size()
     d2h = q.numel() * q.element_size()
-    del q_h, k_h, v_h, qd, kd, vd
+    del q_h, k_h, v_h
 
     # ---- fidelity (not timed) ---------------------------------------------
     psnr = None

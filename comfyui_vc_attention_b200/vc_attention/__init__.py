@@ -12,7 +12,7 @@ Quick start::
 from .device import DeviceProfile, detect_profile, resolve_backend  # noqa: F401
 from .grouping import GroupingConfig, build_permutation  # noqa: F401
 from .h3 import H3, TAG, H3Profile, estimate_tokens, recommended_config  # noqa: F401
-from .kernels.cuda_attn import vc_attention_cuda, vc_attention_triton  # noqa: F401
+from .kernels.cuda_attn import vc_attention_cuda, vc_attention_host, vc_attention_triton  # noqa: F401
 from .schedule import GroupSchedule, PermutationCache, StepTracker  # noqa: F401
 
 __all__ = [
@@ -20,5 +20,5 @@ __all__ = [
     "GroupingConfig", "build_permutation",
     "H3", "H3Profile", "TAG", "estimate_tokens", "recommended_config",
     "GroupSchedule", "PermutationCache", "StepTracker",
-    "vc_attention_triton", "vc_attention_cuda",
+    "vc_attention_triton", "vc_attention_cuda", "vc_attention_host",
 ]

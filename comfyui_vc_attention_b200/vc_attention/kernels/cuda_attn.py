@@ -27,7 +27,7 @@ import torch
 from .. import _native as N
 from ..grouping import _dtype_code, as_bhnd
 
-__all__ = ["TritonConfig", "Prepared", "has_triton", "has_kernel", "prepare", "restore",
+__all__ = ["TritonConfig", "Prepared", "has_triton", "has_kernel", "prepare", "restore", "vc_attention_host",
            "vc_attention_cuda", "vc_attention_triton", "route_mask"]
 
 LOG2E = 1.4426950408889634
@@ -402,6 +402,92 @@ def attention_status(reset: bool = True):
     N.check("vcattn_attn_status", lib.vcattn_attn_status(ctypes.byref(code), ctypes.byref(where),
                                                           ctypes.byref(block), 1 if reset else 0))
     return code.value, where.value, block.value
+
+
+_HOST_STREAMS = {}
+
+
+def _host_streams(dev: torch.device):
+    """The copy-in, compute and copy-out streams of vc_attention_host, one set
+    per device for the process: the caching allocator keeps freed blocks per
+    stream, so fresh streams on every call would re-allocate (and free) the
+    prepared operands each time."""
+    key = dev.index
+    if key not in _HOST_STREAMS:
+        _HOST_STREAMS[key] = tuple(torch.cuda.Stream(dev) for _ in range(3))
+    return _HOST_STREAMS[key]
+
+
+def vc_attention_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      perm: Optional[torch.Tensor] = None, cfg: Optional[TritonConfig] = None,
+                      scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                      chunk_heads: Optional[int] = None, device=None) -> torch.Tensor:
+    """VC-Attention of host-resident (B, H, N, D) tensors on one GPU.
+
+    The path is independent per (b, h) unit, so the units are streamed in
+    chunks of ``chunk_heads``: while chunk i is prepared and attended on one
+    stream, chunk i+1 is copied in and chunk i-1 copied out on two others
+    (double-buffered device slabs), so the host<->device transfers overlap the
+    compute and each other.  q, k, v: contiguous (pinned for overlap) host
+    tensors; perm: (G, N) or (1, N) int32 on the device, or None; out: a host
+    tensor of q's shape and dtype (allocated pinned when None).  The call
+    returns once ``out`` holds the result.
+    """
+    cfg = cfg or TritonConfig()
+    if q.is_cuda or k.is_cuda or v.is_cuda:
+        raise ValueError("vc_attention_host takes host tensors; use vc_attention_cuda for device tensors")
+    if q.shape != k.shape or q.shape != v.shape or q.dim() != 4 or q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k, v must share a (B, H, N, D) shape and dtype")
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("q, k, v must be contiguous (B, H, N, D) host tensors")
+    b, h, n, d = q.shape
+    g = b * h
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    if out.shape != q.shape or out.dtype != q.dtype or out.is_cuda or not out.is_contiguous():
+        raise ValueError("out must be a contiguous host tensor of q's shape and dtype")
+    c = chunk_heads or max(1, -(-g // 14))   # ~14 chunks: the copies dominate, keep the pipe full
+    if scale is None:
+        scale = d ** -0.5
+    src = [t.reshape(g, n, d) for t in (q, k, v)]
+    dst = out.reshape(g, n, d)
+    cur = torch.cuda.current_stream(dev)
+    s_in, s_comp, s_out = _host_streams(dev)
+    for st in (s_in, s_comp, s_out):
+        st.wait_stream(cur)
+    slab_in = [[torch.empty((c, n, d), dtype=q.dtype, device=dev) for _ in range(3)] for _ in range(2)]
+    slab_out = [torch.empty((c, n, d), dtype=q.dtype, device=dev) for _ in range(2)]
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+    nchunk = -(-g // c)
+    for i in range(nchunk):
+        lo, hi = i * c, min(g, (i + 1) * c)
+        u, slot = hi - lo, i % 2
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(comp_done[slot])     # chunk i-2 no longer reads this slab
+            for t_h, t_d in zip(src, slab_in[slot]):
+                t_d[:u].copy_(t_h[lo:hi], non_blocking=True)
+            in_ready[slot].record(s_in)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(in_ready[slot])
+            if i >= 2:
+                s_comp.wait_event(out_done[slot])    # chunk i-2's result copied out
+            qd, kd, vd = (t[:u].unsqueeze(0) for t in slab_in[slot])
+            pl = None if perm is None else (perm if perm.shape[0] == 1 else perm[lo:hi])
+            res = vc_attention_cuda(qd, kd, vd, pl, cfg, scale)
+            slab_out[slot][:u].copy_(res.reshape(u, n, d))
+            comp_done[slot].record(s_comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(comp_done[slot])
+            dst[lo:hi].copy_(slab_out[slot][:u], non_blocking=True)
+            out_done[slot].record(s_out)
+    for st in (s_in, s_comp, s_out):
+        cur.wait_stream(st)
+    s_out.synchronize()
+    return out
 
 
 vc_attention_triton = vc_attention_cuda

@@ -533,3 +533,24 @@ def test_vc_attention_cuda_nvfp4_entry_point(dev):
     ref = O.attention_codes_nvfp4(O.prepare(qg, kg, vg, perm, block_rows=128), n, 128, 128, 128 ** -0.5,
                                   expcast=True)
     assert O.rel_l2(got, ref) <= 5e-3      # bf16 output rounding
+
+
+# ------------------------------------------------- host-tensor entry point ----
+
+@pytest.mark.parametrize("sparse", [False, True])
+def test_vc_attention_host_matches_device_call(dev, sparse):
+    """The chunk-pipelined host entry point gives the device call's bytes
+    (units are independent; chunks of 4 heads, the last one partial)."""
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, vc_attention_cuda,
+                                                                           vc_attention_host)
+    b, h, n, d = 1, 6, 1024, 128
+    q, k, v = make_qkv(b, h, n, d, seed=31)
+    qt, kt, vt = _bf16(q, dev), _bf16(k, dev), _bf16(v, dev)
+    perm = torch.stack([torch.randperm(n, generator=torch.Generator().manual_seed(i)) for i in range(h)])
+    perm = perm.to(torch.int32).to(dev)
+    cfg = TritonConfig(block_m=64, block_n=128, sparse=sparse, tau=1.3, enable_expcast=True)
+    want = vc_attention_cuda(qt, kt, vt, perm, cfg).cpu()
+    qh, kh, vh = (t.cpu().pin_memory() for t in (qt, kt, vt))
+    got = vc_attention_host(qh, kh, vh, perm, cfg, chunk_heads=4)
+    assert not got.is_cuda and got.shape == want.shape
+    assert torch.equal(got, want)
