@@ -25,7 +25,7 @@ values (``bf16_round``) or as uint16 bit patterns.
 from __future__ import annotations
 
 import math
-from typing import Dict, Optional, Tuple
+from typing import Dict, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -601,12 +601,22 @@ def _tile_from_scores(s, v8_blk, vs_row, mu_row, valid, m_i, l_i, acc, expcast, 
     return m_new, l_i, acc
 
 
+def _row_starts(n: int, block_m: int, row_blocks: Optional[Sequence[int]]):
+    """(index, first row) of the block_m-row query blocks to evaluate: all of
+    them, or only ``row_blocks`` (rows of the others stay zero)."""
+    nqb = -(-n // block_m)
+    idx = range(nqb) if row_blocks is None else sorted(set(int(i) for i in row_blocks))
+    return [(i, i * block_m) for i in idx if 0 <= i < nqb]
+
+
 def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_m: int,
-                    sm_scale: float, expcast: bool = False, beta: float = -0.35) -> np.ndarray:
+                    sm_scale: float, expcast: bool = False, beta: float = -0.35,
+                    row_blocks: Optional[Sequence[int]] = None) -> np.ndarray:
     """The fused kernel's arithmetic in code units (triton_attn.py:203-322):
     s = dot(q8,k8) * (qs*ks) * sm_scale ; P as E4M3 (exp2*448 cast or ExpCast);
     r = sum(P)/448 ; acc = alpha*acc + (P@V8)*vs/448 + r*mu*vs ; O = acc/l.
-    Consumes prepare() output; returns (G, N, D) float32.
+    Consumes prepare() output; returns (G, N, D) float32.  ``row_blocks``
+    restricts the evaluation to those query blocks (full-size spot checks).
     """
     q8 = e4m3_decode(prep["q"])
     k8 = e4m3_decode(prep["k"])
@@ -616,7 +626,7 @@ def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_
     nb = n_pad // block_rows
     out = np.zeros((g, n, d), np.float32)
     for gi in range(g):
-        for sm in range(0, n, block_m):
+        for _, sm in _row_starts(n, block_m, row_blocks):
             em = min(n, sm + block_m)
             rows = em - sm
             m_i = np.full(rows, -np.inf, np.float32)
@@ -672,13 +682,14 @@ def attention_codes_nvfp4(prep: Dict[str, np.ndarray], n: int, block_rows: int, 
 
 
 def attention_sparse_codes(prep, stats, keep, n, block_rows, block_m, sm_scale,
-                           group=16, expcast=False, beta=-0.35) -> np.ndarray:
+                           group=16, expcast=False, beta=-0.35, row_blocks=None) -> np.ndarray:
     """Sparse kernel arithmetic (triton_attn.py:384-501) driven by a given
     routing mask ``keep`` (G, NP/block_m, NB).  Per KV group of ``group``
     blocks: approximated blocks are folded first with their per-row proxy
     score s_ap = (q8 . bf16(k_mean)) * qs * sm_scale, weighted by the block's
     real length, against bf16(p_ap) @ bf16(v_mean); kept blocks then run the
-    exact tile in ascending order.
+    exact tile in ascending order.  ``row_blocks`` restricts the evaluation
+    to those query blocks.
     """
     q8 = e4m3_decode(prep["q"])
     k8 = e4m3_decode(prep["k"])
@@ -690,7 +701,7 @@ def attention_sparse_codes(prep, stats, keep, n, block_rows, block_m, sm_scale,
     nb = n_pad // block_rows
     out = np.zeros((g, n, d), np.float32)
     for gi in range(g):
-        for qi, sm in enumerate(range(0, n, block_m)):
+        for qi, sm in _row_starts(n, block_m, row_blocks):
             em = min(n, sm + block_m)
             rows = em - sm
             m_i = np.full(rows, -np.inf, np.float32)

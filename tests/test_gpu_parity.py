@@ -8,6 +8,7 @@ the reference's own PSNR; a tighter 1e-3 against the oracle of the kernel's
 own code-unit arithmetic.
 """
 
+import functools
 import os
 
 import numpy as np
@@ -554,3 +555,139 @@ def test_vc_attention_host_matches_device_call(dev, sparse):
     got = vc_attention_host(qh, kh, vh, perm, cfg, chunk_heads=4)
     assert not got.is_cuda and got.shape == want.shape
     assert torch.equal(got, want)
+
+
+# ------------------------------------------- BASELINE full sizes (56 x 16K) ----
+#
+# configs[1] (dense, ExpCast) and configs[2] (tau = 1.3 sparse) at their own
+# shape, B=1, H=56, N=16384, D=128, V-Smooth k=64.  The GPU runs every head;
+# the oracle re-derives sampled heads (k-means permutation, prepared codes,
+# routing statistics and mask: bit-exact) and sampled 64-row query blocks of
+# the output (rel-L2 <= REL_L2_CODES).  Size-independent properties cover the
+# rest: every permutation row is a permutation, the output is finite, and the
+# sparse kernel with every block kept equals the dense kernel bit for bit.
+
+FULL_H, FULL_N, FULL_D = 56, 16384, 128
+FULL_HEADS = [0, 37]
+FULL_ROW_BLOCKS = [0, 97, 255]
+
+
+@functools.lru_cache(maxsize=2)
+def _full_pipeline(dev, spatial, seed):
+    """Inputs (host and device) and the GPU permutation, shared by the tests
+    of one config (generating 3 x 117M seeded values takes most of a minute)."""
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
+    q, k, v = make_qkv(1, FULL_H, FULL_N, FULL_D, seed=seed, spatial=spatial)
+    qt, kt, vt = _bf16(q, dev), _bf16(k, dev), _bf16(v, dev)
+    res = build_permutation(vt.view(FULL_H, FULL_N, FULL_D),
+                            GroupingConfig(block_rows=128, iters=3, max_clusters=64))
+    assert res.k == 64
+    perm = res.perm
+    srt = torch.sort(perm.long(), dim=-1).values
+    assert torch.equal(srt, torch.arange(FULL_N, device=dev).expand_as(srt)), "a row is not a permutation"
+    return q, k, v, qt, kt, vt, perm.cpu().numpy()
+
+
+def _oracle_heads(q, k, v, gpu_perm, heads):
+    """Oracle permutation and prepare() of the sampled heads."""
+    sel = (lambda a: a.reshape(FULL_H, FULL_N, FULL_D)[heads])
+    qh, kh, vh = sel(q), sel(k), sel(v)
+    for i, hh in enumerate(heads):
+        perm_o, _, kc, _ = O.build_permutation(vh[i:i + 1], block_rows=128, iters=3, max_clusters=64)
+        assert kc == 64
+        np.testing.assert_array_equal(gpu_perm[hh], perm_o[0], err_msg=f"k-means permutation, head {hh}")
+    return O.prepare(qh, kh, vh, gpu_perm[heads], block_rows=128)
+
+
+def _assert_prepare_heads(p, ref, heads):
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import v_natural
+    d = p.q.shape[-1]
+    np.testing.assert_array_equal(p.q.view(torch.uint8).reshape(FULL_H, -1, d)[heads].cpu().numpy(), ref["q"])
+    np.testing.assert_array_equal(p.k.view(torch.uint8).reshape(FULL_H, -1, d)[heads].cpu().numpy(), ref["k"])
+    np.testing.assert_array_equal(v_natural(p).reshape(FULL_H, -1, d)[heads].cpu().numpy(), ref["v"])
+    for f in ("q_scale", "k_scale", "v_scale", "mu"):
+        got = getattr(p, f).reshape((FULL_H,) + ref[f].shape[1:])[heads].cpu().numpy()
+        np.testing.assert_array_equal(got, ref[f], err_msg=f)
+
+
+def _rows(a, heads):
+    """(len(heads), rows of FULL_ROW_BLOCKS, D) slice of a (G, N, D) array."""
+    idx = np.concatenate([np.arange(i * 64, (i + 1) * 64) for i in FULL_ROW_BLOCKS])
+    return a[heads][:, idx]
+
+
+def test_full_size_config1_dense(dev):
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
+                                                                           attention_status, prepare)
+    q, k, v, qt, kt, vt, perm = _full_pipeline(dev, None, seed=7)
+    p = prepare(qt, kt, vt, _t(perm, dev), block_rows=128, want_v=True)
+    sc = FULL_D ** -0.5
+    out = torch.empty((1, FULL_H, FULL_N, FULL_D), dtype=torch.float32, device=dev)
+    attention_prepared(p, FULL_N, out, sc, TritonConfig(block_n=128, enable_expcast=True), kernel="tc")
+    torch.cuda.synchronize()
+    assert attention_status() == (0, 0, 0), "a bounded wait of the tcgen05 kernel expired"
+    assert bool(torch.isfinite(out).all())
+    got = out.reshape(FULL_H, FULL_N, FULL_D).cpu().numpy()
+
+    ref = _oracle_heads(q, k, v, perm, FULL_HEADS)
+    _assert_prepare_heads(p, ref, FULL_HEADS)
+    codes = O.attention_codes(ref, FULL_N, 128, 64, sc, expcast=True, row_blocks=FULL_ROW_BLOCKS)
+    assert O.rel_l2(_rows(got, FULL_HEADS), _rows(codes, slice(None))) <= REL_L2_CODES
+    # against fp32 SDPA on the same rows (all 16384 keys)
+    qh = q.reshape(FULL_H, FULL_N, FULL_D)[FULL_HEADS]
+    idx = np.concatenate([np.arange(i * 64, (i + 1) * 64) for i in FULL_ROW_BLOCKS])
+    sd = O.sdpa_f32(qh[:, idx], k.reshape(FULL_H, FULL_N, FULL_D)[FULL_HEADS],
+                    v.reshape(FULL_H, FULL_N, FULL_D)[FULL_HEADS])
+    assert O.psnr(_rows(got, FULL_HEADS), sd) > 30.0
+
+
+def test_full_size_config2_sparse(dev):
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
+                                                                           attention_status, prepare)
+    q, k, v, qt, kt, vt, perm = _full_pipeline(dev, (16, 32, 32), seed=9)
+    sc, tau = FULL_D ** -0.5, 1.3
+    pt = _t(perm, dev)
+    p = prepare(qt, kt, vt, pt, block_rows=128, sparse=True, tau=tau, q_block=64, want_v=True)
+    cfg = TritonConfig(block_m=64, block_n=128, sparse=True, tau=tau, enable_expcast=True)
+    out = torch.empty((1, FULL_H, FULL_N, FULL_D), dtype=torch.float32, device=dev)
+    attention_prepared(p, FULL_N, out, sc, cfg, kernel="tc")
+    torch.cuda.synchronize()
+    assert attention_status() == (0, 0, 0), "a bounded wait of the tcgen05 sparse kernel expired"
+    assert bool(torch.isfinite(out).all())
+    keep_all = p.keep.cpu().numpy().astype(bool)
+    assert 0.02 < 1.0 - keep_all.mean() < 0.98, "routing must skip some blocks and keep some"
+    got = out.reshape(FULL_H, FULL_N, FULL_D).cpu().numpy()
+
+    ref = _oracle_heads(q, k, v, perm, FULL_HEADS)
+    _assert_prepare_heads(p, ref, FULL_HEADS)
+    st = O.route_stats(ref, 128, 64, tau, sc)
+    keep_o, _ = O.route_mask(ref, st, FULL_N, 128, 64, sc)
+    nb = FULL_N // 128
+    for f, shp in (("k_mean", (nb, FULL_D)), ("v_mean", (nb, FULL_D)), ("thresh", (FULL_N // 64,))):
+        np.testing.assert_array_equal(getattr(p, f).reshape((FULL_H,) + shp)[FULL_HEADS].cpu().numpy(), st[f],
+                                      err_msg=f)
+    np.testing.assert_array_equal(keep_all[FULL_HEADS], keep_o)
+    codes = O.attention_sparse_codes(ref, st, keep_o, FULL_N, 128, 64, sc, group=16, expcast=True,
+                                     row_blocks=FULL_ROW_BLOCKS)
+    assert O.rel_l2(_rows(got, FULL_HEADS), _rows(codes, slice(None))) <= REL_L2_CODES
+
+
+def test_full_size_sparse_keep_all_equals_dense(dev):
+    """tau -> -inf at configs[2]'s shape: all 56 x 256 x 128 blocks kept, the
+    sparse kernel's output equals the dense kernel's bit for bit."""
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
+                                                                           attention_status, prepare)
+    q, k, v, qt, kt, vt, perm = _full_pipeline(dev, (16, 32, 32), seed=9)
+    pt, sc = _t(perm, dev), FULL_D ** -0.5
+    ps = prepare(qt, kt, vt, pt, block_rows=128, sparse=True, tau=-1000.0, q_block=64, want_v=True)
+    assert bool(ps.keep.bool().all())
+    o_s = torch.empty((1, FULL_H, FULL_N, FULL_D), dtype=torch.bfloat16, device=dev)
+    attention_prepared(ps, FULL_N, o_s, sc, TritonConfig(block_m=64, block_n=128, sparse=True, tau=-1000.0,
+                                                        enable_expcast=True), kernel="tc")
+    del ps
+    pd = prepare(qt, kt, vt, pt, block_rows=128, want_v=True)
+    o_d = torch.empty_like(o_s)
+    attention_prepared(pd, FULL_N, o_d, sc, TritonConfig(block_n=128, enable_expcast=True), kernel="tc")
+    torch.cuda.synchronize()
+    assert attention_status() == (0, 0, 0)
+    assert torch.equal(o_s, o_d)
