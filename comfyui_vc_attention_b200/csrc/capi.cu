@@ -344,6 +344,13 @@ int vcattn_attn_status(int* code, int* where, int* block, int reset) {
     *where = 200 + w3;   // and those of the tcgen05 sparse kernel as 200 + site
     *block = b3;
   }
+  int c4 = 0, w4 = 0, b4 = 0;
+  if (e == cudaSuccess) e = kmeans_tc_status(&c4, &w4, &b4, reset != 0);
+  if (e == cudaSuccess && *code == 0 && c4 != 0) {
+    *code = c4;
+    *where = 300 + w4;   // and those of the tensor-core k-means assignment as 300 + site
+    *block = b4;
+  }
   return cuda_status(e, "vcattn_attn_status");
 }
 

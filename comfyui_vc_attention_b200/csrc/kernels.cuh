@@ -79,6 +79,14 @@ cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st);
 cudaError_t launch_route_tiles(const float* k_mean, const float* v_mean, int G, int nb, uint8_t* tiles,
                                cudaStream_t st);
 cudaError_t launch_kmeans(const KMeansParams& p, cudaStream_t st);
+// Tensor-core nearest-centroid assignment (kmeans_tc.cu): labels identical to
+// the CUDA-core assign.  `maps` holds two CUtensorMap (256 bytes, 64-aligned):
+// the token rows of p.v and the bf16 centroid table cb16 (G, k, 128).
+bool assign_tc_supported(const KMeansParams& p);
+bool assign_tc_maps(const KMeansParams& p, const uint16_t* cb16, void* maps);
+cudaError_t launch_assign_tc(const KMeansParams& p, const void* maps, const float* c2, int32_t* labels,
+                             const int32_t* key_offset, int nkeys, int nchunks, int32_t* counts, cudaStream_t st);
+cudaError_t kmeans_tc_status(int* code, int* where, int* block, bool reset);
 cudaError_t launch_attn_mma(const AttnParams& p, cudaStream_t st);
 cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t st);
 cudaError_t launch_attn_nvfp4(const AttnParams& p, cudaStream_t st);

@@ -26,6 +26,8 @@ struct KmWs {
   int32_t* offsets;
   float* cent;
   float* seeds;
+  uint16_t* cb16;   // (G, k, D) bf16 centroids: B operand of the tensor-core assign
+  float* c2;        // (G, k) |c|^2, sequential fp32 over channels
 };
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -39,7 +41,9 @@ KmWs carve(void* base, int G, int N, int D, int k, int nkeys) {
   w.counts = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * G * nk * nchunks);
   w.offsets = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * G * nk * nchunks);
   w.cent = reinterpret_cast<float*>(p); p += align256(sizeof(float) * G * static_cast<size_t>(k) * D);
-  w.seeds = reinterpret_cast<float*>(p);
+  w.seeds = reinterpret_cast<float*>(p); p += align256(sizeof(float) * G * static_cast<size_t>(k) * D);
+  w.cb16 = reinterpret_cast<uint16_t*>(p); p += align256(sizeof(uint16_t) * G * static_cast<size_t>(k) * D);
+  w.c2 = reinterpret_cast<float*>(p);
   return w;
 }
 
@@ -51,13 +55,28 @@ __device__ __forceinline__ float load_bf16_value(const vcattn_bhnd& v, int b, in
   else return bf16_round(static_cast<const float*>(v.data)[off]);
 }
 
+// The bf16 copy of centroid (g, c) and its |c|^2 as a sequential fp32 FMA
+// chain over channels (what the assignment subtracts).  One CTA of D threads,
+// thread d holding channel d.
+__device__ __forceinline__ void centroid_side(float val, int D, int64_t row, uint16_t* cb16, float* c2) {
+  __shared__ float sq[128];
+  const int d = threadIdx.x;
+  cb16[row * D + d] = static_cast<uint16_t>(__float_as_uint(val) >> 16);   // val holds a bf16 value
+  sq[d] = val;
+  __syncthreads();
+  if (d == 0) {
+    float acc = 0.f;
+    for (int j = 0; j < D; ++j) acc = __fmaf_rn(sq[j], sq[j], acc);
+    c2[row] = acc;
+  }
+}
+
 // grouping.py:71-83: centroid c = bf16(mean of the samples at
-// round(linspace(0, N-1, m))[c*m_per : (c+1)*m_per]).
+// round(linspace(0, N-1, m))[c*m_per : (c+1)*m_per]).  Launched with D threads.
 template <int DT>
 __global__ void seed_kernel(vcattn_bhnd v, int H, int N, int D, int k, int m, int m_per,
-                            float* seeds, float* cent, const uint16_t* warm) {
+                            float* seeds, float* cent, const uint16_t* warm, uint16_t* cb16, float* c2) {
   const int g = blockIdx.y, c = blockIdx.x, d = threadIdx.x;
-  if (d >= D) return;
   const int b = g / H, h = g % H;
   float step = 0.f;
   if (m > 1) step = __fdiv_rn(static_cast<float>(N - 1), static_cast<float>(m - 1));
@@ -75,7 +94,9 @@ __global__ void seed_kernel(vcattn_bhnd v, int H, int N, int D, int k, int m, in
   const float mean = bf16_round(__fdiv_rn(__double2float_rn(s), static_cast<float>(m_per)));
   const int64_t o = (static_cast<int64_t>(g) * k + c) * D + d;
   seeds[o] = mean;
-  cent[o] = warm ? bf16_bits_to_float(warm[o]) : mean;
+  const float cv = warm ? bf16_bits_to_float(warm[o]) : mean;
+  cent[o] = cv;
+  centroid_side(cv, D, static_cast<int64_t>(g) * k + c, cb16, c2);
 }
 
 // Row of D bf16 values packed two per register.
@@ -234,14 +255,14 @@ __global__ void __launch_bounds__(kAssignThreads) scatter_kernel(
 }
 
 // grouping.py:103-124: fp32 sums in token order, / max(count, 1), re-seed
-// clusters with count <= 1, bf16.  One CTA per (cluster, head), thread = channel.
+// clusters with count <= 1, bf16.  One CTA per (cluster, head), D threads,
+// thread = channel.
 template <int DT>
 __global__ void update_kernel(vcattn_bhnd v, int H, int N, int D, int k, int nchunks,
                               const int32_t* __restrict__ offsets, const int32_t* __restrict__ sorted,
                               const float* __restrict__ seeds, float* __restrict__ cent,
-                              uint16_t* __restrict__ cent_out) {
+                              uint16_t* __restrict__ cent_out, uint16_t* __restrict__ cb16, float* __restrict__ c2) {
   const int g = blockIdx.y, c = blockIdx.x, d = threadIdx.x;
-  if (d >= D) return;
   const int b = g / H, h = g % H;
   const int64_t base = static_cast<int64_t>(g) * k * nchunks;
   const int start = offsets[base + static_cast<int64_t>(c) * nchunks];
@@ -264,6 +285,7 @@ __global__ void update_kernel(vcattn_bhnd v, int H, int N, int D, int k, int nch
   const float nv = (cnt <= 1) ? seeds[o] : bf16_round(__fdiv_rn(acc, cntc));
   cent[o] = nv;
   if (cent_out) cent_out[o] = __bfloat16_as_ushort(__float2bfloat16_rn(nv));
+  centroid_side(nv, D, static_cast<int64_t>(g) * k + c, cb16, c2);
 }
 
 __global__ void copy_centroids_kernel(const float* __restrict__ cent, uint16_t* __restrict__ out, int64_t n) {
@@ -281,13 +303,24 @@ cudaError_t kmeans_impl(const KMeansParams& p, cudaStream_t st) {
   int32_t* labels = p.labels_out ? p.labels_out : w.labels;
   const int m = (p.N < 4 * k) ? p.N : 4 * k;          // init_samples_per_centroid = 4
   const int m_per = (m / k) > 1 ? (m / k) : 1;
-  seed_kernel<DT><<<dim3(k, G), D, 0, st>>>(*p.v, p.H, p.N, D, k, m, m_per, w.seeds, w.cent, p.warm);
+  seed_kernel<DT><<<dim3(k, G), D, 0, st>>>(*p.v, p.H, p.N, D, k, m, m_per, w.seeds, w.cent, p.warm, w.cb16,
+                                            w.c2);
   const dim3 agrid((p.N + kAssignThreads - 1) / kAssignThreads, G, 1);
+  // Tensor-core assignment when the token rows can be tiled by TMA (bf16,
+  // D = 128); the CUDA-core kernel otherwise.  Both give the same labels.
+  alignas(64) unsigned char maps[256];
+  const bool tc = assign_tc_supported(p) && assign_tc_maps(p, w.cb16, maps);
+  cudaError_t err = cudaSuccess;
   auto sort_pass = [&](const int32_t* koff, int nkey, int32_t* out_sorted) {
     const size_t cnt_bytes = sizeof(int32_t) * static_cast<size_t>(G) * nkey * nchunks;
     cudaMemsetAsync(w.counts, 0, cnt_bytes, st);
-    assign_kernel<DT, D><<<agrid, kAssignThreads, 0, st>>>(
-        *p.v, p.H, p.N, k, w.cent, labels, koff, nkey, nchunks, w.counts);
+    if (tc) {
+      const cudaError_t e = launch_assign_tc(p, maps, w.c2, labels, koff, nkey, nchunks, w.counts, st);
+      if (e != cudaSuccess && err == cudaSuccess) err = e;
+    } else {
+      assign_kernel<DT, D><<<agrid, kAssignThreads, 0, st>>>(
+          *p.v, p.H, p.N, k, w.cent, labels, koff, nkey, nchunks, w.counts);
+    }
     scan_kernel<<<G, 1024, 0, st>>>(w.counts, w.offsets, static_cast<int64_t>(nkey) * nchunks);
     scatter_kernel<<<dim3(agrid.x, G), kAssignThreads, 0, st>>>(labels, koff, p.N, nkey, nchunks,
                                                               w.offsets, out_sorted);
@@ -296,11 +329,12 @@ cudaError_t kmeans_impl(const KMeansParams& p, cudaStream_t st) {
   for (int it = 0; it < iters; ++it) {
     sort_pass(nullptr, k, p.perm_out);
     update_kernel<DT><<<dim3(k, G), D, 0, st>>>(*p.v, p.H, p.N, D, k, nchunks, w.offsets, p.perm_out,
-                                               w.seeds, w.cent, nullptr);
+                                               w.seeds, w.cent, nullptr, w.cb16, w.c2);
   }
   copy_centroids_kernel<<<static_cast<unsigned>((static_cast<int64_t>(G) * k * D + 255) / 256), 256, 0, st>>>(
       w.cent, p.centroids_out, static_cast<int64_t>(G) * k * D);
   sort_pass(p.key_offset, nkeys, p.perm_out);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 
@@ -311,7 +345,9 @@ size_t kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys) {
   const size_t nk = static_cast<size_t>(nkeys > k ? nkeys : k);
   return align256(sizeof(int32_t) * G * static_cast<size_t>(N)) +
          2 * align256(sizeof(int32_t) * G * nk * nchunks) +
-         2 * align256(sizeof(float) * G * static_cast<size_t>(k) * D) + 256;
+         2 * align256(sizeof(float) * G * static_cast<size_t>(k) * D) +
+         align256(sizeof(uint16_t) * G * static_cast<size_t>(k) * D) + align256(sizeof(float) * G * static_cast<size_t>(k)) +
+         256;
 }
 
 cudaError_t launch_kmeans(const KMeansParams& p, cudaStream_t st) {

@@ -99,7 +99,11 @@ VCATTN_API void vcattn_inject_fault(const char* entry_point);
  *    the cluster label before the stable sort (modality / padding keys,
  *    grouping.py:176-183); nkeys bounds the keys (k when key_offset is NULL).
  * Outputs: centroids_out (G,k,D) bf16 bits, perm_out (G,N) int32, and
- *    labels_out (G,N) int32 (may be NULL). */
+ *    labels_out (G,N) int32 (may be NULL).
+ * bf16 input with D = 128 is assigned on the tensor cores (tcgen05, labels
+ * certified equal to the sequential-FMA definition; bounded waits report
+ * through vcattn_attn_status as 300 + site); other inputs on the CUDA cores.
+ * Environment VCATTN_KMEANS_SIMT=1 forces the CUDA-core assignment. */
 VCATTN_API size_t vcattn_kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys);
 VCATTN_API int vcattn_kmeans(const vcattn_bhnd* v, int dtype, int B, int H, int N, int D,
                   int k, int iters, const uint16_t* warm_centroids,
@@ -215,8 +219,10 @@ VCATTN_API int vcattn_attn_fp8_mma(const uint8_t* q8, const float* q_scale, cons
                     void* stream);
 
 /* Device status word of the tcgen05 kernels: code 0 = ok, 1 = a bounded wait
- * expired (the kernel gave up and returned); where = which wait; block = the
- * first failing CTA.  Synchronises the current device.  reset != 0 clears it. */
+ * expired (the kernel gave up and returned); where = which wait (NVFP4
+ * attention 100 + site, sparse attention 200 + site, the tensor-core k-means
+ * assignment of vcattn_kmeans 300 + site); block = the first failing CTA.
+ * Synchronises the current device.  reset != 0 clears it. */
 VCATTN_API int vcattn_attn_status(int* code, int* where, int* block, int reset);
 
 /* ---- fused block-sparse FP8 attention: triton_attn.py:384-501 ----------

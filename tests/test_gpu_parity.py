@@ -157,6 +157,33 @@ def test_kmeans_input_layouts_agree(dev):
         assert torch.equal(lab, lab_a) and torch.equal(cent, cent_a) and torch.equal(perm, perm_a)
 
 
+@pytest.mark.parametrize("n,k_clusters,iters", [(16384, 512, 2), (5000, 300, 1), (4096, 1000, 1), (3000, 37, 2)])
+def test_kmeans_tensor_core_assign_equals_cuda_core(dev, n, k_clusters, iters, monkeypatch):
+    """bf16 D=128 input takes the tcgen05 assignment (certified argmax); the
+    CUDA-core assignment (VCATTN_KMEANS_SIMT=1) is the definition it must
+    reproduce: labels, centroids and permutation bit for bit, for k in one
+    chunk, two chunks and two TMEM passes, and a head against the oracle."""
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import attention_status
+    q, k, v = make_qkv(1, 2, n, 128, seed=n + k_clusters)
+    vt = _bf16(v.reshape(2, n, 128), dev)
+    br = max(1, n // k_clusters)          # ceil(n / br) >= k_clusters: k = max_clusters
+    cfg = GroupingConfig(block_rows=br, iters=iters, max_clusters=k_clusters)
+    res_tc = build_permutation(vt, cfg)
+    assert attention_status() == (0, 0, 0), "a bounded wait of the tensor-core assignment expired"
+    monkeypatch.setenv("VCATTN_KMEANS_SIMT", "1")
+    res_ref = build_permutation(vt, cfg)
+    assert res_tc.k == res_ref.k == k_clusters
+    assert torch.equal(res_tc.labels, res_ref.labels)
+    assert torch.equal(res_tc.centroids, res_ref.centroids)
+    assert torch.equal(res_tc.perm, res_ref.perm)
+    if n <= 5000:
+        perm_o, cent_o, _, lab_o = O.build_permutation(v.reshape(2, n, 128)[:1], block_rows=br, iters=iters,
+                                                       max_clusters=k_clusters)
+        assert np.array_equal(res_tc.labels[:1].cpu().numpy(), lab_o)
+        assert np.array_equal(res_tc.perm[:1].cpu().numpy(), perm_o)
+
+
 # --------------------------------------------------------------- prepare ----
 
 def _prep_gpu(q, k, v, perm, br, dev, **kw):
