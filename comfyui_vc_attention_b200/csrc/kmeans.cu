@@ -28,6 +28,7 @@ struct KmWs {
   float* seeds;
   uint16_t* cb16;   // (G, k, D) bf16 centroids: B operand of the tensor-core assign
   float* c2;        // (G, k) |c|^2, sequential fp32 over channels
+  int32_t* tsum;    // (G, scan tiles) tile sums of the counting-sort scan
 };
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -43,7 +44,8 @@ KmWs carve(void* base, int G, int N, int D, int k, int nkeys) {
   w.cent = reinterpret_cast<float*>(p); p += align256(sizeof(float) * G * static_cast<size_t>(k) * D);
   w.seeds = reinterpret_cast<float*>(p); p += align256(sizeof(float) * G * static_cast<size_t>(k) * D);
   w.cb16 = reinterpret_cast<uint16_t*>(p); p += align256(sizeof(uint16_t) * G * static_cast<size_t>(k) * D);
-  w.c2 = reinterpret_cast<float*>(p);
+  w.c2 = reinterpret_cast<float*>(p); p += align256(sizeof(float) * G * static_cast<size_t>(k));
+  w.tsum = reinterpret_cast<int32_t*>(p);
   return w;
 }
 
@@ -208,31 +210,98 @@ __global__ void __launch_bounds__(kAssignThreads) assign_kernel(
   }
 }
 
-// Exclusive scan of counts[g] in (key, chunk) order: one CTA per head.
-__global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ counts,
-                                                    int32_t* __restrict__ offsets, int64_t len) {
+// Exclusive scan of counts[g] in (key, chunk) order, per head, in three
+// data-parallel steps over tiles of kScanTile entries: tile sums, a scan of
+// the tile sums per head, then each tile's scan plus its offset.
+constexpr int kScanThreads = 256;
+constexpr int kScanPer = 16;                            // entries per thread
+constexpr int kScanTile = kScanThreads * kScanPer;      // 4096
+
+__device__ __forceinline__ int32_t block_sum256(int32_t x) {
+  __shared__ int32_t ws[kScanThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = x;
+  __syncthreads();
+  int32_t t = 0;
+#pragma unroll
+  for (int w = 0; w < kScanThreads / 32; ++w) t += ws[w];
+  return t;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_tile_sum_kernel(const int32_t* __restrict__ counts,
+                                                                     int64_t len, int ntiles,
+                                                                     int32_t* __restrict__ tsum) {
+  const int g = blockIdx.y, tile = blockIdx.x;
+  const int32_t* c = counts + static_cast<int64_t>(g) * len;
+  const int64_t base = static_cast<int64_t>(tile) * kScanTile;
+  int32_t x = 0;
+#pragma unroll
+  for (int j = 0; j < kScanPer; ++j) {
+    const int64_t i = base + j * kScanThreads + threadIdx.x;   // coalesced
+    if (i < len) x += c[i];
+  }
+  x = block_sum256(x);
+  if (threadIdx.x == 0) tsum[static_cast<int64_t>(g) * ntiles + tile] = x;
+}
+
+// Exclusive scan of the ntiles tile sums of one head, in place (one CTA per head).
+__global__ void __launch_bounds__(1024) scan_tiles_kernel(int32_t* __restrict__ tsum, int ntiles) {
   __shared__ int32_t part[1024];
-  const int g = blockIdx.x;
+  int32_t* ts = tsum + static_cast<int64_t>(blockIdx.x) * ntiles;
+  int32_t carry = 0;
+  for (int b = 0; b < ntiles; b += 1024) {
+    const int i = b + threadIdx.x;
+    const int32_t v = i < ntiles ? ts[i] : 0;
+    part[threadIdx.x] = v;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {
+      const int32_t x = (threadIdx.x >= off) ? part[threadIdx.x - off] : 0;
+      __syncthreads();
+      part[threadIdx.x] += x;
+      __syncthreads();
+    }
+    if (i < ntiles) ts[i] = carry + part[threadIdx.x] - v;
+    const int32_t total = part[1023];
+    __syncthreads();
+    carry += total;
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const int32_t* __restrict__ counts,
+                                                                  int64_t len, int ntiles,
+                                                                  const int32_t* __restrict__ tsum,
+                                                                  int32_t* __restrict__ offsets) {
+  __shared__ int32_t wsum[kScanThreads / 32];
+  const int g = blockIdx.y, tile = blockIdx.x;
   const int32_t* c = counts + static_cast<int64_t>(g) * len;
   int32_t* o = offsets + static_cast<int64_t>(g) * len;
-  const int64_t per = (len + blockDim.x - 1) / blockDim.x;
-  const int64_t s = threadIdx.x * per;
-  const int64_t e = min(len, s + per);
-  int32_t local = 0;
-  for (int64_t i = s; i < e; ++i) local += c[i];
-  part[threadIdx.x] = local;
-  __syncthreads();
-  // Hillis-Steele inclusive scan over the 1024 partial sums.
-  for (int off = 1; off < 1024; off <<= 1) {
-    const int32_t x = (threadIdx.x >= off) ? part[threadIdx.x - off] : 0;
-    __syncthreads();
-    part[threadIdx.x] += x;
-    __syncthreads();
+  const int64_t base = static_cast<int64_t>(tile) * kScanTile + static_cast<int64_t>(threadIdx.x) * kScanPer;
+  int32_t v[kScanPer];
+  int32_t run = 0;
+#pragma unroll
+  for (int j = 0; j < kScanPer; ++j) {
+    v[j] = (base + j < len) ? c[base + j] : 0;
+    run += v[j];
   }
-  int32_t run = part[threadIdx.x] - local;
-  for (int64_t i = s; i < e; ++i) {
-    o[i] = run;
-    run += c[i];
+  // exclusive scan of the thread totals: warp shuffles, then warp totals
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int32_t inc = run;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += y;
+  }
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  int32_t wpre = 0;
+#pragma unroll
+  for (int w = 0; w < kScanThreads / 32; ++w) wpre += (w < warp) ? wsum[w] : 0;
+  int32_t acc = tsum[static_cast<int64_t>(g) * ntiles + tile] + wpre + inc - run;
+#pragma unroll
+  for (int j = 0; j < kScanPer; ++j) {
+    if (base + j < len) o[base + j] = acc;
+    acc += v[j];
   }
 }
 
@@ -321,7 +390,11 @@ cudaError_t kmeans_impl(const KMeansParams& p, cudaStream_t st) {
       assign_kernel<DT, D><<<agrid, kAssignThreads, 0, st>>>(
           *p.v, p.H, p.N, k, w.cent, labels, koff, nkey, nchunks, w.counts);
     }
-    scan_kernel<<<G, 1024, 0, st>>>(w.counts, w.offsets, static_cast<int64_t>(nkey) * nchunks);
+    const int64_t len = static_cast<int64_t>(nkey) * nchunks;
+    const int ntiles = static_cast<int>((len + kScanTile - 1) / kScanTile);
+    scan_tile_sum_kernel<<<dim3(ntiles, G), kScanThreads, 0, st>>>(w.counts, len, ntiles, w.tsum);
+    scan_tiles_kernel<<<G, 1024, 0, st>>>(w.tsum, ntiles);
+    scan_apply_kernel<<<dim3(ntiles, G), kScanThreads, 0, st>>>(w.counts, len, ntiles, w.tsum, w.offsets);
     scatter_kernel<<<dim3(agrid.x, G), kAssignThreads, 0, st>>>(labels, koff, p.N, nkey, nchunks,
                                                               w.offsets, out_sorted);
   };
@@ -347,7 +420,7 @@ size_t kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys) {
          2 * align256(sizeof(int32_t) * G * nk * nchunks) +
          2 * align256(sizeof(float) * G * static_cast<size_t>(k) * D) +
          align256(sizeof(uint16_t) * G * static_cast<size_t>(k) * D) + align256(sizeof(float) * G * static_cast<size_t>(k)) +
-         256;
+         align256(sizeof(int32_t) * G * ((nk * nchunks + 4095) / 4096)) + 256;
 }
 
 cudaError_t launch_kmeans(const KMeansParams& p, cudaStream_t st) {

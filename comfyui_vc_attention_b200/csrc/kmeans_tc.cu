@@ -105,24 +105,32 @@ __host__ __device__ constexpr uint32_t idesc_bf16_kk(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-// Byte address of channel pair (2i, 2i+1) of row r in a 128-byte-swizzled
-// K-major tile whose two 64-channel halves are `half_bytes` apart.
-__device__ __forceinline__ const uint32_t* swz_pair(const uint8_t* tile, int half_bytes, int r, int i) {
-  const int ch = 2 * i, half = ch >> 6, byte = (ch & 63) * 2;
-  const int chunk = (byte >> 4) ^ (r & 7);
-  return reinterpret_cast<const uint32_t*>(tile + half * half_bytes + r * 128 + (chunk << 4) + (byte & 15));
+// Channels 8c .. 8c+7 (c = 0..15) of row r of a 128-byte-swizzled K-major
+// tile whose two 64-channel halves are `half_bytes` apart: the 16-byte chunk
+// c % 8 of the row sits at chunk position (c % 8) ^ (r % 8).
+__device__ __forceinline__ uint4 swz_chunk(const uint8_t* tile, int half_bytes, int r, int c) {
+  const int pos = (c & 7) ^ (r & 7);
+  return *reinterpret_cast<const uint4*>(tile + (c >> 3) * half_bytes + r * 128 + (pos << 4));
 }
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
 // Sequential fp32 FMA chain of a token row and a centroid row (both bf16 in
 // swizzled shared memory), channels in increasing order.
 __device__ __noinline__ float exact_dot(const uint8_t* ta, int r, const uint8_t* tb, int cr) {
   float acc = 0.f;
-#pragma unroll 4
-  for (int i = 0; i < 64; ++i) {
-    const uint32_t va = *swz_pair(ta, kHalfA, r, i);
-    const uint32_t vb = *swz_pair(tb, kHalfB, cr, i);
-    acc = __fmaf_rn(__uint_as_float(va << 16), __uint_as_float(vb << 16), acc);
-    acc = __fmaf_rn(__uint_as_float(va & 0xffff0000u), __uint_as_float(vb & 0xffff0000u), acc);
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    const uint4 a = swz_chunk(ta, kHalfA, r, c);
+    const uint4 b = swz_chunk(tb, kHalfB, cr, c);
+    acc = __fmaf_rn(bf_lo(a.x), bf_lo(b.x), acc);
+    acc = __fmaf_rn(bf_hi(a.x), bf_hi(b.x), acc);
+    acc = __fmaf_rn(bf_lo(a.y), bf_lo(b.y), acc);
+    acc = __fmaf_rn(bf_hi(a.y), bf_hi(b.y), acc);
+    acc = __fmaf_rn(bf_lo(a.z), bf_lo(b.z), acc);
+    acc = __fmaf_rn(bf_hi(a.z), bf_hi(b.z), acc);
+    acc = __fmaf_rn(bf_lo(a.w), bf_lo(b.w), acc);
+    acc = __fmaf_rn(bf_hi(a.w), bf_hi(b.w), acc);
   }
   return acc;
 }
@@ -264,14 +272,21 @@ __global__ void __launch_bounds__(32 * (EW + 1), 1)
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(qd * 32) << 16);
     const float c2max = __int_as_float(ctl.c2max_bits);
     bool ok = mbar_wait(&ctl.a_full, 0, abort, status, 4);
-    float vv = 0.f;
+    float vv = 0.f, vw = 0.f;
     if (ok) {
-#pragma unroll 8
-      for (int i = 0; i < 64; ++i) {
-        const uint32_t w = *swz_pair(sa, kHalfA, r, i);
-        const float v0 = __uint_as_float(w << 16), v1 = __uint_as_float(w & 0xffff0000u);
-        vv = __fmaf_rn(v0, v0, __fmaf_rn(v1, v1, vv));
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 a4 = swz_chunk(sa, kHalfA, r, c);
+        vv = __fmaf_rn(bf_lo(a4.x), bf_lo(a4.x), vv);
+        vw = __fmaf_rn(bf_hi(a4.x), bf_hi(a4.x), vw);
+        vv = __fmaf_rn(bf_lo(a4.y), bf_lo(a4.y), vv);
+        vw = __fmaf_rn(bf_hi(a4.y), bf_hi(a4.y), vw);
+        vv = __fmaf_rn(bf_lo(a4.z), bf_lo(a4.z), vv);
+        vw = __fmaf_rn(bf_hi(a4.z), bf_hi(a4.z), vw);
+        vv = __fmaf_rn(bf_lo(a4.w), bf_lo(a4.w), vv);
+        vw = __fmaf_rn(bf_hi(a4.w), bf_hi(a4.w), vw);
       }
+      vv += vw;
     }
     // Upper bounds (fp32 rounding of the norms covered by the 1 + 2^-10 factors).
     const float S = sqrtf(vv) * sqrtf(c2max) * (1.0f + 0x1p-10f);
