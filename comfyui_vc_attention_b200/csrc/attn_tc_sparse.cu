@@ -58,7 +58,6 @@ constexpr int kThreads = 512;
 constexpr int kMaxSteps = 1024 + 64;    // nb + groups for N up to 128K tokens
 constexpr uint32_t kColS = 0, kColT = 256;
 constexpr int kFStride = 36;
-__host__ __device__ constexpr int cm_index(int c) { return ((c & 7) >> 1) * kFStride + (c >> 3) * 2 + (c & 1); }
 __host__ __device__ constexpr int ks_index(int k) {
   return ((k >> 1) & 3) * kFStride + (k >> 5) * 8 + ((k >> 3) & 3) * 2 + (k & 1);
 }
@@ -92,8 +91,8 @@ struct SpSmem {
   alignas(16) float mu[kStages][kD];
   alignas(16) float cm[kRing][2][4 * kFStride];
   alignas(16) float ksf[kRing][4 * kFStride];
-  alignas(16) float alpha[kRing][kBM];   // row r at 32 (r/32) + 4 (r%8) + (r%32)/8
-  alignas(16) float lsum[kRing][kBM];    // approximation steps: sum p_ap, same order
+  alignas(16) float alpha[kRing][kBM];   // per query row
+  alignas(16) float lsum[kRing][kBM];    // approximation steps: sum p_ap, per query row
   Step steps[kMaxSteps];
   int nsteps;
   int has_ap;
@@ -427,8 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int h = 0; h < 2; ++h) {
           const int c = c2 + 64 * h;
           const float vsc = sm.vs[s][c];
-          sm.cm[ring][0][cm_index(c)] = __fdiv_rn(vsc, 448.0f);
-          sm.cm[ring][1][cm_index(c)] = __fmul_rn(sm.mu[s][c], vsc);
+          sm.cm[ring][0][c] = __fdiv_rn(vsc, 448.0f);
+          sm.cm[ring][1][c] = __fmul_rn(sm.mu[s][c], vsc);
         }
 #pragma unroll
         for (int kc = c2; kc < kBR; kc += 64) sm.ksf[ring][ks_index(kc)] = sm.ks[s][kc];
@@ -631,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       warp_arrive(&sm.p_full[b], lane);
       if (j >= kRing && !mbar_wait(&sm.a_free[ring], ((j / kRing) + 1) & 1, abort, status, 10)) break;
       if (q < 2) {
-        const int slot = wq * 32 + 4 * rl + 2 * sg + q;
+        const int slot = ra + 8 * q;
         sm.alpha[ring][slot] = q ? al_b : al_a;
         sm.lsum[ring][slot] = q ? ls_b : ls_a;
       }
@@ -640,13 +639,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 248;\n" ::: "memory");
     // ------------------------------------------------------------ correction
-    const int wq = warp & 3, q = lane & 3, rl = lane >> 2;
-    const uint32_t lb0 = tbase + (static_cast<uint32_t>(wq * 32) << 16);
-    const uint32_t lb1 = tbase + (static_cast<uint32_t>(wq * 32 + 16) << 16);
-    float o[128];
+    // Thread = query row r = 32 (w%4) + lane (TMEM lane r), O[128] in
+    // registers; T read with the 32x32b shape, 64 columns per load batch.
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const uint32_t lb = tbase + (static_cast<uint32_t>(wq * 32) << 16);
+    float o[kD];
 #pragma unroll
-    for (int c = 0; c < 128; ++c) o[c] = 0.f;
-    float l[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < kD; ++c) o[c] = 0.f;
+    float l = 0.f;
     bool ok = true;
     for (int i = 0; i < nst; ++i) {
       const int ring = i % kRing, tb = i & 1;
@@ -655,93 +656,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const bool ap = step_is_ap(sm.steps[i]);
       const uint32_t tcol = kColT + tb * 128;
-      float r0[4] = {0.f, 0.f, 0.f, 0.f}, r1[4] = {0.f, 0.f, 0.f, 0.f};
-      float t0a[16], t0b[16], t1a[16], t1b[16];
-      if (!ap) {
-        tmem_ld_16x256b_x1(lb0 + kColT + (tb ^ 1) * 128, r0);   // R_i sits in T_{(i+1)&1}
-        tmem_ld_16x256b_x1(lb1 + kColT + (tb ^ 1) * 128, r1);
-      }
-      tmem_ld_16x256b_x4(lb0 + tcol, t0a);
-      tmem_ld_16x256b_x4(lb1 + tcol, t0b);
+      float xa[32], xb[32];
+      float rs = 0.f;
+      if (!ap) rs = tmem_ld1(lb + kColT + (tb ^ 1) * 128);   // R_i sits in T_{(i+1)&1}
+      tmem_ld32(lb + tcol, xa);
+      tmem_ld32(lb + tcol + 32, xb);
       tmem_ld_wait();
-      reg_fence4(r0);
-      reg_fence4(r1);
-      reg_fence16(t0a);
-      reg_fence16(t0b);
+      asm volatile("" : "+f"(rs));
+      reg_fence(xa);
+      reg_fence(xb);
       tc_fence_before();
       warp_arrive(&sm.t_rel, lane);
       ok = mbar_wait2(&sm.a_full[ring], (i / kRing) & 1, &sm.f_full[ring], (i / kRing) & 1, abort, status, 12);
       if (!ok) break;
-      const float4 al4 = *reinterpret_cast<const float4*>(&sm.alpha[ring][wq * 32 + 4 * rl]);
-      const float4 ls4 = *reinterpret_cast<const float4*>(&sm.lsum[ring][wq * 32 + 4 * rl]);
+      const float al = sm.alpha[ring][r];
+      const float rr = ap ? sm.lsum[ring][r] : rs * (1.0f / 448.0f);
       warp_arrive(&sm.a_free[ring], lane);
-      const float al[4] = {al4.x, al4.y, al4.z, al4.w};
-      const bool rescale =
-          !__all_sync(0xffffffffu, al4.x == 1.0f && al4.y == 1.0f && al4.z == 1.0f && al4.w == 1.0f);
-      constexpr float kInv448 = 1.0f / 448.0f;
-      float r[4];
-      if (ap) {
-        r[0] = ls4.x; r[1] = ls4.y; r[2] = ls4.z; r[3] = ls4.w;
-      } else {
-        r[0] = r0[0] * kInv448; r[1] = r0[2] * kInv448; r[2] = r1[0] * kInv448; r[3] = r1[2] * kInv448;
-      }
-      const float* cvp = sm.cm[ring][0] + q * kFStride;
-      const float* mvp = sm.cm[ring][1] + q * kFStride;
+      const bool rescale = !__all_sync(0xffffffffu, al == 1.0f);
+      const float4* f4 = reinterpret_cast<const float4*>(sm.cm[ring][0]);
+      const float4* g4 = reinterpret_cast<const float4*>(sm.cm[ring][1]);
 #pragma unroll
-      for (int qq = 0; qq < 4; ++qq) {
-        float (&ca)[16] = (qq & 1) ? t1a : t0a;
-        float (&cb)[16] = (qq & 1) ? t1b : t0b;
-        float (&na)[16] = (qq & 1) ? t0a : t1a;
-        float (&nb16)[16] = (qq & 1) ? t0b : t1b;
-        if (qq + 1 < 4) {
-          tmem_ld_16x256b_x4(lb0 + tcol + 32 * (qq + 1), na);
-          tmem_ld_16x256b_x4(lb1 + tcol + 32 * (qq + 1), nb16);
+      for (int half = 0; half < 2; ++half) {
+        if (half == 1) {
+          tmem_ld32(lb + tcol + 64, xa);
+          tmem_ld32(lb + tcol + 96, xb);
+          tmem_ld_wait();
+          reg_fence(xa);
+          reg_fence(xb);
         }
         if (ap) {
           // acc = alpha acc + T (values already in output units)
 #pragma unroll
-          for (int gl = 0; gl < 4; ++gl) {
-            const int grp = 4 * qq + gl;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float* src = (k < 2 ? ca : cb) + 4 * gl + 2 * (k & 1);
-              float& oa = o[(grp * 4 + k) * 2];
-              float& ob = o[(grp * 4 + k) * 2 + 1];
-              if (rescale) mul2(oa, ob, al[k], al[k]);
-              add2(oa, ob, src[0], src[1]);
+          for (int q = 0; q < 16; ++q) {
+            const float* src = (q < 8) ? xa + 4 * q : xb + 4 * (q - 8);
+            float* oc = o + 64 * half + 4 * q;
+            if (rescale) {
+              mul2(oc[0], oc[1], al, al);
+              mul2(oc[2], oc[3], al, al);
             }
+            add2(oc[0], oc[1], src[0], src[1]);
+            add2(oc[2], oc[3], src[2], src[3]);
           }
         } else {
 #pragma unroll
-          for (int ii = 0; ii < 4; ii += 2) {
-            const float4 cv = *reinterpret_cast<const float4*>(cvp + (4 * qq + ii) * 2);
-            const float4 mv = *reinterpret_cast<const float4*>(mvp + (4 * qq + ii) * 2);
-#pragma unroll
-            for (int sub = 0; sub < 2; ++sub) {
-              const int gl = ii + sub, grp = 4 * qq + gl;
-              const float c0 = sub ? cv.z : cv.x, c1 = sub ? cv.w : cv.y;
-              const float u0 = sub ? mv.z : mv.x, u1 = sub ? mv.w : mv.y;
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float* src = (k < 2 ? ca : cb) + 4 * gl + 2 * (k & 1);
-                float& oa = o[(grp * 4 + k) * 2];
-                float& ob = o[(grp * 4 + k) * 2 + 1];
-                if (rescale) mul2(oa, ob, al[k], al[k]);
-                fma2(oa, ob, src[0], src[1], c0, c1);
-                fma2(oa, ob, r[k], r[k], u0, u1);
-              }
+          for (int q = 0; q < 16; ++q) {
+            const float* src = (q < 8) ? xa + 4 * q : xb + 4 * (q - 8);
+            const float4 fv = f4[16 * half + q];
+            const float4 gv = g4[16 * half + q];
+            float* oc = o + 64 * half + 4 * q;
+            if (rescale) {
+              mul2(oc[0], oc[1], al, al);
+              mul2(oc[2], oc[3], al, al);
             }
+            fma2(oc[0], oc[1], src[0], src[1], fv.x, fv.y);
+            fma2(oc[2], oc[3], src[2], src[3], fv.z, fv.w);
+            fma2(oc[0], oc[1], rr, rr, gv.x, gv.y);
+            fma2(oc[2], oc[3], rr, rr, gv.z, gv.w);
           }
-        }
-        if (qq + 1 < 4) {
-          tmem_ld_wait();
-          reg_fence16(na);
-          reg_fence16(nb16);
         }
       }
       warp_arrive(&sm.f_free[ring], lane);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) l[k] = __fadd_rn(__fmul_rn(l[k], al[k]), r[k]);
+      l = __fadd_rn(__fmul_rn(l, al), rr);
     }
     if (ok && !*abort) {
       constexpr int ES = (ODT == VCATTN_DTYPE_F32) ? 4 : 2;
@@ -750,13 +725,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     "output staging must fit in the operand buffers");
       uint8_t* stage = sm.q + wq * 32 * RS;
 #pragma unroll
-      for (int grp = 0; grp < 16; ++grp) {
+      for (int c0 = 0; c0 < kD; c0 += 16 / ES) {
+        uint4 w;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float v0 = __fdiv_rn(o[(grp * 4 + k) * 2], l[k]);
-          const float v1 = __fdiv_rn(o[(grp * 4 + k) * 2 + 1], l[k]);
-          stage2<ODT>(stage + (rl + 8 * k) * RS + (8 * grp + 2 * q) * ES, v0, v1);
-        }
+        for (int e = 0; e < 16 / ES; e += 2)
+          stage2<ODT>(reinterpret_cast<uint8_t*>(&w) + e * ES, __fdiv_rn(o[c0 + e], l), __fdiv_rn(o[c0 + e + 1], l));
+        *reinterpret_cast<uint4*>(stage + lane * RS + c0 * ES) = w;
       }
       __syncwarp();
       constexpr int CPR = kD * ES / 16;
