@@ -47,11 +47,6 @@ constexpr int kStages = 4;
 constexpr int kRing = 4;        // alpha / column-factor hand-off depth
 constexpr int kThreads = 512;   // 16 warps = 4 warpgroups
 constexpr uint32_t kColS = 0, kColT = 256, kColR = 384, kColSFA = 400, kColSFB = 408;
-// Column factors in the correction's order: the 32 channels 8 grp + 2 q + e
-// of lane group q are contiguous; groups are 36 floats apart so the four
-// groups' float4 reads fall in different banks.
-constexpr int kCmStride = 36;
-__host__ __device__ constexpr int cm_index(int c) { return ((c & 7) >> 1) * kCmStride + (c >> 3) * 2 + (c & 1); }
 
 template <int BR>
 struct TcSmem {
@@ -64,8 +59,8 @@ struct TcSmem {
   alignas(128) uint8_t sfb[kStages][2 * 512];
   alignas(16) float vs[kStages][kD];
   alignas(16) float mu[kStages][kD];
-  alignas(16) float cm[kRing][2][4 * kCmStride];   // vs / 448 and mu * vs at cm_index(c)
-  alignas(16) float alpha[kRing][kBM];  // row r at 32 (r/32) + 4 (r%8) + (r%32)/8
+  alignas(16) float cm[kRing][2][kD];   // vs / 448 and mu * vs per channel
+  alignas(16) float alpha[kRing][kBM];  // per query row
   alignas(8) uint64_t q_full;
   alignas(8) uint64_t kv_full[kStages];
   alignas(8) uint64_t kv_empty[kStages];
@@ -255,9 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < 2; ++h) {
         const int c = c2 + 64 * h;
         const float vsc = sm.vs[s][c];
-        const int idx = cm_index(c);
-        sm.cm[ring][0][idx] = __fdiv_rn(vsc, 448.0f);
-        sm.cm[ring][1][idx] = __fmul_rn(sm.mu[s][c], vsc);
+        sm.cm[ring][0][c] = __fdiv_rn(vsc, 448.0f);
+        sm.cm[ring][1][c] = __fmul_rn(sm.mu[s][c], vsc);
       }
       warp_arrive(&sm.cm_full[ring], lane);
       warp_arrive(&sm.kv_empty[s], lane);
@@ -269,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = (warp & 3) * 32 + lane;          // query row within the tile = TMEM lane
     const uint32_t lane_base = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const int row = row0 + t;
-    const int aidx = (warp & 3) * 32 + 4 * (lane & 7) + (lane >> 3);
+    const int aidx = (warp & 3) * 32 + lane;
     (void)row;
     // one score scale for the whole head: g_q * g_k * sm_scale
     const float qsm = __fmul_rn(__fmul_rn(a.q_g[g], a.k_g[g]), a.sm_scale);
@@ -363,17 +357,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 168;\n" ::: "memory");
     // ------------------------------------------------------------ correction
-    // Warpgroup cg owns channels [64 cg, 64 cg + 64).  Thread (warp w, lane)
-    // owns rows 32 (w%4) + lane/4 + {0, 8, 16, 24} and channels
-    // 64 cg + 8 grp + 2 (lane%4) + {0, 1}, grp = 0..7.
+    // Warpgroup cg owns channels [64 cg, 64 cg + 64); thread = query row
+    // r = 32 (w%4) + lane (TMEM lane r), T read with the 32x32b shape.
     const int cg = (warp >> 2) - 2;
-    const int wq = warp & 3, q = lane & 3, rl = lane >> 2;
-    const uint32_t lb0 = tbase + (static_cast<uint32_t>(wq * 32) << 16);
-    const uint32_t lb1 = tbase + (static_cast<uint32_t>(wq * 32 + 16) << 16);
-    float o[64];   // o[(grp * 4 + k) * 2 + e]: row k, channel 64 cg + 8 grp + 2q + e
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const uint32_t lb = tbase + (static_cast<uint32_t>(wq * 32) << 16);
+    float o[64];   // channels 64 cg + c
 #pragma unroll
     for (int c = 0; c < 64; ++c) o[c] = 0.f;
-    float l[4] = {0.f, 0.f, 0.f, 0.f};
+    float l = 0.f;
     bool ok = true;
     for (int i = 0; i < nb; ++i) {
       const int ring = i % kRing;
@@ -382,52 +375,43 @@ __global__ void __launch_bounds__(kThreads, 1)
            mbar_wait(&sm.cm_full[ring], (i / kRing) & 1, abort, status, 15);
       if (!ok) break;
       tc_fence_after();
-      float r0[4], r1[4], ta[32], tb[32];
-      tmem_ld_16x256b_x1(lb0 + kColR, r0);
-      tmem_ld_16x256b_x1(lb1 + kColR, r1);
-      tmem_ld_16x256b_x8(lb0 + kColT + 64 * cg, ta);
-      tmem_ld_16x256b_x8(lb1 + kColT + 64 * cg, tb);
-      const float4 al4 = *reinterpret_cast<const float4*>(&sm.alpha[ring][wq * 32 + 4 * rl]);
-      tmem_ld_wait_regs(ta);
+      float ta[32], tb[32];
+      float rs = tmem_ld1(lb + kColR);
+      tmem_ld32(lb + kColT + 64 * cg, ta);
+      tmem_ld32(lb + kColT + 64 * cg + 32, tb);
+      const float al = sm.alpha[ring][r];
+      tmem_ld_wait();
+      asm volatile("" : "+f"(rs));
+      reg_fence(ta);
       reg_fence(tb);
-      asm volatile("" : "+f"(r0[0]), "+f"(r0[2]), "+f"(r1[0]), "+f"(r1[2]));
       tc_fence_before();
       warp_arrive(&sm.t_free, lane);     // T and R read: the next PV may start
       warp_arrive(&sm.a_free[ring], lane);
-      const float al[4] = {al4.x, al4.y, al4.z, al4.w};
-      const bool rescale =
-          !__all_sync(0xffffffffu, al4.x == 1.0f && al4.y == 1.0f && al4.z == 1.0f && al4.w == 1.0f);
-      constexpr float kInv448 = 1.0f / 448.0f;
-      const float r[4] = {r0[0] * kInv448, r0[2] * kInv448, r1[0] * kInv448, r1[2] * kInv448};
-      const float* cvp = sm.cm[ring][0] + q * kCmStride + 16 * cg;
-      const float* mvp = sm.cm[ring][1] + q * kCmStride + 16 * cg;
+      const bool rescale = !__all_sync(0xffffffffu, al == 1.0f);
+      const float rr = rs * (1.0f / 448.0f);
+      const float4* f4 = reinterpret_cast<const float4*>(sm.cm[ring][0] + 64 * cg);
+      const float4* g4 = reinterpret_cast<const float4*>(sm.cm[ring][1] + 64 * cg);
 #pragma unroll
-      for (int ii = 0; ii < 8; ii += 2) {
-        const float4 cv = *reinterpret_cast<const float4*>(cvp + 2 * ii);
-        const float4 mv = *reinterpret_cast<const float4*>(mvp + 2 * ii);
-#pragma unroll
-        for (int sub = 0; sub < 2; ++sub) {
-          const int grp = ii + sub;
-          const float c0 = sub ? cv.z : cv.x, c1 = sub ? cv.w : cv.y;
-          const float u0 = sub ? mv.z : mv.x, u1 = sub ? mv.w : mv.y;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float* src = (k < 2 ? ta : tb) + 4 * grp + 2 * (k & 1);
-            float& oa = o[(grp * 4 + k) * 2];
-            float& ob = o[(grp * 4 + k) * 2 + 1];
-            if (rescale) mul2(oa, ob, al[k], al[k]);
-            fma2(oa, ob, src[0], src[1], c0, c1);
-            fma2(oa, ob, r[k], r[k], u0, u1);
-          }
+      for (int q = 0; q < 16; ++q) {
+        const float* src = (q < 8) ? ta + 4 * q : tb + 4 * (q - 8);
+        const float4 fv = f4[q];
+        const float4 gv = g4[q];
+        float* oc = o + 4 * q;
+        if (rescale) {
+          mul2(oc[0], oc[1], al, al);
+          mul2(oc[2], oc[3], al, al);
         }
+        fma2(oc[0], oc[1], src[0], src[1], fv.x, fv.y);
+        fma2(oc[2], oc[3], src[2], src[3], fv.z, fv.w);
+        fma2(oc[0], oc[1], rr, rr, gv.x, gv.y);
+        fma2(oc[2], oc[3], rr, rr, gv.z, gv.w);
       }
       warp_arrive(&sm.cm_free[ring], lane);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) l[k] = __fadd_rn(__fmul_rn(l[k], al[k]), r[k]);
+      l = __fadd_rn(__fmul_rn(l, al), rr);
     }
     if (ok && !*abort) {
-      // Stage this warp's 32 rows x 64 channels (padded stride: conflict-free
-      // 4-byte writes), then write them out as whole 16-byte row chunks.
+      // Stage this warp's 32 rows x 64 channels (padded stride), then write
+      // them out as whole 16-byte row chunks.
       constexpr int ES = (ODT == VCATTN_DTYPE_F32) ? 4 : 2;
       constexpr int RS = 64 * ES + 16;
       static_assert(8 * 32 * RS <= static_cast<int>(sizeof(TcSmem<BR>::q) + sizeof(TcSmem<BR>::k) +
@@ -435,13 +419,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     "output staging must fit in the operand buffers");
       uint8_t* stage = sm.q + (cg * 4 + wq) * 32 * RS;
 #pragma unroll
-      for (int grp = 0; grp < 8; ++grp) {
+      for (int c0 = 0; c0 < 64; c0 += 16 / ES) {
+        uint4 w;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float v0 = __fdiv_rn(o[(grp * 4 + k) * 2], l[k]);
-          const float v1 = __fdiv_rn(o[(grp * 4 + k) * 2 + 1], l[k]);
-          stage2<ODT>(stage + (rl + 8 * k) * RS + (8 * grp + 2 * q) * ES, v0, v1);
-        }
+        for (int e = 0; e < 16 / ES; e += 2)
+          stage2<ODT>(reinterpret_cast<uint8_t*>(&w) + e * ES, __fdiv_rn(o[c0 + e], l), __fdiv_rn(o[c0 + e + 1], l));
+        *reinterpret_cast<uint4*>(stage + lane * RS + c0 * ES) = w;
       }
       __syncwarp();
       constexpr int CPR = 64 * ES / 16;   // 16-byte chunks per staged row
