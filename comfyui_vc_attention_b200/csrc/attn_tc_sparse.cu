@@ -61,16 +61,10 @@ constexpr int kFStride = 36;
 __host__ __device__ constexpr int ks_index(int k) {
   return ((k >> 1) & 3) * kFStride + (k >> 5) * 8 + ((k >> 3) & 3) * 2 + (k & 1);
 }
-// Block of a group at A-operand position k of the approximation PV: thread q
-// of the softmax holds the proxies of blocks 2q, 2q+1, 8+2q, 9+2q (the
-// 16x256b fragment) and writes them to positions 4q .. 4q+3.
-__host__ __device__ constexpr int ap_block_of_pos(int k) {
-  return ((k & 3) < 2) ? 2 * (k >> 2) + (k & 3) : 8 + 2 * (k >> 2) + (k & 3) - 2;
-}
 // Byte offset of (row r, byte c) in a 128-byte-swizzled tile with 128-byte rows.
 __host__ __device__ constexpr int sw128(int r, int c) { return r * 128 + ((((c >> 4) ^ (r & 7)) & 7) << 4) + (c & 15); }
 
-// Step list entry: info = index (block or group) | ap ordinal << 16 | kind << 31;
+// Step list entry: info = index (block or group) | kind << 31 (1 = approximation);
 // mask = kept bits (bit 0 block A, bit 1 block B) of an exact step, or the
 // approximated-block bits of an approximation step (A: 0-15, B: 16-31).
 struct Step {
@@ -78,7 +72,6 @@ struct Step {
 };
 __device__ __forceinline__ bool step_is_ap(const Step& s) { return (s.info >> 31) != 0; }
 __device__ __forceinline__ int step_index(const Step& s) { return static_cast<int>(s.info & 0xffffu); }
-__device__ __forceinline__ int step_ap_ord(const Step& s) { return static_cast<int>((s.info >> 16) & 0x7fffu); }
 
 struct SpSmem {
   alignas(1024) uint8_t q[kBM * 128];
@@ -219,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint8_t* keep_b = a.keep + (static_cast<int64_t>(g) * a.nqb + qbk) * nb;
     const bool has_b = qbk < a.nqb;
     const int ngr = (nb + kGroup - 1) / kGroup;
-    int n_base = 0, ap_base = 0;
+    int n_base = 0, any_ap = 0;
     for (int gbase = 0; gbase < ngr; gbase += 32) {
       const int gi = gbase + lane;
       uint32_t km_a = 0, km_b = 0, vm = 0;
@@ -238,21 +231,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ku = km_a | km_b;                                        // union of kept blocks
       const int has_ap = am != 0;
       const int cnt = has_ap + __popc(ku);
-      int s_incl = cnt, a_incl = has_ap;
+      int s_incl = cnt;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int ts = __shfl_up_sync(0xffffffffu, s_incl, o), ta = __shfl_up_sync(0xffffffffu, a_incl, o);
-        if (lane >= o) {
-          s_incl += ts;
-          a_incl += ta;
-        }
+        const int ts = __shfl_up_sync(0xffffffffu, s_incl, o);
+        if (lane >= o) s_incl += ts;
       }
       int n = n_base + s_incl - cnt;
       if (gi < ngr) {
         if (has_ap) {
           if (n < kMaxSteps) {
-            sm.steps[n].info = static_cast<uint32_t>(gi) |
-                               (static_cast<uint32_t>(ap_base + a_incl - has_ap) << 16) | (1u << 31);
+            sm.steps[n].info = static_cast<uint32_t>(gi) | (1u << 31);
             sm.steps[n].mask = am;
           }
           ++n;
@@ -267,11 +256,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       n_base += __shfl_sync(0xffffffffu, s_incl, 31);
-      ap_base += __shfl_sync(0xffffffffu, a_incl, 31);
+      any_ap |= __any_sync(0xffffffffu, has_ap != 0);
     }
     if (lane == 0) {
       sm.nsteps = n_base;
-      sm.has_ap = ap_base > 0;
+      sm.has_ap = any_ap != 0;
     }
   }
   fence_proxy_async_smem();
