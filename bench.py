@@ -444,8 +444,7 @@ def main() -> int:
         p = prepare(q, k, v, perm, block_rows=w["block_rows"], hadamard=True, smooth_k=True,
                     sparse=cfg.sparse, tau=cfg.tau, q_block=cfg.block_m, scale=scale,
                     want_v=want_v, want_v_t=not want_v, local_blocks=cfg.local_blocks,
-                    sink_blocks=cfg.sink_blocks, qk_fp4=cfg.qk_fp4, v_mma_order=not cfg.qk_fp4,
-                    fp8_qk=not cfg.qk_fp4)
+                    sink_blocks=cfg.sink_blocks, qk_fp4=cfg.qk_fp4, fp8_qk=not cfg.qk_fp4)
         if evs is not None:
             evs[1].record()
         attention_prepared(p, NT, out, scale, cfg)

@@ -8,31 +8,28 @@
 //   acc = alpha * acc + (P @ V8) * (vs / 448) + (rowsum(P) / 448) * (mu * vs)
 //   l   = alpha * l + rowsum(P) / 448 ;  O = acc / l
 //
-// One CTA = 128 query rows of one (batch, head); 16 warps in 4 warpgroups:
+// One CTA = 128 query rows of one (batch, head); 12 warps in 3 warpgroups:
 //   warp 0       TMA producer (Q once; K, V codes + ks, vs, mu per tile)
 //   warp 1       MMA issuer and TMEM owner
-//   warps 2-3    per-tile factors: vs / 448, mu * vs and ks, reordered for
-//                the fragments below
-//   warps 4-11   softmax, two warpgroups: warp w of group s reads TMEM lanes
-//                32 (w%4) + 16 s .. +15 with the 16x256b shape, so a thread
-//                owns 2 rows x 32 key columns (columns 8 grp + 2 (lane%4) +
-//                {0,1}); the row max is finished with two lane shuffles
-//   warps 12-15  correction: O in registers, one query row (TMEM lane) per
-//                thread, T read with the 32x32b shape (the 16x256b shape
-//                sustains about a quarter of its tensor-memory bandwidth)
-// The softmax reads the per-column ks only for the columns it owns; the
-// correction reads the per-channel factors as shared-memory broadcasts.
-// TMEM columns: S double buffer [0,128) [128,256); the P bytes (E4M3, four
-// keys per column) go over the first BR/4 columns of their S buffer and feed
-// the PV MMA from tensor memory; PV tile T_j double buffer [256,384)
+//   warps 2-3    per-tile factors vs / 448 and mu * vs
+//   warps 4-7    softmax: thread = query row = TMEM lane; the row's scores
+//                come in with four 32x32b loads behind one wait, the row max
+//                needs no shuffles, and the P bytes go back in key order
+//   warps 8-11   correction: O in registers, one query row (TMEM lane) per
+//                thread, T read with the 32x32b shape
+// (The 16x256b shape, which splits a row over four threads, sustains about a
+// quarter of the 32x32b tensor-memory bandwidth.)  ks and the per-channel
+// factors are read as shared-memory broadcasts.
+// TMEM columns: S double buffer [0,128) [128,256); the P bytes (E4M3, keys
+// 4c..4c+3 in column c) go over the first BR/4 columns of their S buffer and
+// feed the PV MMA from tensor memory; PV tile T_j double buffer [256,384)
 // [384,512); the row sum R_j (an N=16 MMA of P_j against an all-ones block)
 // goes to the first 16 columns of the other T buffer, whose first quarter
 // (T_{j-1}) the correction warps have already read.  Every MMA gate points at
 // least one MMA back, so the in-order tensor pipe never drains while a
 // handshake completes.
-// A thread's P bytes for keys 8 r + 2 q + e of each 32-key chunk land at
-// A-operand positions 8 q + 2 r + e, so V rows are stored in that order
-// (VCATTN_V_MMA_ORDER).  Q, K use the 128-byte swizzle K-major, V MN-major.
+// P is in key order, so V rows are read in token order (prepared without
+// VCATTN_V_MMA_ORDER).  Q, K use the 128-byte swizzle K-major, V MN-major.
 // Every wait is bounded.
 #include <cuda.h>
 #include <cstdio>
@@ -55,16 +52,11 @@ constexpr int kBM = 128;
 constexpr int kD = 128;
 constexpr int kStages = 4;
 constexpr int kRing = 4;        // per-tile factor / alpha hand-off depth
-constexpr int kThreads = 512;   // 16 warps = 4 warpgroups
+constexpr int kThreads = 384;   // 12 warps = 3 warpgroups
 constexpr uint32_t kColS = 0, kColT = 256;
 // Factor tables in fragment order: the 32 entries lane group q (= lane % 4)
 // reads are contiguous, groups 36 floats apart so their float4 reads fall
 // in different banks.
-constexpr int kFStride = 36;
-// key column k -> slot of (q = k/2 % 4, chunk = k/32, r = k/8 % 4, e = k % 2)
-__host__ __device__ constexpr int ks_index(int k) {
-  return ((k >> 1) & 3) * kFStride + (k >> 5) * 8 + ((k >> 3) & 3) * 2 + (k & 1);
-}
 
 template <int BR>
 struct TcSmem {
@@ -77,7 +69,6 @@ struct TcSmem {
   alignas(16) float vs[kStages][kD];
   alignas(16) float mu[kStages][kD];
   alignas(16) float cm[kRing][2][kD];            // vs / 448 and mu * vs per channel
-  alignas(16) float ksf[kRing][4 * kFStride];     // ks at ks_index
   alignas(16) float alpha[kRing][kBM];            // per query row
   alignas(8) uint64_t q_full;
   alignas(8) uint64_t kv_full[kStages];
@@ -133,15 +124,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.s_full[b], 1);
-      mbar_init(&sm.p_full[b], 8);
+      mbar_init(&sm.p_full[b], 4);
       mbar_init(&sm.t_full[b], 1);
     }
     mbar_init(&sm.t_rel, 4);
     for (int r = 0; r < kRing; ++r) {
-      mbar_init(&sm.a_full[r], 8);
+      mbar_init(&sm.a_full[r], 4);
       mbar_init(&sm.a_free[r], 4);
       mbar_init(&sm.f_full[r], 2);
-      mbar_init(&sm.f_free[r], 8 + 4);
+      mbar_init(&sm.f_free[r], 4);
     }
     mbar_init(&sm.drain, 1);
     fence_mbar_init();
@@ -159,8 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = &sm.abort;
 
   if (warp < 4) {
-  // Register budget per warpgroup (launched at 128 x 512 = 65536):
-  // 128 x (40 producer/MMA/factors + 2 x 112 softmax + 248 correction) = 65536.
+  // Register budget per warpgroup (launched at 168 x 384 = 64512):
+  // 128 x (40 producer/MMA/factors + 200 softmax + 248 correction) = 62464.
   asm volatile("setmaxnreg.dec.sync.aligned.u32 40;\n" ::: "memory");
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -262,119 +253,96 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm.cm[ring][0][c] = __fdiv_rn(vsc, 448.0f);
         sm.cm[ring][1][c] = __fmul_rn(sm.mu[s][c], vsc);
       }
-#pragma unroll
-      for (int kc = c2; kc < BR; kc += 64) sm.ksf[ring][ks_index(kc)] = sm.ks[s][kc];
       warp_arrive(&sm.f_full[ring], lane);
       warp_arrive(&sm.kv_empty[s], lane);
     }
   }
-  } else if (warp < 12) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 112;\n" ::: "memory");
+  } else if (warp < 8) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
     // ------------------------------------------------------------ softmax
-    // Group sg of warp w: rows ra = 32 (w%4) + 16 sg + lane/4 and rb = ra + 8;
-    // key columns 32 ch + 8 r + 2 q + e of every chunk ch (q = lane % 4).
-    const int sg = (warp >> 2) - 1;
-    const int wq = warp & 3, q = lane & 3, rl = lane >> 2;
-    const int ra = wq * 32 + 16 * sg + rl;
-    const uint32_t lane_base = tbase + (static_cast<uint32_t>(wq * 32 + 16 * sg) << 16);
-    const int64_t qrow = static_cast<int64_t>(g) * a.n_pad + row0;
-    const float qs_a = (row0 + ra < a.n_pad) ? a.q_scale[qrow + ra] : 0.f;
-    const float qs_b = (row0 + ra + 8 < a.n_pad) ? a.q_scale[qrow + ra + 8] : 0.f;
-    const float qsm_a = __fmul_rn(qs_a, a.sm_scale), qsm_b = __fmul_rn(qs_b, a.sm_scale);
+    // Thread = query row t = 32 (w%4) + lane = TMEM lane t: the whole row of S
+    // in registers (32x32b loads, one wait), the row max without shuffles,
+    // P for keys 4c..4c+3 in column c (key order: V is read in token order).
+    const int t = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int64_t qrow = static_cast<int64_t>(g) * a.n_pad + row0 + t;
+    const float qs = (row0 + t < a.n_pad) ? a.q_scale[qrow] : 0.f;
+    const float qsm = __fmul_rn(qs, a.sm_scale);
     // ExpCast: c = A * (x - m) + c120 with A = 8 log2e qs sm; evaluated as
     // fma.sat(x, A/128, B/128) so the clamp at 0 is free and the /128 scale
     // makes a + 98304 round the code to an integer in the low bits.
-    const float As_a = __fmul_rn(8.0f * kLog2e, qsm_a) * (1.0f / 128.0f);
-    const float As_b = __fmul_rn(8.0f * kLog2e, qsm_b) * (1.0f / 128.0f);
-    const float Ae_a = __fmul_rn(qsm_a, kLog2e), Ae_b = __fmul_rn(qsm_b, kLog2e);
-    float m_a = -INFINITY, m_b = -INFINITY;
+    const float As = __fmul_rn(8.0f * kLog2e, qsm) * (1.0f / 128.0f);
+    const float Ae = __fmul_rn(qsm, kLog2e);
+    float m = -INFINITY;
     for (int j = 0; j < nb; ++j) {
-      const int b = j & 1, ring = j % kRing;
-      if (!mbar_wait(&sm.s_full[b], (j >> 1) & 1, abort, status, 7)) break;
-      if (!mbar_wait(&sm.f_full[ring], (j / kRing) & 1, abort, status, 8)) break;
+      const int b = j & 1, ring = j % kRing, s = j % kStages;
+      // ks of tile j came with its K/V stage (bulk copy completed on kv_full)
+      if (!mbar_wait2(&sm.s_full[b], (j >> 1) & 1, &sm.kv_full[s], (j / kStages) & 1, abort, status, 7)) break;
       tc_fence_after();
       const uint32_t sb = lane_base + kColS + b * 128;
-      float x[NCH][16];
+      float x[BR];
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) tmem_ld_16x256b_x4(sb + 32 * ch, x[ch]);
+      for (int ch = 0; ch < NCH; ++ch)
+        tmem_ld32(sb + 32 * ch, *reinterpret_cast<float(*)[32]>(x + 32 * ch));
       tmem_ld_wait();
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) reg_fence16(x[ch]);
-      const float* kf = sm.ksf[ring] + q * kFStride;
+      for (int ch = 0; ch < NCH; ++ch) reg_fence(*reinterpret_cast<float(*)[32]>(x + 32 * ch));
+      const float4* k4 = reinterpret_cast<const float4*>(sm.ks[s]);
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
-        const float4 k0 = *reinterpret_cast<const float4*>(kf + 8 * ch);
-        const float4 k1 = *reinterpret_cast<const float4*>(kf + 8 * ch + 4);
-        const float kr[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          mul2(x[ch][4 * r], x[ch][4 * r + 1], kr[2 * r], kr[2 * r + 1]);
-          mul2(x[ch][4 * r + 2], x[ch][4 * r + 3], kr[2 * r], kr[2 * r + 1]);
-        }
+      for (int q = 0; q < BR / 4; ++q) {
+        const float4 kv = k4[q];
+        mul2(x[4 * q], x[4 * q + 1], kv.x, kv.y);
+        mul2(x[4 * q + 2], x[4 * q + 3], kv.z, kv.w);
       }
-      warp_arrive(&sm.f_free[ring], lane);
       const int valid = a.N - j * BR;                 // keys >= valid are padding
       if (valid < BR) {
 #pragma unroll
-        for (int ch = 0; ch < NCH; ++ch)
-#pragma unroll
-          for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int e = 0; e < 2; ++e)
-              if (32 * ch + 8 * r + 2 * q + e >= valid) x[ch][4 * r + e] = x[ch][4 * r + 2 + e] = -1.0e30f;
+        for (int c = 0; c < BR; ++c)
+          if (c >= valid) x[c] = -1.0e30f;
       }
-      float ma0 = m_a, ma1 = -INFINITY, mb0 = m_b, mb1 = -INFINITY;
+      float m0 = m, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
-        ma0 = fmax3(ma0, x[ch][0], x[ch][1]);
-        mb0 = fmax3(mb0, x[ch][2], x[ch][3]);
-        ma1 = fmax3(ma1, x[ch][4], x[ch][5]);
-        mb1 = fmax3(mb1, x[ch][6], x[ch][7]);
-        ma0 = fmax3(ma0, x[ch][8], x[ch][9]);
-        mb0 = fmax3(mb0, x[ch][10], x[ch][11]);
-        ma1 = fmax3(ma1, x[ch][12], x[ch][13]);
-        mb1 = fmax3(mb1, x[ch][14], x[ch][15]);
+      for (int c = 0; c < BR; c += 8) {
+        m0 = fmax3(m0, x[c], x[c + 1]);
+        m1 = fmax3(m1, x[c + 2], x[c + 3]);
+        m2 = fmax3(m2, x[c + 4], x[c + 5]);
+        m3 = fmax3(m3, x[c + 6], x[c + 7]);
       }
-      float mn_a = fmaxf(ma0, ma1), mn_b = fmaxf(mb0, mb1);
-      mn_a = fmaxf(mn_a, __shfl_xor_sync(0xffffffffu, mn_a, 1));
-      mn_b = fmaxf(mn_b, __shfl_xor_sync(0xffffffffu, mn_b, 1));
-      mn_a = fmaxf(mn_a, __shfl_xor_sync(0xffffffffu, mn_a, 2));
-      mn_b = fmaxf(mn_b, __shfl_xor_sync(0xffffffffu, mn_b, 2));
-      const float al_a = (m_a == -INFINITY) ? 0.f : exp2f(__fmul_rn(__fsub_rn(m_a, mn_a), Ae_a));
-      const float al_b = (m_b == -INFINITY) ? 0.f : exp2f(__fmul_rn(__fsub_rn(m_b, mn_b), Ae_b));
-      // P words: per chunk (row a keys r=0,1 | r=2,3, row b keys r=0,1 | r=2,3)
-      uint32_t packed[4 * NCH];
+      const float mn = fmax3(m0, m1, fmaxf(m2, m3));
+      const float al = (m == -INFINITY) ? 0.f : exp2f(__fmul_rn(__fsub_rn(m, mn), Ae));
+      // P words: chunk ch (keys 32 ch .. 32 ch + 31) to columns 8 ch .. 8 ch + 7
       if constexpr (EXPCAST) {
-        const float Bs_a = __fmaf_rn(-As_a, mn_a, a.c120 * (1.0f / 128.0f));
-        const float Bs_b = __fmaf_rn(-As_b, mn_b, a.c120 * (1.0f / 128.0f));
+        const float Bs = __fmaf_rn(-As, mn, a.c120 * (1.0f / 128.0f));
 #pragma unroll
         for (int ch = 0; ch < NCH; ++ch) {
-          packed[4 * ch + 0] = expcast4(x[ch][0], x[ch][1], x[ch][4], x[ch][5], As_a, Bs_a);
-          packed[4 * ch + 1] = expcast4(x[ch][8], x[ch][9], x[ch][12], x[ch][13], As_a, Bs_a);
-          packed[4 * ch + 2] = expcast4(x[ch][2], x[ch][3], x[ch][6], x[ch][7], As_b, Bs_b);
-          packed[4 * ch + 3] = expcast4(x[ch][10], x[ch][11], x[ch][14], x[ch][15], As_b, Bs_b);
+          uint32_t packed[8];
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const float* xc = x + 32 * ch + 4 * w;
+            packed[w] = expcast4(xc[0], xc[1], xc[2], xc[3], As, Bs);
+          }
+          tmem_st8(sb + 8 * ch, packed);
         }
       } else {
-        const float Be_a = __fmaf_rn(-Ae_a, mn_a, 8.807354922057604f);   // log2(448)
-        const float Be_b = __fmaf_rn(-Ae_b, mn_b, 8.807354922057604f);
+        const float Be = __fmaf_rn(-Ae, mn, 8.807354922057604f);   // log2(448)
 #pragma unroll
         for (int ch = 0; ch < NCH; ++ch) {
-          packed[4 * ch + 0] = exp4(x[ch][0], x[ch][1], x[ch][4], x[ch][5], Ae_a, Be_a);
-          packed[4 * ch + 1] = exp4(x[ch][8], x[ch][9], x[ch][12], x[ch][13], Ae_a, Be_a);
-          packed[4 * ch + 2] = exp4(x[ch][2], x[ch][3], x[ch][6], x[ch][7], Ae_b, Be_b);
-          packed[4 * ch + 3] = exp4(x[ch][10], x[ch][11], x[ch][14], x[ch][15], Ae_b, Be_b);
+          uint32_t packed[8];
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const float* xc = x + 32 * ch + 4 * w;
+            packed[w] = exp4(xc[0], xc[1], xc[2], xc[3], Ae, Be);
+          }
+          tmem_st8(sb + 8 * ch, packed);
         }
       }
-      if constexpr (NCH == 4) tmem_st_16x256b_x4(sb, packed);
-      else tmem_st_16x256b_x2(sb, packed);
       tmem_st_wait();
       tc_fence_before();
       warp_arrive(&sm.p_full[b], lane);
       if (j >= kRing && !mbar_wait(&sm.a_free[ring], ((j / kRing) + 1) & 1, abort, status, 10)) break;
-      if (q < 2) sm.alpha[ring][ra + 8 * q] = q ? al_b : al_a;
+      sm.alpha[ring][t] = al;
       warp_arrive(&sm.a_full[ring], lane);
-      m_a = mn_a;
-      m_b = mn_b;
+      m = mn;
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 248;\n" ::: "memory");

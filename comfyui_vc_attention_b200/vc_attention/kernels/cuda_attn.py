@@ -124,7 +124,7 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
             block_rows: int = 128, hadamard: bool = True, smooth_k: bool = True, *,
             sparse: bool = False, tau: float = 1.3, q_block: int = 64,
             scale: Optional[float] = None, want_v: bool = True, want_v_t: bool = False,
-            local_blocks: int = 1, sink_blocks: int = 0, v_mma_order: bool = True,
+            local_blocks: int = 1, sink_blocks: int = 0, v_mma_order: Optional[bool] = None,
             qk_fp4: bool = False, fp8_qk: bool = True) -> Prepared:
     """Quantise and permute Q/K/V into the kernel layout (triton_attn.py:504-579).
 
@@ -167,6 +167,8 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
     vs = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
     mu = torch.empty((g, nb, d), dtype=torch.float32, device=dev)
     flags = (N.HADAMARD if hadamard else 0) | (N.SMOOTH_K if smooth_k else 0)
+    if v_mma_order is None:
+        v_mma_order = sparse   # the order the matching tcgen05 kernel reads
     v_mma_order = bool(v_mma_order and want_v)
     if v_mma_order:
         flags |= N.V_MMA_ORDER
@@ -309,8 +311,7 @@ def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     use_tc = d == 128 and (not sparse or sparse_tc_applies(d, br, cfg.block_m, cfg.group, n))
     p = prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
                 tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=use_tc, want_v_t=not use_tc,
-                local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks, v_mma_order=not fp4,
-                qk_fp4=fp4, fp8_qk=not fp4)
+                local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks, qk_fp4=fp4, fp8_qk=not fp4)
     out = _out_view(q, q.dtype)
     return attention_prepared(p, n, out, scale, cfg)
 
@@ -366,10 +367,10 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
             out.stride(0), out.stride(1), out.stride(2), st))
         return out
     if kernel == "auto":
-        kernel = "tc" if (d == 128 and p.v is not None) else "mma"
+        kernel = "tc" if (d == 128 and p.v is not None and not p.v_mma_order) else "mma"
     if kernel == "tc":
-        if p.v is None or not p.v_mma_order:
-            raise ValueError("the tcgen05 kernel reads V codes in its key order (want_v=True, v_mma_order=True)")
+        if p.v is None or p.v_mma_order:
+            raise ValueError("the dense tcgen05 kernel reads V codes in token order (want_v=True, v_mma_order=False)")
         N.check("vcattn_attn_fp8", lib.vcattn_attn_fp8(
             q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
             p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), b, h, n, n_pad, d,

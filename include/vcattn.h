@@ -53,10 +53,12 @@ extern "C" {
 /* ---- prepare flags (triton_attn.py:504-512 hadamard / smooth_k) --------- */
 #define VCATTN_HADAMARD 1
 #define VCATTN_SMOOTH_K 2
-/* V codes (v8) in the tcgen05 kernel's key order: inside every 32-row chunk
- * of a value block, row 8a + 2b + e is stored at slot 8b + 2a + e (a, b in
- * 0..3, e in 0..1).  The order is its own inverse.  vcattn_attn_fp8 requires
- * it; the other outputs are unaffected.  No counterpart in the reference. */
+/* V codes (v8) in the tcgen05 sparse kernel's key order: inside every 32-row
+ * chunk of a value block, row 8a + 2b + e is stored at slot 8b + 2a + e (a, b
+ * in 0..3, e in 0..1).  The order is its own inverse.
+ * vcattn_attn_fp8_sparse_tc requires it; vcattn_attn_fp8 and
+ * vcattn_attn_nvfp4 read token order (without the flag); the other outputs are
+ * unaffected.  No counterpart in the reference. */
 #define VCATTN_V_MMA_ORDER 4
 
 /* ---- attention flags (TritonConfig, triton_attn.py:93-129) ------------- */
@@ -198,7 +200,8 @@ VCATTN_API int vcattn_attn_nvfp4(const uint8_t* q4, const uint8_t* q4_sf_mma, co
 
 /* ---- fused dense FP8 attention: triton_attn.py:203-322 (+ launch :831-844)
  * The tcgen05 kernel (D = 128, block_rows 64 or 128).  Consumes the prepare
- * outputs in the Prepared layout (v8 row-major (G,NP,D)); writes O (B,H,N,D)
+ * outputs in the Prepared layout (v8 row-major (G,NP,D) in token order, i.e.
+ * prepared without VCATTN_V_MMA_ORDER); writes O (B,H,N,D)
  * through the out view (out_dtype one of the three dtypes; strides in
  * elements).  Its bounded waits report through vcattn_attn_status(). */
 VCATTN_API int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8,

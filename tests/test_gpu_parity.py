@@ -207,7 +207,7 @@ def test_prepare_config0_bit_exact(dev):
     g = _load("config0.npz")
     q, k, v = make_qkv(1, 2, 1024, 128, seed=0)
     q, k, v = (a.reshape(1, 2, 1024, 128) for a in (q, k, v))
-    p = _prep_gpu(q, k, v, g["perm"], 64, dev, want_v_t=True)
+    p = _prep_gpu(q, k, v, g["perm"], 64, dev, want_v_t=True, v_mma_order=True)
     ref = O.prepare(q.reshape(2, 1024, 128), k.reshape(2, 1024, 128), v.reshape(2, 1024, 128),
                     g["perm"], block_rows=64)
     _assert_prepare_equal(p, ref, 2)
