@@ -643,13 +643,15 @@ def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_
 
 
 def attention_codes_nvfp4(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_m: int,
-                          sm_scale: float, expcast: bool = False, beta: float = -0.35) -> np.ndarray:
+                          sm_scale: float, expcast: bool = False, beta: float = -0.35,
+                          row_blocks: Optional[Sequence[int]] = None) -> np.ndarray:
     """NVFP4-QK variant of attention_codes (triton_attn.py:227-239, 263-271 with
     the tensor-scaled NVFP4 of quant.py:172-204): Q and K are the NVFP4 codes
     of the rotated (and smoothed) rows with one tensor scale per head,
     s = dot(q4 * micro_q, k4 * micro_k) * fp32(fp32(g_q * g_k) * sm_scale)
     (the block-scaled MMA's product, then one scale for the whole head); P and
-    V stay FP8 exactly as in attention_codes.  Returns (G, N, D) float32.
+    V stay FP8 exactly as in attention_codes.  Returns (G, N, D) float32;
+    ``row_blocks`` restricts the evaluation to those query blocks.
     """
     def deq(x_t):
         packed, micro, gs = nvfp4_per_head(x_t)
@@ -666,7 +668,7 @@ def attention_codes_nvfp4(prep: Dict[str, np.ndarray], n: int, block_rows: int, 
     out = np.zeros((g, n, d), np.float32)
     for gi in range(g):
         c = F32(F32(gq[gi] * gk[gi]) * F32(sm_scale))
-        for sm in range(0, n, block_m):
+        for _, sm in _row_starts(n, block_m, row_blocks):
             em = min(n, sm + block_m)
             rows = em - sm
             m_i = np.full(rows, -np.inf, np.float32)

@@ -718,3 +718,86 @@ def test_full_size_sparse_keep_all_equals_dense(dev):
     torch.cuda.synchronize()
     assert attention_status() == (0, 0, 0)
     assert torch.equal(o_s, o_d)
+
+
+# ------------------------------------ per-head full size, N = 65536, k = 512 ----
+#
+# configs[3] / configs[4] / the N = 65536 case of configs[2] run 65536 tokens
+# per head with V-Smooth k = 512.  Two heads of that size carry the per-head
+# work of the 56-head calls; the GPU permutation (tensor-core k-means, checked
+# against the oracle at smaller sizes) feeds both sides, and the oracle checks
+# the prepared codes bit for bit and three query blocks of each output.
+
+N64K, H64K = 65536, 2
+
+
+def _perm64k(vt):
+    from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
+    res = build_permutation(vt.view(H64K, N64K, 128), GroupingConfig(block_rows=128, iters=3, max_clusters=512))
+    assert res.k == 512
+    srt = torch.sort(res.perm.long(), dim=-1).values
+    assert torch.equal(srt, torch.arange(N64K, device=vt.device).expand_as(srt))
+    return res.perm
+
+
+def test_n65536_dense_fp8_and_nvfp4(dev):
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
+                                                                           attention_status, prepare)
+    q, k, v = make_qkv(1, H64K, N64K, 128, seed=31)
+    qt, kt, vt = _bf16(q, dev), _bf16(k, dev), _bf16(v, dev)
+    perm = _perm64k(vt)
+    sc = 128 ** -0.5
+    qg, kg, vg = (a.reshape(H64K, N64K, 128) for a in (q, k, v))
+    ref = O.prepare(qg, kg, vg, perm.cpu().numpy(), block_rows=128)
+    # FP8 (configs[3] FP8 line, configs[4] dense)
+    p = prepare(qt, kt, vt, perm, block_rows=128, want_v=True)
+    np.testing.assert_array_equal(p.q.view(torch.uint8).reshape(H64K, -1, 128).cpu().numpy(), ref["q"])
+    np.testing.assert_array_equal(p.k.view(torch.uint8).reshape(H64K, -1, 128).cpu().numpy(), ref["k"])
+    np.testing.assert_array_equal(p.v.view(torch.uint8).reshape(H64K, -1, 128).cpu().numpy(), ref["v"])
+    out = torch.empty((1, H64K, N64K, 128), dtype=torch.float32, device=dev)
+    attention_prepared(p, N64K, out, sc, TritonConfig(block_n=128, enable_expcast=True), kernel="tc")
+    torch.cuda.synchronize()
+    assert attention_status() == (0, 0, 0)
+    got = out.reshape(H64K, N64K, 128).cpu().numpy()
+    blocks = [0, 511, 1023]
+    rows = np.concatenate([np.arange(i * 64, (i + 1) * 64) for i in blocks])
+    codes = O.attention_codes(ref, N64K, 128, 64, sc, expcast=True, row_blocks=blocks)
+    assert O.rel_l2(got[:, rows], codes[:, rows]) <= REL_L2_CODES
+    del p
+    # NVFP4 QK^T
+    p4 = prepare(qt, kt, vt, perm, block_rows=128, want_v=True, qk_fp4=True, fp8_qk=False)
+    attention_prepared(p4, N64K, out, sc, TritonConfig(block_n=128, enable_expcast=True, qk_fp4=True))
+    torch.cuda.synchronize()
+    assert attention_status() == (0, 0, 0)
+    got4 = out.reshape(H64K, N64K, 128).cpu().numpy()
+    blocks4 = [0, 255, 511]
+    rows4 = np.concatenate([np.arange(i * 128, (i + 1) * 128) for i in blocks4])
+    codes4 = O.attention_codes_nvfp4(ref, N64K, 128, 128, sc, expcast=True, row_blocks=blocks4)
+    assert O.rel_l2(got4[:, rows4], codes4[:, rows4]) <= REL_L2_CODES
+
+
+def test_n65536_sparse_on_the_64x32x32_grid(dev):
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
+                                                                           attention_status, prepare)
+    q, k, v = make_qkv(1, H64K, N64K, 128, seed=33, spatial=(64, 32, 32))
+    qt, kt, vt = _bf16(q, dev), _bf16(k, dev), _bf16(v, dev)
+    perm = _perm64k(vt)
+    sc, tau = 128 ** -0.5, 1.3
+    p = prepare(qt, kt, vt, perm, block_rows=128, sparse=True, tau=tau, q_block=64, want_v=True)
+    out = torch.empty((1, H64K, N64K, 128), dtype=torch.float32, device=dev)
+    attention_prepared(p, N64K, out, sc, TritonConfig(block_m=64, block_n=128, sparse=True, tau=tau,
+                                                     enable_expcast=True), kernel="tc")
+    torch.cuda.synchronize()
+    assert attention_status() == (0, 0, 0)
+    qg, kg, vg = (a.reshape(H64K, N64K, 128) for a in (q, k, v))
+    ref = O.prepare(qg, kg, vg, perm.cpu().numpy(), block_rows=128)
+    st = O.route_stats(ref, 128, 64, tau, sc)
+    keep_o, _ = O.route_mask(ref, st, N64K, 128, 64, sc)
+    keep = p.keep.cpu().numpy().astype(bool).reshape(keep_o.shape)
+    np.testing.assert_array_equal(keep, keep_o)
+    assert 0.5 < 1.0 - keep.mean() < 0.99
+    got = out.reshape(H64K, N64K, 128).cpu().numpy()
+    blocks = [0, 511, 1023]
+    rows = np.concatenate([np.arange(i * 64, (i + 1) * 64) for i in blocks])
+    codes = O.attention_sparse_codes(ref, st, keep_o, N64K, 128, 64, sc, group=16, expcast=True, row_blocks=blocks)
+    assert O.rel_l2(got[:, rows], codes[:, rows]) <= REL_L2_CODES
