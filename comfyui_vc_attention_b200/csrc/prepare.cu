@@ -386,8 +386,10 @@ __global__ void __launch_bounds__(256) route_mask_kernel(const float* __restrict
                                                          float sm_scale, uint8_t* __restrict__ keep,
                                                          float* __restrict__ thresh_out) {
   extern __shared__ float rsm[];                 // proxy, score [kRouteQB][nb]
-  __shared__ __align__(16) float qcs[kRouteQB][D];
-  __shared__ __align__(16) float qbs[kRouteQB][D];
+  // the eight query vectors as doubles: each is converted once, not once per
+  // k_mean row (the float -> double conversions bounded this kernel)
+  __shared__ __align__(16) double qcs[kRouteQB][D];
+  __shared__ __align__(16) double qbs[kRouteQB][D];
   float* proxy = rsm;
   float* score = rsm + kRouteQB * nb;
   const int g = blockIdx.y;
@@ -395,8 +397,8 @@ __global__ void __launch_bounds__(256) route_mask_kernel(const float* __restrict
   for (int e = tid; e < kRouteQB * D; e += blockDim.x) {
     const int w = e / D, d = e % D, i = blockIdx.x * kRouteQB + w;
     const bool ok = i < nqb;
-    qcs[w][d] = ok ? q_cent[(static_cast<int64_t>(g) * nqb + i) * D + d] : 0.f;
-    qbs[w][d] = ok ? q_bar[(static_cast<int64_t>(g) * nqb + i) * D + d] : 0.f;
+    qcs[w][d] = ok ? static_cast<double>(q_cent[(static_cast<int64_t>(g) * nqb + i) * D + d]) : 0.0;
+    qbs[w][d] = ok ? static_cast<double>(q_bar[(static_cast<int64_t>(g) * nqb + i) * D + d]) : 0.0;
   }
   __syncthreads();
   const float inv_q = static_cast<float>(q_block);
@@ -408,17 +410,21 @@ __global__ void __launch_bounds__(256) route_mask_kernel(const float* __restrict
 #pragma unroll 2
     for (int d = 0; d < D; d += 4) {
       const float4 kv = *reinterpret_cast<const float4*>(km + d);
-      const float kf[4] = {kv.x, kv.y, kv.z, kv.w};
-      const float kb[4] = {bf16_round(kv.x), bf16_round(kv.y), bf16_round(kv.z), bf16_round(kv.w)};
+      const double kf[4] = {static_cast<double>(kv.x), static_cast<double>(kv.y), static_cast<double>(kv.z),
+                            static_cast<double>(kv.w)};
+      const double kb[4] = {static_cast<double>(bf16_round(kv.x)), static_cast<double>(bf16_round(kv.y)),
+                            static_cast<double>(bf16_round(kv.z)), static_cast<double>(bf16_round(kv.w))};
 #pragma unroll
       for (int w = 0; w < kRouteQB; ++w) {
-        const float4 c4 = *reinterpret_cast<const float4*>(&qcs[w][d]);
-        const float4 b4 = *reinterpret_cast<const float4*>(&qbs[w][d]);
-        const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+        const double2 c01 = *reinterpret_cast<const double2*>(&qcs[w][d]);
+        const double2 c23 = *reinterpret_cast<const double2*>(&qcs[w][d + 2]);
+        const double2 b01 = *reinterpret_cast<const double2*>(&qbs[w][d]);
+        const double2 b23 = *reinterpret_cast<const double2*>(&qbs[w][d + 2]);
+        const double cv[4] = {c01.x, c01.y, c23.x, c23.y}, bv[4] = {b01.x, b01.y, b23.x, b23.y};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          d1[w] = fma(static_cast<double>(cv[e]), static_cast<double>(kf[e]), d1[w]);
-          d2[w] = fma(static_cast<double>(bv[e]), static_cast<double>(kb[e]), d2[w]);
+          d1[w] = fma(cv[e], kf[e], d1[w]);
+          d2[w] = fma(bv[e], kb[e], d2[w]);
         }
       }
     }
