@@ -419,6 +419,23 @@ def _host_streams(dev: torch.device):
     return _HOST_STREAMS[key]
 
 
+def _chunk_bounds(g: int, c: int):
+    """Unit ranges [lo, hi) for vc_attention_host: chunks of c units, with the
+    last c (or fewer) units split into shrinking pieces (c=4: ..., 4, 2, 1, 1)
+    so that the work left after the final copy-in, one piece's compute and
+    copy-out, is small."""
+    out, lo = [], 0
+    while g - lo > c:
+        out.append((lo, lo + c))
+        lo += c
+    while lo < g:
+        r = g - lo
+        s = r // 2 if r > 1 else 1
+        out.append((lo, lo + s))
+        lo += s
+    return out
+
+
 def vc_attention_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                       perm: Optional[torch.Tensor] = None, cfg: Optional[TritonConfig] = None,
                       scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
@@ -462,9 +479,7 @@ def vc_attention_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     in_ready = [torch.cuda.Event() for _ in range(2)]
     comp_done = [torch.cuda.Event() for _ in range(2)]
     out_done = [torch.cuda.Event() for _ in range(2)]
-    nchunk = -(-g // c)
-    for i in range(nchunk):
-        lo, hi = i * c, min(g, (i + 1) * c)
+    for i, (lo, hi) in enumerate(_chunk_bounds(g, c)):
         u, slot = hi - lo, i % 2
         with torch.cuda.stream(s_in):
             if i >= 2:

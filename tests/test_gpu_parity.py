@@ -568,7 +568,7 @@ def test_vc_attention_cuda_nvfp4_entry_point(dev):
 @pytest.mark.parametrize("sparse", [False, True])
 def test_vc_attention_host_matches_device_call(dev, sparse):
     """The chunk-pipelined host entry point gives the device call's bytes
-    (units are independent; chunks of 4 heads, the last one partial)."""
+    (units are independent; 6 heads in chunks of 4, 1 and 1)."""
     from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, vc_attention_cuda,
                                                                            vc_attention_host)
     b, h, n, d = 1, 6, 1024, 128

@@ -186,3 +186,18 @@ def test_mma_key_slot_is_an_involution_within_32_row_chunks():
         for rr in range(4):
             for e in range(2):
                 assert int(mma_key_slot(torch.tensor(8 * rr + 2 * q + e))) == 8 * q + 2 * rr + e
+
+
+def test_host_chunk_bounds_cover_every_unit_once():
+    """vc_attention_host's unit ranges: contiguous, non-empty, covering [0, G),
+    at most c units each, the last c units in shrinking pieces."""
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import _chunk_bounds
+    for g in range(1, 130):
+        for c in (1, 2, 3, 4, 7, 8, 16):
+            b = _chunk_bounds(g, c)
+            assert b[0][0] == 0 and b[-1][1] == g
+            assert all(x[1] == y[0] for x, y in zip(b, b[1:]))
+            assert all(0 < hi - lo <= c for lo, hi in b)
+            if g > 1:
+                assert b[-1][1] - b[-1][0] == 1
+    assert [hi - lo for lo, hi in _chunk_bounds(56, 4)] == [4] * 13 + [2, 1, 1]
