@@ -18,9 +18,12 @@
 // than E away from both bf16 rounding boundaries around it, bf16(acc_c) =
 // bf16(a_c) and sim_c follows without recomputation; otherwise the token's
 // dot with that centroid is recomputed as the sequential FMA chain from the
-// bf16 rows staged in shared memory.  The candidates are visited in index
-// order and a later one replaces the best only when strictly greater, which
-// is numpy's / torch's first-argmax rule.
+// bf16 rows staged in shared memory.  The recomputations are queued per
+// token (a bit per column of the 32-column block) and run one per lane per
+// round, so a warp pays one sequential chain per round rather than one per
+// column any of its tokens flagged.  The best is the highest sim, ties going
+// to the lower index (numpy's / torch's first-argmax rule), which does not
+// depend on the order candidates are visited in.
 //
 // One CTA = 128 tokens (MMA M) of one (batch, head); warps 0-15 are the
 // epilogue (thread = token = TMEM lane, four warps per row splitting the
@@ -135,22 +138,29 @@ __device__ __noinline__ float exact_dot(const uint8_t* ta, int r, const uint8_t*
   return acc;
 }
 
-// Exact sim of a candidate from its tensor-core dot `a`: bf16(acc) = bf16(a)
-// when a lies more than E inside the rounding interval of bf16(a), else the
-// dot is recomputed in the defining order.
-__device__ __forceinline__ float cand_sim(float a, float E, float nc2v, const uint8_t* ta, int r,
-                                          const uint8_t* tb, int cr) {
-  const float bf = bf16_round(a);
-  const uint32_t ab = __float_as_uint(fabsf(bf));
-  bool safe = false;
+// bf16(acc) of a candidate from its tensor-core dot `a`: equal to bf16(a)
+// when a lies more than E inside the rounding interval of bf16(a) (returns
+// true and sets *bf); otherwise the dot must be recomputed in the defining
+// order.
+__device__ __forceinline__ bool cand_certified(float a, float E, float* bf) {
+  *bf = bf16_round(a);
+  const uint32_t ab = __float_as_uint(fabsf(*bf));
   if (ab >= (8u << 23) && ab < 0x7f800000u) {
     const float ulp = __uint_as_float((ab & 0x7f800000u) - (7u << 23));   // bf16 spacing above |bf|
     const float dn = (ab & 0x007f0000u) ? ulp : 0.5f * ulp;              // spacing below |bf|
-    const float d = fabsf(a) - fabsf(bf);                                // exact: same binade or adjacent
-    safe = (d + E < 0.5f * ulp) && (E - d < 0.5f * dn);
+    const float d = fabsf(a) - fabsf(*bf);                               // exact: same binade or adjacent
+    return (d + E < 0.5f * ulp) && (E - d < 0.5f * dn);
   }
-  const float b = safe ? bf : bf16_round(exact_dot(ta, r, tb, cr));
-  return __fadd_rn(__fmul_rn(b, 2.0f), nc2v);
+  return false;
+}
+
+// First-argmax update: a higher sim wins, an equal sim wins only with a
+// lower index, so candidates may be visited in any order.
+__device__ __forceinline__ void take_best(float sim, int idx, float& bsim, int& bidx) {
+  if (sim > bsim || (sim == bsim && idx < bidx)) {
+    bsim = sim;
+    bidx = idx;
+  }
 }
 
 template <int NCH, int EW>
@@ -359,20 +369,30 @@ __global__ void __launch_bounds__(32 * (EW + 1), 1)
         float x[32];
         tmem_ld32(lane_base + cpt * kChunkC + 32 * blk, x);
         tmem_ld_wait_regs(x);
+        const int col0 = gi * kGroupC + cpt * kChunkC + 32 * blk;
+        const int nv = min(32, k - col0);
+        const uint8_t* tb = sb + cpt * 2 * kHalfB;
+        // Certified candidates are taken now; the others queue in `pend`.
+        uint32_t pend = 0;
         if ((flags >> j) & 1u) {
-          const int col0 = gi * kGroupC + cpt * kChunkC + 32 * blk;
-          const int nv = min(32, k - col0);
-          const uint8_t* tb = sb + cpt * 2 * kHalfB;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float nv2 = i < nv ? nc2[col0 + i] : 0.f;
             if (i < nv && __fmaf_rn(x[i], 2.0f, nv2) >= T) {
-              const float sim = cand_sim(x[i], E, nv2, sa, r, tb, 32 * blk + i);
-              if (sim > bsim) {
-                bsim = sim;
-                bidx = col0 + i;
-              }
+              float bf;
+              if (cand_certified(x[i], E, &bf)) take_best(__fadd_rn(__fmul_rn(bf, 2.0f), nv2), col0 + i, bsim, bidx);
+              else pend |= 1u << i;
             }
+          }
+        }
+        // Queued candidates: each lane recomputes its next one as the
+        // sequential FMA chain, all lanes in parallel, one chain per round.
+        while (__any_sync(0xffffffffu, pend != 0u)) {
+          if (pend != 0u) {
+            const int i = __ffs(pend) - 1;
+            pend &= pend - 1u;
+            const float acc = exact_dot(sa, r, tb, 32 * blk + i);
+            take_best(__fadd_rn(__fmul_rn(bf16_round(acc), 2.0f), nc2[col0 + i]), col0 + i, bsim, bidx);
           }
         }
       }
