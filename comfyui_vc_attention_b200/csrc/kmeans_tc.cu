@@ -115,8 +115,22 @@ __device__ __forceinline__ uint4 swz_chunk(const uint8_t* tile, int half_bytes, 
   const int pos = (c & 7) ^ (r & 7);
   return *reinterpret_cast<const uint4*>(tile + (c >> 3) * half_bytes + r * 128 + (pos << 4));
 }
-__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// acc + a * b for the low (or high) bf16 halves of two words: the mixed
+// precision FMA rounds the exact a * b + acc once to fp32, the same result as
+// the fp32 FMA of the widened operands (bf16 values are exact in fp32).
+__device__ __forceinline__ float fma_lo(uint32_t a, uint32_t b, float acc) {
+  float d;
+  asm("{\n\t.reg .b16 a0, a1, b0, b1;\n\tmov.b32 {a0, a1}, %1;\n\tmov.b32 {b0, b1}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, a0, b0, %3;\n\t}\n" : "=f"(d) : "r"(a), "r"(b), "f"(acc));
+  return d;
+}
+__device__ __forceinline__ float fma_hi(uint32_t a, uint32_t b, float acc) {
+  float d;
+  asm("{\n\t.reg .b16 a0, a1, b0, b1;\n\tmov.b32 {a0, a1}, %1;\n\tmov.b32 {b0, b1}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, a1, b1, %3;\n\t}\n" : "=f"(d) : "r"(a), "r"(b), "f"(acc));
+  return d;
+}
 
 // Sequential fp32 FMA chain of a token row and a centroid row (both bf16 in
 // swizzled shared memory), channels in increasing order.
@@ -126,14 +140,14 @@ __device__ __noinline__ float exact_dot(const uint8_t* ta, int r, const uint8_t*
   for (int c = 0; c < 16; ++c) {
     const uint4 a = swz_chunk(ta, kHalfA, r, c);
     const uint4 b = swz_chunk(tb, kHalfB, cr, c);
-    acc = __fmaf_rn(bf_lo(a.x), bf_lo(b.x), acc);
-    acc = __fmaf_rn(bf_hi(a.x), bf_hi(b.x), acc);
-    acc = __fmaf_rn(bf_lo(a.y), bf_lo(b.y), acc);
-    acc = __fmaf_rn(bf_hi(a.y), bf_hi(b.y), acc);
-    acc = __fmaf_rn(bf_lo(a.z), bf_lo(b.z), acc);
-    acc = __fmaf_rn(bf_hi(a.z), bf_hi(b.z), acc);
-    acc = __fmaf_rn(bf_lo(a.w), bf_lo(b.w), acc);
-    acc = __fmaf_rn(bf_hi(a.w), bf_hi(b.w), acc);
+    acc = fma_lo(a.x, b.x, acc);
+    acc = fma_hi(a.x, b.x, acc);
+    acc = fma_lo(a.y, b.y, acc);
+    acc = fma_hi(a.y, b.y, acc);
+    acc = fma_lo(a.z, b.z, acc);
+    acc = fma_hi(a.z, b.z, acc);
+    acc = fma_lo(a.w, b.w, acc);
+    acc = fma_hi(a.w, b.w, acc);
   }
   return acc;
 }
@@ -287,14 +301,14 @@ __global__ void __launch_bounds__(32 * (EW + 1), 1)
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         const uint4 a4 = swz_chunk(sa, kHalfA, r, c);
-        vv = __fmaf_rn(bf_lo(a4.x), bf_lo(a4.x), vv);
-        vw = __fmaf_rn(bf_hi(a4.x), bf_hi(a4.x), vw);
-        vv = __fmaf_rn(bf_lo(a4.y), bf_lo(a4.y), vv);
-        vw = __fmaf_rn(bf_hi(a4.y), bf_hi(a4.y), vw);
-        vv = __fmaf_rn(bf_lo(a4.z), bf_lo(a4.z), vv);
-        vw = __fmaf_rn(bf_hi(a4.z), bf_hi(a4.z), vw);
-        vv = __fmaf_rn(bf_lo(a4.w), bf_lo(a4.w), vv);
-        vw = __fmaf_rn(bf_hi(a4.w), bf_hi(a4.w), vw);
+        vv = fma_lo(a4.x, a4.x, vv);
+        vw = fma_hi(a4.x, a4.x, vw);
+        vv = fma_lo(a4.y, a4.y, vv);
+        vw = fma_hi(a4.y, a4.y, vw);
+        vv = fma_lo(a4.z, a4.z, vv);
+        vw = fma_hi(a4.z, a4.z, vw);
+        vv = fma_lo(a4.w, a4.w, vv);
+        vw = fma_hi(a4.w, a4.w, vw);
       }
       vv += vw;
     }
@@ -372,16 +386,38 @@ __global__ void __launch_bounds__(32 * (EW + 1), 1)
         const int col0 = gi * kGroupC + cpt * kChunkC + 32 * blk;
         const int nv = min(32, k - col0);
         const uint8_t* tb = sb + cpt * 2 * kHalfB;
-        // Certified candidates are taken now; the others queue in `pend`.
-        uint32_t pend = 0;
+        // This token's candidates of the block as a bitmask (no branches),
+        // then the columns some lane flagged: certified candidates are taken
+        // now, the others queue in `pend`.
+        uint32_t cm = 0;
         if ((flags >> j) & 1u) {
+          if (nv == 32) {
+            const float4* nc4 = reinterpret_cast<const float4*>(nc2 + col0);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float nv2 = i < nv ? nc2[col0 + i] : 0.f;
-            if (i < nv && __fmaf_rn(x[i], 2.0f, nv2) >= T) {
+            for (int q = 0; q < 8; ++q) {
+              const float4 n4 = nc4[q];
+              cm |= (__fmaf_rn(x[4 * q], 2.0f, n4.x) >= T ? 1u : 0u) << (4 * q);
+              cm |= (__fmaf_rn(x[4 * q + 1], 2.0f, n4.y) >= T ? 1u : 0u) << (4 * q + 1);
+              cm |= (__fmaf_rn(x[4 * q + 2], 2.0f, n4.z) >= T ? 1u : 0u) << (4 * q + 2);
+              cm |= (__fmaf_rn(x[4 * q + 3], 2.0f, n4.w) >= T ? 1u : 0u) << (4 * q + 3);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < nv && __fmaf_rn(x[i], 2.0f, nc2[col0 + i]) >= T) cm |= 1u << i;
+          }
+        }
+        const uint32_t wcm = __reduce_or_sync(0xffffffffu, cm);
+        uint32_t pend = 0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if ((wcm >> i) & 1u) {                 // warp-uniform
+            if ((cm >> i) & 1u) {
               float bf;
-              if (cand_certified(x[i], E, &bf)) take_best(__fadd_rn(__fmul_rn(bf, 2.0f), nv2), col0 + i, bsim, bidx);
-              else pend |= 1u << i;
+              if (cand_certified(x[i], E, &bf))
+                take_best(__fadd_rn(__fmul_rn(bf, 2.0f), nc2[col0 + i]), col0 + i, bsim, bidx);
+              else
+                pend |= 1u << i;
             }
           }
         }
