@@ -50,6 +50,8 @@ WORKLOADS = {
                   spatial=None),
     "c3": dict(desc="dense FP8 VC-Attention, B1 H56 N65536 D128, ExpCast on, V-Smooth k=512",
                B=1, H=56, N=65536, D=128, expcast=True, sparse=False, k=512, block_rows=128, spatial=None),
+    "c3h8": dict(desc="profiling slice of the N=65536 dense shape: B1 H8 N65536 D128, ExpCast on, V-Smooth k=512",
+                 B=1, H=8, N=65536, D=128, expcast=True, sparse=False, k=512, block_rows=128, spatial=None),
     "c3nv": dict(desc="configs[3]: NVFP4 QK^T (E2M1, E4M3 per-16 scales, fp32 tensor scale per head) + FP8 PV, "
                       "B1 H56 N65536 D128, ExpCast on, V-Smooth k=512", B=1, H=56, N=65536, D=128, expcast=True,
                  sparse=False, k=512, block_rows=128, spatial=None, qk_fp4=True),
