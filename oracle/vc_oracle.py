@@ -578,9 +578,9 @@ def _exact_tile(q8s, qs_rows, k8_blk, ks_blk, v8_blk, vs_row, mu_row, valid, sm_
     return _tile_from_scores(s, v8_blk, vs_row, mu_row, valid, m_i, l_i, acc, expcast, beta)
 
 
-def _tile_from_scores(s, v8_blk, vs_row, mu_row, valid, m_i, l_i, acc, expcast, beta):
-    """The part of the exact tile after the scores: online max, P bytes, row
-    sum and the V-Smooth accumulation (triton_attn.py:272-318)."""
+def _tile_softmax(s, valid, m_i, expcast, beta):
+    """Online max, rescale factor and P values of one tile's scores
+    (triton_attn.py:272-295): returns (m_new, alpha, p8)."""
     s = np.where(valid[None, :], s, F32(-1e30))
     m_new = np.maximum(m_i, s.max(-1))
     m_new = np.where(np.isneginf(m_new), F32(0), m_new).astype(np.float32)
@@ -592,6 +592,13 @@ def _tile_from_scores(s, v8_blk, vs_row, mu_row, valid, m_i, l_i, acc, expcast, 
     else:
         e = np.exp2(((s - m_new[:, None]) * F32(LOG2E)).astype(np.float32)).astype(np.float32)
         p8 = e4m3_decode(e4m3_encode((e * F32(P_SCALE)).astype(np.float32)))
+    return m_new, alpha, p8
+
+
+def _tile_from_scores(s, v8_blk, vs_row, mu_row, valid, m_i, l_i, acc, expcast, beta):
+    """The part of the exact tile after the scores: online max, P bytes, row
+    sum and the V-Smooth accumulation (triton_attn.py:272-318)."""
+    m_new, alpha, p8 = _tile_softmax(s, valid, m_i, expcast, beta)
     r = (p8.sum(-1, dtype=np.float32) / F32(P_SCALE)).astype(np.float32)
     tile = np.matmul(p8, v8_blk).astype(np.float32)
     acc = (acc * alpha[:, None]).astype(np.float32)
@@ -639,6 +646,64 @@ def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_
                     vs[gi, j], mu[gi, j], np.arange(js, je) < n, sm_scale, m_i, l_i, acc,
                     expcast, beta)
             out[gi, sm:em] = acc / l_i[:, None]
+    return out
+
+
+def attention_codes_units(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_m: int,
+                          sm_scale: float, expcast: bool = False, beta: float = -0.35,
+                          floor_exp: int = -120) -> np.ndarray:
+    """attention_codes (triton_attn.py:203-322) with the output accumulated the
+    way a kernel that lets the P.V tensor-core MMA add into O itself must: in
+    units of the current value block's scale.  With u_j = max(vs_j, floor) per
+    channel, O_hat holds acc * 448 / u_j; before block j's P.V it gets block
+    j-1's mean term R_{j-1} * mu_{j-1} and the factor alpha_j * u_{j-1} / u_j,
+    then the MMA adds P_j . V8_j unscaled; the output is O_hat * u_last / 448 / l.
+    floor = max|V_c| * 448 * 2^floor_exp per channel keeps O_hat finite when a
+    block's scale sits at the amax clamp (a constant channel); such a block's
+    codes are then counted at the floor's scale.  The result differs from
+    attention_codes only by float32 rounding (and, for floored blocks, by at
+    most 448 * 2^floor_exp of max|V_c|).  Returns (G, N, D) float32.
+    """
+    q8 = e4m3_decode(prep["q"])
+    k8 = e4m3_decode(prep["k"])
+    v8 = e4m3_decode(prep["v"])
+    qs, ks, vs, mu = prep["q_scale"], prep["k_scale"], prep["v_scale"], prep["mu"]
+    g, n_pad, d = q8.shape
+    nb = n_pad // block_rows
+    out = np.zeros((g, n, d), np.float32)
+    for gi in range(g):
+        # max |V_c| over the head: |mean| + the residual bound 448 * scale
+        vmax = np.max(np.abs(mu[gi] * vs[gi]) + F32(P_SCALE) * vs[gi], axis=0).astype(np.float32)
+        floor = (vmax * F32(P_SCALE) * F32(2.0 ** floor_exp)).astype(np.float32)
+        for _, sm in _row_starts(n, block_m, None):
+            em = min(n, sm + block_m)
+            rows = em - sm
+            m_i = np.full(rows, -np.inf, np.float32)
+            l_i = np.zeros(rows, np.float32)
+            oh = np.zeros((rows, d), np.float32)
+            u_prev = r_prev = mu_prev = None
+            for j in range(nb):
+                js, je = j * block_rows, (j + 1) * block_rows
+                sd = np.matmul(q8[gi, sm:em], k8[gi, js:je].T).astype(np.float32)
+                sc = (sd * (qs[gi, sm:em, None] * ks[gi, None, js:je]).astype(np.float32)).astype(np.float32)
+                sc = (sc * F32(sm_scale)).astype(np.float32)
+                m_new, alpha, p8 = _tile_softmax(sc, np.arange(js, je) < n, m_i, expcast, beta)
+                r = p8.sum(-1, dtype=np.float32)                 # un-normalised row sum
+                u = np.maximum(vs[gi, j], floor).astype(np.float32)
+                if u_prev is not None:
+                    oh = (oh + (r_prev[:, None] * mu_prev[None, :]).astype(np.float32)).astype(np.float32)
+                    f = (alpha[:, None] * (u_prev / u).astype(np.float32)[None, :]).astype(np.float32)
+                    oh = (oh * f).astype(np.float32)
+                else:
+                    oh = (oh * alpha[:, None]).astype(np.float32)
+                oh = (oh + np.matmul(p8, v8[gi, js:je]).astype(np.float32)).astype(np.float32)
+                l_i = (l_i * alpha + (r / F32(P_SCALE)).astype(np.float32)).astype(np.float32)
+                # mu is in units of vs_j; in units of u_j it carries vs_j / u_j
+                u_prev, r_prev, m_i = u, r, m_new
+                mu_prev = (mu[gi, j] * (vs[gi, j] / u).astype(np.float32)).astype(np.float32)
+            oh = (oh + (r_prev[:, None] * mu_prev[None, :]).astype(np.float32)).astype(np.float32)
+            o = (oh * (u_prev / F32(P_SCALE)).astype(np.float32)[None, :]).astype(np.float32)
+            out[gi, sm:em] = (o / l_i[:, None]).astype(np.float32)
     return out
 
 
