@@ -337,17 +337,26 @@ __global__ void update_kernel(vcattn_bhnd v, int H, int N, int D, int k, int nch
   const int start = offsets[base + static_cast<int64_t>(c) * nchunks];
   const int end = (c + 1 < k) ? offsets[base + static_cast<int64_t>(c + 1) * nchunks] : N;
   const int32_t* mem = sorted + static_cast<int64_t>(g) * N;
+  // The sum runs in member order (one fp32 add after another); only the
+  // loads run ahead: kB member values are in flight per batch, and the next
+  // batch's member indices are fetched while the current values arrive, so a
+  // large cluster costs about one memory round trip per kB members.
+  constexpr int kB = 8;
   float acc = 0.f;
-  int i = start;
-  for (; i + 4 <= end; i += 4) {
-    const float x0 = load_bf16_value<DT>(v, b, h, mem[i], d);
-    const float x1 = load_bf16_value<DT>(v, b, h, mem[i + 1], d);
-    const float x2 = load_bf16_value<DT>(v, b, h, mem[i + 2], d);
-    const float x3 = load_bf16_value<DT>(v, b, h, mem[i + 3], d);
-    acc = __fadd_rn(acc, x0); acc = __fadd_rn(acc, x1);
-    acc = __fadd_rn(acc, x2); acc = __fadd_rn(acc, x3);
+  int nid[kB];
+#pragma unroll
+  for (int u = 0; u < kB; ++u) nid[u] = (start + u < end) ? mem[start + u] : 0;
+  for (int i = start; i < end; i += kB) {
+    float x[kB];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) x[u] = (i + u < end) ? load_bf16_value<DT>(v, b, h, nid[u], d) : 0.f;
+    const int in = i + kB;
+#pragma unroll
+    for (int u = 0; u < kB; ++u) nid[u] = (in + u < end) ? mem[in + u] : 0;
+#pragma unroll
+    for (int u = 0; u < kB; ++u)
+      if (i + u < end) acc = __fadd_rn(acc, x[u]);
   }
-  for (; i < end; ++i) acc = __fadd_rn(acc, load_bf16_value<DT>(v, b, h, mem[i], d));
   const int cnt = end - start;
   const int64_t o = (static_cast<int64_t>(g) * k + c) * D + d;
   const float cntc = static_cast<float>(cnt > 1 ? cnt : 1);
