@@ -136,11 +136,12 @@ struct QKArgs {
   float sm_scale;
 };
 
-// STATS: the routing block statistics are requested (blk_mean / blk_qbar);
-// without them the kernel keeps no float64 accumulators and fits four CTAs
-// per SM (64 registers), with them three (72 registers).
+// STATS: the routing block statistics are requested (blk_mean / blk_qbar),
+// kept as float64 accumulators.  Both variants run four CTAs per SM (64
+// registers): the kernel is latency-bound, and the statistics variant is
+// faster at four CTAs with a few bytes of spills than at three without.
 template <int DT, int D, bool STATS>
-__global__ void __launch_bounds__(256, STATS ? 3 : 4) quant_rows_kernel(QKArgs a) {
+__global__ void __launch_bounds__(256, 4) quant_rows_kernel(QKArgs a) {
   using RM = RowMap<D>;
   const int g = blockIdx.y;
   const int b = g / a.H, h = g % a.H;
