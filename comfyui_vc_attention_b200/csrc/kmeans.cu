@@ -323,10 +323,30 @@ __global__ void __launch_bounds__(kAssignThreads) scatter_kernel(
   if (pos >= 0 && pos < N) sorted[static_cast<int64_t>(g) * N + pos] = t;
 }
 
+// Clusters above kBigCluster members with bf16 rows at 16-byte aligned
+// strides are summed by the BIG launch, which stages member rows in shared
+// memory; the other launch leaves them out.
+constexpr int kBigCluster = 512;
+constexpr int kStageM = 64;   // member rows per staged batch (64 x 256 B)
+
+__device__ __forceinline__ bool staged_rows_ok(const vcattn_bhnd& v, int D) {
+  const uint64_t bits = reinterpret_cast<uint64_t>(v.data) | static_cast<uint64_t>(v.sb * 2) |
+                        static_cast<uint64_t>(v.sh * 2) | static_cast<uint64_t>(v.sn * 2);
+  return D == 128 && (bits & 15u) == 0 && v.sb >= 0 && v.sh >= 0 && v.sn >= 0;
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
 // grouping.py:103-124: fp32 sums in token order, / max(count, 1), re-seed
 // clusters with count <= 1, bf16.  One CTA per (cluster, head), D threads,
 // thread = channel.
-template <int DT>
+template <int DT, bool BIG>
 __global__ void update_kernel(vcattn_bhnd v, int H, int N, int D, int k, int nchunks,
                               const int32_t* __restrict__ offsets, const int32_t* __restrict__ sorted,
                               const float* __restrict__ seeds, float* __restrict__ cent,
@@ -337,12 +357,57 @@ __global__ void update_kernel(vcattn_bhnd v, int H, int N, int D, int k, int nch
   const int start = offsets[base + static_cast<int64_t>(c) * nchunks];
   const int end = (c + 1 < k) ? offsets[base + static_cast<int64_t>(c + 1) * nchunks] : N;
   const int32_t* mem = sorted + static_cast<int64_t>(g) * N;
+  const bool big = DT == VCATTN_DTYPE_BF16 && end - start > kBigCluster && staged_rows_ok(v, D);
+  if (big != BIG) return;   // uniform per CTA: the other launch owns this cluster
+  float acc = 0.f;
+  if constexpr (BIG && DT == VCATTN_DTYPE_BF16) {
+    // Member rows in batches of kStageM, gathered into shared memory with
+    // cp.async (16 bytes per copy) while the previous batch is summed; each
+    // thread adds its channel of the staged rows in member order, so the sum
+    // is the same sequence of fp32 adds as the direct loop below.
+    __shared__ __align__(16) uint16_t rows[2][kStageM][128];
+    __shared__ int sidx[2][kStageM];
+    const __nv_bfloat16* vb = static_cast<const __nv_bfloat16*>(v.data) + b * v.sb + h * v.sh;
+    const int cnt = end - start;
+    const int nbatch = (cnt + kStageM - 1) / kStageM;
+    auto member = [&](int bt) -> int {
+      const int m = start + bt * kStageM + d;
+      return (d < kStageM && bt < nbatch && m < end) ? mem[m] : 0;
+    };
+    auto issue = [&](int bt, int buf) {
+      const int nm = min(kStageM, cnt - bt * kStageM);
+      for (int q = d; q < nm * 16; q += 128) {
+        const int u = q >> 4, ch = q & 15;
+        cp_async16(&rows[buf][u][ch * 8], vb + static_cast<int64_t>(sidx[buf][u]) * v.sn + ch * 8);
+      }
+      cp_async_commit();
+    };
+    if (d < kStageM) sidx[0][d] = member(0);
+    __syncthreads();
+    issue(0, 0);
+    int pend = member(1);
+    for (int bt = 0; bt < nbatch; ++bt) {
+      const int cur = bt & 1;
+      if (bt + 1 < nbatch) {
+        if (d < kStageM) sidx[cur ^ 1][d] = pend;
+        __syncthreads();
+        issue(bt + 1, cur ^ 1);
+        pend = member(bt + 2);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+      const int nm = min(kStageM, cnt - bt * kStageM);
+      for (int u = 0; u < nm; ++u) acc = __fadd_rn(acc, __uint_as_float(static_cast<uint32_t>(rows[cur][u][d]) << 16));
+      __syncthreads();   // rows[cur] is refilled by the next iteration's copies
+    }
+  } else {
   // The sum runs in member order (one fp32 add after another); only the
   // loads run ahead: kB member values are in flight per batch, and the next
   // batch's member indices are fetched while the current values arrive, so a
   // large cluster costs about one memory round trip per kB members.
   constexpr int kB = 8;
-  float acc = 0.f;
   int nid[kB];
 #pragma unroll
   for (int u = 0; u < kB; ++u) nid[u] = (start + u < end) ? mem[start + u] : 0;
@@ -356,6 +421,7 @@ __global__ void update_kernel(vcattn_bhnd v, int H, int N, int D, int k, int nch
 #pragma unroll
     for (int u = 0; u < kB; ++u)
       if (i + u < end) acc = __fadd_rn(acc, x[u]);
+  }
   }
   const int cnt = end - start;
   const int64_t o = (static_cast<int64_t>(g) * k + c) * D + d;
@@ -410,8 +476,11 @@ cudaError_t kmeans_impl(const KMeansParams& p, cudaStream_t st) {
   const int iters = p.iters;
   for (int it = 0; it < iters; ++it) {
     sort_pass(nullptr, k, p.perm_out);
-    update_kernel<DT><<<dim3(k, G), D, 0, st>>>(*p.v, p.H, p.N, D, k, nchunks, w.offsets, p.perm_out,
-                                               w.seeds, w.cent, nullptr, w.cb16, w.c2);
+    update_kernel<DT, false><<<dim3(k, G), D, 0, st>>>(*p.v, p.H, p.N, D, k, nchunks, w.offsets, p.perm_out,
+                                                      w.seeds, w.cent, nullptr, w.cb16, w.c2);
+    if constexpr (DT == VCATTN_DTYPE_BF16)
+      update_kernel<DT, true><<<dim3(k, G), D, 0, st>>>(*p.v, p.H, p.N, D, k, nchunks, w.offsets, p.perm_out,
+                                                       w.seeds, w.cent, nullptr, w.cb16, w.c2);
   }
   copy_centroids_kernel<<<static_cast<unsigned>((static_cast<int64_t>(G) * k * D + 255) / 256), 256, 0, st>>>(
       w.cent, p.centroids_out, static_cast<int64_t>(G) * k * D);
