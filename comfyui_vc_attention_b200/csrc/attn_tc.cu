@@ -3,8 +3,9 @@
 // Same semantics as triton_attn.py:203-322: for every KV tile j (one value
 // block of BR keys)
 //   s   = (q8 . k8) * qs * ks * sm_scale
-//   P   = ExpCast byte of s against the running row max (one FMA form), or
-//         E4M3(exp2((s - m) * log2e) * 448)
+//   P   = ExpCast byte of s against the running row max (one FMA form, or
+//         with VCATTN_EXPCAST_EXACT the operation order of expcast.py:67-69),
+//         or E4M3(exp2((s - m) * log2e) * 448)
 //   acc = alpha * acc + (P @ V8) * (vs / 448) + (rowsum(P) / 448) * (mu * vs)
 //   l   = alpha * l + rowsum(P) / 448 ;  O = acc / l
 //
@@ -100,7 +101,9 @@ struct TcArgs {
   int64_t osb, osh, osn;
 };
 
-template <int BR, bool EXPCAST, int ODT>
+// ECM: 0 = E4M3 of exp2, 1 = one-FMA ExpCast, 2 = ExpCast in the reference's
+// operation order on s = (S * (qs * ks)) * sm_scale (parity runs).
+template <int BR, int ECM, int ODT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
@@ -272,7 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // fma.sat(x, A/128, B/128) so the clamp at 0 is free and the /128 scale
     // makes a + 98304 round the code to an integer in the low bits.
     const float As = __fmul_rn(8.0f * kLog2e, qsm) * (1.0f / 128.0f);
-    const float Ae = __fmul_rn(qsm, kLog2e);
+    // The row max is kept in x units (x = S * ks), or in score units s for ECM 2.
+    const float Ae = (ECM == 2) ? kLog2e : __fmul_rn(qsm, kLog2e);
     float m = -INFINITY;
     for (int j = 0; j < nb; ++j) {
       const int b = j & 1, ring = j % kRing, s = j % kStages;
@@ -288,11 +292,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) reg_fence(*reinterpret_cast<float(*)[32]>(x + 32 * ch));
       const float4* k4 = reinterpret_cast<const float4*>(sm.ks[s]);
+      if constexpr (ECM == 2) {
+        // s = (S * (qs * ks)) * sm_scale, rounded at each step
 #pragma unroll
-      for (int q = 0; q < BR / 4; ++q) {
-        const float4 kv = k4[q];
-        mul2(x[4 * q], x[4 * q + 1], kv.x, kv.y);
-        mul2(x[4 * q + 2], x[4 * q + 3], kv.z, kv.w);
+        for (int q = 0; q < BR / 4; ++q) {
+          const float4 kv = k4[q];
+          x[4 * q] = __fmul_rn(__fmul_rn(x[4 * q], __fmul_rn(qs, kv.x)), a.sm_scale);
+          x[4 * q + 1] = __fmul_rn(__fmul_rn(x[4 * q + 1], __fmul_rn(qs, kv.y)), a.sm_scale);
+          x[4 * q + 2] = __fmul_rn(__fmul_rn(x[4 * q + 2], __fmul_rn(qs, kv.z)), a.sm_scale);
+          x[4 * q + 3] = __fmul_rn(__fmul_rn(x[4 * q + 3], __fmul_rn(qs, kv.w)), a.sm_scale);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < BR / 4; ++q) {
+          const float4 kv = k4[q];
+          mul2(x[4 * q], x[4 * q + 1], kv.x, kv.y);
+          mul2(x[4 * q + 2], x[4 * q + 3], kv.z, kv.w);
+        }
       }
       const int valid = a.N - j * BR;                 // keys >= valid are padding
       if (valid < BR) {
@@ -311,7 +327,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float mn = fmax3(m0, m1, fmaxf(m2, m3));
       const float al = (m == -INFINITY) ? 0.f : exp2f(__fmul_rn(__fsub_rn(m, mn), Ae));
       // P words: chunk ch (keys 32 ch .. 32 ch + 31) to columns 8 ch .. 8 ch + 7
-      if constexpr (EXPCAST) {
+      if constexpr (ECM == 2) {
+        // expcast.py:67-69: u = (s - m) * log2e + 8 ; c = u * 8 + (56 + beta)
+        // (u * 8 is exact, so one FMA rounds the sum once, as torch does)
+        const float c0 = a.c120 - 64.0f;
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch) {
+          uint32_t packed[8];
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const float* xc = x + 32 * ch + 4 * w;
+            uint32_t word = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float u = __fadd_rn(__fmul_rn(__fsub_rn(xc[e], mn), kLog2e), 8.0f);
+              const float c = fminf(fmaxf(rintf(__fmaf_rn(u, 8.0f, c0)), 0.0f), 120.0f);
+              word |= static_cast<uint32_t>(c) << (8 * e);
+            }
+            packed[w] = word;
+          }
+          tmem_st8(sb + 8 * ch, packed);
+        }
+      } else if constexpr (ECM == 1) {
         const float Bs = __fmaf_rn(-As, mn, a.c120 * (1.0f / 128.0f));
 #pragma unroll
         for (int ch = 0; ch < NCH; ++ch) {
@@ -474,7 +511,7 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BR, bool EC, int ODT>
+template <int BR, int EC, int ODT>
 cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   const uint64_t rows = static_cast<uint64_t>(p.B) * p.H * p.n_pad;
@@ -506,14 +543,17 @@ cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
 
 template <int BR>
 cudaError_t dispatch_tc(const AttnParams& p, cudaStream_t st) {
-  const bool ec = (p.flags & VCATTN_EXPCAST) != 0;
+  const int ec = (p.flags & VCATTN_EXPCAST) ? ((p.flags & VCATTN_EXPCAST_EXACT) ? 2 : 1) : 0;
   switch (p.out_dtype) {
     case VCATTN_DTYPE_BF16:
-      return ec ? launch_tc<BR, true, VCATTN_DTYPE_BF16>(p, st) : launch_tc<BR, false, VCATTN_DTYPE_BF16>(p, st);
+      return ec == 1 ? launch_tc<BR, 1, VCATTN_DTYPE_BF16>(p, st)
+                     : ec == 2 ? launch_tc<BR, 2, VCATTN_DTYPE_BF16>(p, st) : launch_tc<BR, 0, VCATTN_DTYPE_BF16>(p, st);
     case VCATTN_DTYPE_F16:
-      return ec ? launch_tc<BR, true, VCATTN_DTYPE_F16>(p, st) : launch_tc<BR, false, VCATTN_DTYPE_F16>(p, st);
+      return ec == 1 ? launch_tc<BR, 1, VCATTN_DTYPE_F16>(p, st)
+                     : ec == 2 ? launch_tc<BR, 2, VCATTN_DTYPE_F16>(p, st) : launch_tc<BR, 0, VCATTN_DTYPE_F16>(p, st);
     default:
-      return ec ? launch_tc<BR, true, VCATTN_DTYPE_F32>(p, st) : launch_tc<BR, false, VCATTN_DTYPE_F32>(p, st);
+      return ec == 1 ? launch_tc<BR, 1, VCATTN_DTYPE_F32>(p, st)
+                     : ec == 2 ? launch_tc<BR, 2, VCATTN_DTYPE_F32>(p, st) : launch_tc<BR, 0, VCATTN_DTYPE_F32>(p, st);
   }
 }
 

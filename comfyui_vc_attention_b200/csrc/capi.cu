@@ -9,6 +9,7 @@
 #include <string>
 
 #include "kernels.cuh"
+#include "tc_math.cuh"
 
 namespace vcattn {
 
@@ -25,25 +26,42 @@ __global__ void fp4_encode_kernel(const float* __restrict__ x, int64_t n, uint8_
   if (i < n) out[i] = static_cast<uint8_t>(e2m1x2(x[i], 0.f) & 0xf);
 }
 
-// mode 1: the operation sequence of expcast.py:67-69; mode 0: one FMA per
-// element with the per-row bias folded, c = fma(s, 8*log2e, 64 + 56 + beta -
-// 8*log2e*m), which is the form the attention kernel evaluates.
-__global__ void expcast_kernel(const float* __restrict__ s, const float* __restrict__ m, int rows, int cols,
-                               float c0, float c120, int mode, uint8_t* __restrict__ out) {
+// mode 1: the operation sequence of expcast.py:67-69 (what the attention
+// kernel evaluates under VCATTN_EXPCAST_EXACT).
+__global__ void expcast_exact_kernel(const float* __restrict__ s, const float* __restrict__ m, int rows, int cols,
+                                     float c0, uint8_t* __restrict__ out) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<int64_t>(rows) * cols) return;
   const int r = static_cast<int>(i / cols);
-  const float sv = s[i], mv = m[r];
-  float c;
-  if (mode == 1) {
-    const float u = __fadd_rn(__fmul_rn(__fsub_rn(sv, mv), kLog2e), 8.0f);
-    c = __fmaf_rn(u, 8.0f, c0);
-  } else {
-    const float k8 = 8.0f * kLog2e;
-    c = __fmaf_rn(sv, k8, __fmaf_rn(-k8, mv, c120));
-  }
-  c = fminf(fmaxf(rintf(c), 0.0f), 120.0f);
+  const float u = __fadd_rn(__fmul_rn(__fsub_rn(s[i], m[r]), kLog2e), 8.0f);
+  const float c = fminf(fmaxf(rintf(__fmaf_rn(u, 8.0f, c0)), 0.0f), 120.0f);
   out[i] = static_cast<uint8_t>(c);
+}
+
+// mode 0: the attention kernels' own one-FMA form, through the same device
+// function (tc::expcast4) and the same folding of the per-row constants: with
+// the score s = x * qsm (here qsm = 1, x = s), As = 8 log2e qsm / 128 and
+// Bs = fma(-As, m, (64 + 56 + beta) / 128); the code is fma.sat(x, As, Bs)
+// rounded by the 98304 magic add.  Four consecutive columns per thread.
+__global__ void expcast_fast_kernel(const float* __restrict__ s, const float* __restrict__ m, int rows, int cols,
+                                    float c120, uint8_t* __restrict__ out) {
+  const int quads = (cols + 3) / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(rows) * quads) return;
+  const int r = static_cast<int>(i / quads);
+  const int c = static_cast<int>(i % quads) * 4;
+  const float qsm = 1.0f;
+  const float As = __fmul_rn(8.0f * kLog2e, qsm) * (1.0f / 128.0f);
+  const float Bs = __fmaf_rn(-As, m[r], c120 * (1.0f / 128.0f));
+  const float* row = s + static_cast<int64_t>(r) * cols;
+  float x[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) x[e] = (c + e < cols) ? row[c + e] : -INFINITY;
+  const uint32_t word = tc::expcast4(x[0], x[1], x[2], x[3], As, Bs);
+  uint8_t* o = out + static_cast<int64_t>(r) * cols + c;
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (c + e < cols) o[e] = static_cast<uint8_t>(word >> (8 * e));
 }
 
 cudaError_t launch_codecs_e4m3(const float* x, int64_t n, uint8_t* out, cudaStream_t st) {
@@ -56,10 +74,15 @@ cudaError_t launch_codecs_fp4(const float* x, int64_t n, uint8_t* out, cudaStrea
 }
 cudaError_t launch_expcast(const float* s, const float* m, int rows, int cols, double beta, int mode,
                            uint8_t* out, cudaStream_t st) {
-  const int64_t n = static_cast<int64_t>(rows) * cols;
   const float c0 = static_cast<float>(56.0 + beta);
   const float c120 = static_cast<float>(64.0 + 56.0 + beta);
-  if (n > 0) expcast_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(s, m, rows, cols, c0, c120, mode, out);
+  if (mode == 1) {
+    const int64_t n = static_cast<int64_t>(rows) * cols;
+    if (n > 0) expcast_exact_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(s, m, rows, cols, c0, out);
+  } else {
+    const int64_t n = static_cast<int64_t>(rows) * ((cols + 3) / 4);
+    if (n > 0) expcast_fast_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(s, m, rows, cols, c120, out);
+  }
   return cudaGetLastError();
 }
 
@@ -116,6 +139,39 @@ namespace vcattn {
 // vcattn_last_error().
 int record_error(int code, const char* msg) { return fail(code, msg); }
 void clear_error() { g_last_error.clear(); }
+bool fault_injected(const char* entry_point) { return injected(entry_point); }
+
+// Argument checks of vcattn_prepare_fp8, shared with vcattn_prepare_fp8_noalloc
+// (everything but the workspace).  Messages start with `name`.
+int prepare_fp8_checks(const char* name, const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_bhnd* v,
+                       int dtype, int B, int H, int N, int D, const int32_t* perm, int perm_rows, int block_rows,
+                       const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
+                       const uint8_t* v8, const float* v_scale, const float* mu, const uint8_t* v8t,
+                       const vcattn_route_stats* route) {
+  const std::string n(name);
+  VC_CHECK(dtype_ok(dtype), n + ": unsupported dtype");
+  VC_CHECK(D == 64 || D == 128, n + ": D must be 64 or 128");
+  VC_CHECK(B > 0 && H > 0 && N > 0, n + ": empty shape");
+  VC_CHECK(block_rows == 64 || block_rows == 128, n + ": block_rows must be 64 or 128");
+  VC_CHECK(view_ok(q, dtype) && view_ok(k, dtype) && view_ok(v, dtype),
+           n + ": q/k/v must be 16-byte aligned with 16-byte multiple strides");
+  VC_CHECK(perm == nullptr || perm_rows == 1 || perm_rows == B * H, n + ": perm_rows must be 1 or G");
+  // Q (or K) codes are skipped when both their code and scale buffers are
+  // null (the NVFP4 path only needs V here); routing needs both.
+  VC_CHECK((q8 == nullptr) == (q_scale == nullptr) && (k8 == nullptr) == (k_scale == nullptr),
+           n + ": q8/q_scale and k8/k_scale must be given (or left out) together");
+  VC_CHECK(v_scale && mu && (v8 || v8t), n + ": null output");
+  VC_CHECK(route == nullptr || (q8 && k8), n + ": routing statistics need the Q and K codes");
+  VC_CHECK((q8 == nullptr || aligned16(q8)) && (k8 == nullptr || aligned16(k8)) && (v8 == nullptr || aligned16(v8)) &&
+               (v8t == nullptr || aligned16(v8t)),
+           n + ": code buffers must be 16-byte aligned");
+  const int n_pad = (N + block_rows - 1) / block_rows * block_rows;
+  if (route) {
+    VC_CHECK(route->q_block == 64 || route->q_block == 128, n + ": route q_block must be 64 or 128");
+    VC_CHECK(n_pad % route->q_block == 0, n + ": n_pad must be a multiple of q_block");
+  }
+  return VCATTN_OK;
+}
 }  // namespace vcattn
 
 extern "C" {
@@ -173,28 +229,11 @@ int vcattn_prepare_fp8(const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_
                        void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error.clear();
   if (injected("vcattn_prepare_fp8")) return fail(VCATTN_ERR_INJECTED, "vcattn_prepare_fp8: injected fault");
-  VC_CHECK(dtype_ok(dtype), "vcattn_prepare_fp8: unsupported dtype");
-  VC_CHECK(D == 64 || D == 128, "vcattn_prepare_fp8: D must be 64 or 128");
-  VC_CHECK(B > 0 && H > 0 && N > 0, "vcattn_prepare_fp8: empty shape");
-  VC_CHECK(block_rows == 64 || block_rows == 128, "vcattn_prepare_fp8: block_rows must be 64 or 128");
-  VC_CHECK(view_ok(q, dtype) && view_ok(k, dtype) && view_ok(v, dtype),
-           "vcattn_prepare_fp8: q/k/v must be 16-byte aligned with 16-byte multiple strides");
-  VC_CHECK(perm == nullptr || perm_rows == 1 || perm_rows == B * H, "vcattn_prepare_fp8: perm_rows must be 1 or G");
-  // Q (or K) codes are skipped when both their code and scale buffers are
-  // null (the NVFP4 path only needs V here); routing needs both.
-  VC_CHECK((q8 == nullptr) == (q_scale == nullptr) && (k8 == nullptr) == (k_scale == nullptr),
-           "vcattn_prepare_fp8: q8/q_scale and k8/k_scale must be given (or left out) together");
-  VC_CHECK(v_scale && mu && (v8 || v8t), "vcattn_prepare_fp8: null output");
-  VC_CHECK(route == nullptr || (q8 && k8), "vcattn_prepare_fp8: routing statistics need the Q and K codes");
-  VC_CHECK((q8 == nullptr || aligned16(q8)) && (k8 == nullptr || aligned16(k8)) && (v8 == nullptr || aligned16(v8)) &&
-               (v8t == nullptr || aligned16(v8t)),
-           "vcattn_prepare_fp8: code buffers must be 16-byte aligned");
+  const int rc = prepare_fp8_checks("vcattn_prepare_fp8", q, k, v, dtype, B, H, N, D, perm, perm_rows, block_rows,
+                                    q8, q_scale, k8, k_scale, v8, v_scale, mu, v8t, route);
+  if (rc != VCATTN_OK) return rc;
   const int G = B * H;
   const int n_pad = (N + block_rows - 1) / block_rows * block_rows;
-  if (route) {
-    VC_CHECK(route->q_block == 64 || route->q_block == 128, "vcattn_prepare_fp8: route q_block must be 64 or 128");
-    VC_CHECK(n_pad % route->q_block == 0, "vcattn_prepare_fp8: n_pad must be a multiple of q_block");
-  }
   const size_t need = prepare_workspace_bytes(G, N, D);
   if ((flags & VCATTN_SMOOTH_K) && k8 != nullptr && (workspace == nullptr || workspace_bytes < need))
     return fail(VCATTN_ERR_WORKSPACE, "vcattn_prepare_fp8: workspace too small (need " + std::to_string(need) + " bytes)");

@@ -13,12 +13,17 @@
 // code cannot pass the array's name to a kernel (on the host the name is only
 // a stand-in, not a device address), so the first call on each device looks
 // the address up with cudaGetSymbolAddress while that device is current and
-// caches it; that first call should come before any stream capture.
+// caches it; that first call should come before any stream capture.  The cache
+// remembers which CUDA context the address belongs to: after a
+// cudaDeviceReset() the device gets a new primary context (and a new copy of
+// the array), and the next call looks the address up again.
 //
 // All calls share the array and it keeps the last call's contents.  Nothing
 // in it needs to start at zero: every partial sum is written before it is
 // read.  Calls that overlap on the GPU (on different streams, or from
 // different threads) race on the array and must be serialised by the caller.
+#include <cuda.h>
+
 #include <mutex>
 #include <string>
 
@@ -27,6 +32,12 @@
 namespace vcattn {
 int record_error(int code, const char* msg);
 void clear_error();
+bool fault_injected(const char* entry_point);
+int prepare_fp8_checks(const char* name, const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_bhnd* v,
+                       int dtype, int B, int H, int N, int D, const int32_t* perm, int perm_rows, int block_rows,
+                       const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
+                       const uint8_t* v8, const float* v_scale, const float* mu, const uint8_t* v8t,
+                       const vcattn_route_stats* route);
 }  // namespace vcattn
 
 namespace {
@@ -36,32 +47,64 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_prepare_scratch[kScratchBytes];
 
-std::mutex g_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
+struct ScratchSlot {
+  void* ptr = nullptr;
+  unsigned long long ctx_id = 0;
+};
 
-// Device address of g_prepare_scratch on the current device (set up once).
+std::mutex g_mu;
+ScratchSlot g_slot[kMaxDevices];
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id (for the life of the process) of the calling thread's current
+// context, or 0 when it cannot be read.
+unsigned long long current_ctx_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_prepare_scratch on the current device (looked up once
+// per device and context).
 cudaError_t scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_prepare_scratch);
-    if (e != cudaSuccess) return e;
-    g_scratch_ptr[dev] = p;
+  ScratchSlot& slot = g_slot[dev];
+  if (slot.ptr != nullptr) {
+    const unsigned long long id = current_ctx_id();
+    if (id != 0 && id == slot.ctx_id) {
+      *out = slot.ptr;
+      return cudaSuccess;
+    }
   }
-  *out = g_scratch_ptr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_prepare_scratch);   // also makes the primary context current
+  if (e != cudaSuccess) return e;
+  slot.ptr = p;
+  slot.ctx_id = current_ctx_id();
+  *out = p;
   return cudaSuccess;
-}
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-bool view_ok(const vcattn_bhnd* v, int dtype) {
-  if (v == nullptr || v->data == nullptr || !aligned16(v->data)) return false;
-  const int64_t q = 16 / (dtype == VCATTN_DTYPE_F32 ? 4 : 2);
-  return (v->sb % q) == 0 && (v->sh % q) == 0 && (v->sn % q) == 0;
 }
 
 int arg_error(const std::string& msg) { return vcattn::record_error(VCATTN_ERR_ARG, msg.c_str()); }
@@ -75,32 +118,22 @@ extern "C" VCATTN_API int vcattn_prepare_fp8_noalloc(
     void* stream) {
   const char* fn = "vcattn_prepare_fp8_noalloc";
   vcattn::clear_error();
-  if (!(dtype == VCATTN_DTYPE_BF16 || dtype == VCATTN_DTYPE_F16 || dtype == VCATTN_DTYPE_F32))
-    return arg_error(std::string(fn) + ": unsupported dtype");
+  if (vcattn::fault_injected(fn))
+    return vcattn::record_error(VCATTN_ERR_INJECTED, "vcattn_prepare_fp8_noalloc: injected fault");
   if (!(D == 64 || D == 128)) return arg_error(std::string(fn) + ": D must be 64 or 128");
   if (B <= 0 || H <= 0 || N <= 0) return arg_error(std::string(fn) + ": empty shape");
-  if (!(block_rows == 64 || block_rows == 128))
-    return arg_error(std::string(fn) + ": block_rows must be 64 or 128");
+  // The size limit is checked before anything else touches the buffers.  The
+  // scratch holds the K token mean, needed when K is smoothed and quantised.
   const int G = B * H;
-  // The size limit is checked before anything else touches the buffers.
-  const size_t need = (flags & VCATTN_SMOOTH_K) ? vcattn::prepare_workspace_bytes(G, N, D) : 0;
+  const size_t need = ((flags & VCATTN_SMOOTH_K) && k8 != nullptr) ? vcattn::prepare_workspace_bytes(G, N, D) : 0;
   if (need > kScratchBytes)
     return arg_error(std::string(fn) + ": shape needs " + std::to_string(need) +
                      " bytes of scratch, above this entry point's fixed " + std::to_string(kScratchBytes) +
                      "-byte limit; use vcattn_prepare_fp8 with a workspace");
-  if (!(view_ok(q, dtype) && view_ok(k, dtype) && view_ok(v, dtype)))
-    return arg_error(std::string(fn) + ": q/k/v must be 16-byte aligned with 16-byte multiple strides");
-  if (!(perm == nullptr || perm_rows == 1 || perm_rows == G))
-    return arg_error(std::string(fn) + ": perm_rows must be 1 or G");
-  if (!(q8 && q_scale && k8 && k_scale && v_scale && mu && (v8 || v8t)))
-    return arg_error(std::string(fn) + ": null output");
-  if (!(aligned16(q8) && aligned16(k8) && (v8 == nullptr || aligned16(v8)) && (v8t == nullptr || aligned16(v8t))))
-    return arg_error(std::string(fn) + ": code buffers must be 16-byte aligned");
+  const int rc = vcattn::prepare_fp8_checks(fn, q, k, v, dtype, B, H, N, D, perm, perm_rows, block_rows, q8, q_scale,
+                                            k8, k_scale, v8, v_scale, mu, v8t, route);
+  if (rc != VCATTN_OK) return rc;
   const int n_pad = (N + block_rows - 1) / block_rows * block_rows;
-  if (route) {
-    if (!(route->q_block == 64 || route->q_block == 128) || n_pad % route->q_block != 0)
-      return arg_error(std::string(fn) + ": route q_block must be 64 or 128 and divide n_pad");
-  }
   void* scratch = nullptr;
   cudaError_t e = scratch_address(&scratch);
   if (e != cudaSuccess)

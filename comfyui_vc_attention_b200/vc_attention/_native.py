@@ -34,6 +34,7 @@ HADAMARD = 1
 SMOOTH_K = 2
 V_MMA_ORDER = 4
 EXPCAST = 1
+EXPCAST_EXACT = 2
 
 
 class NativeUnavailable(RuntimeError):

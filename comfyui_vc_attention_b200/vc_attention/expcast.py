@@ -8,7 +8,8 @@ without an exponential:
     code = clamp(round_even(8 * u + 56 + beta), 0, 120)
 
 ``expcast_codes(..., exact=True)`` evaluates the operation sequence above;
-``exact=False`` the single-FMA form the attention kernel uses.
+``exact=False`` runs the attention kernels' own device routine (one saturating
+FMA per code with the per-row constants folded, rounded by a magic add).
 """
 
 from __future__ import annotations

@@ -43,6 +43,9 @@ class TritonConfig:
     block_n     KV tile == value block rows (64 or 128).
     num_warps / num_stages  accepted for interface parity, unused.
     pv_fp8      accepted; PV is always FP8 E4M3 here.
+    expcast_exact  (this build) with enable_expcast, the dense tcgen05 kernel
+                evaluates ExpCast in expcast.py's operation order instead of
+                the one-FMA form (slower; for parity runs).
     """
     block_m: int = 64
     block_n: int = 128
@@ -57,6 +60,7 @@ class TritonConfig:
     local_blocks: int = 1
     sink_blocks: int = 0
     group: int = 16
+    expcast_exact: bool = False
 
 
 class Prepared(NamedTuple):
@@ -296,6 +300,12 @@ def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     perm: (G, N) or (1, N) int32 V-Smooth permutation or None.
     Returns (B, H, N, D) in q.dtype.
     """
+    return _attention_into(q, k, v, perm, cfg, scale, None)
+
+
+def _attention_into(q, k, v, perm, cfg, scale, out):
+    """vc_attention_cuda writing into ``out`` ((B, H, N, D) view of q's dtype,
+    d contiguous), or into a new buffer when ``out`` is None."""
     cfg = cfg or TritonConfig()
     _check_qkv(q, k, v)
     b, h, n, d = q.shape
@@ -312,7 +322,10 @@ def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     p = prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
                 tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=use_tc, want_v_t=not use_tc,
                 local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks, qk_fp4=fp4, fp8_qk=not fp4)
-    out = _out_view(q, q.dtype)
+    if out is None:
+        out = _out_view(q, q.dtype)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.stride(-1) != 1:
+        raise ValueError("out must be a (B, H, N, D) view of q's dtype with d contiguous")
     return attention_prepared(p, n, out, scale, cfg)
 
 
@@ -327,6 +340,8 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
     lib = N.lib()
     b, h, n_pad, d = (p.q if p.q is not None else p.v).shape
     flags = N.EXPCAST if cfg.enable_expcast else 0
+    if cfg.enable_expcast and cfg.expcast_exact:
+        flags |= N.EXPCAST_EXACT
     odt = _dtype_code(out)
     st = _stream(out)
     if cfg.qk_fp4 and not cfg.sparse:
@@ -493,8 +508,7 @@ def vc_attention_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                 s_comp.wait_event(out_done[slot])    # chunk i-2's result copied out
             qd, kd, vd = (t[:u].unsqueeze(0) for t in slab_in[slot])
             pl = None if perm is None else (perm if perm.shape[0] == 1 else perm[lo:hi])
-            res = vc_attention_cuda(qd, kd, vd, pl, cfg, scale)
-            slab_out[slot][:u].copy_(res.reshape(u, n, d))
+            _attention_into(qd, kd, vd, pl, cfg, scale, slab_out[slot][:u].unsqueeze(0))
             comp_done[slot].record(s_comp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(comp_done[slot])

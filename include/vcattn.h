@@ -5,9 +5,11 @@
  * Every entry point takes plain device pointers, sizes and a cudaStream_t
  * passed as void*, enqueues its kernels on that stream and returns a status
  * code (0 = VCATTN_OK).  Nothing here aborts, traps or synchronises the device
- * unless the entry point says so.  Device buffers are borrowed; the library
- * allocates nothing: scratch memory is a caller-provided workspace whose size
- * the matching *_workspace_bytes() function reports.
+ * unless the entry point says so.  Device buffers are borrowed and no entry
+ * point allocates device memory.  Scratch memory is a caller-provided
+ * workspace whose size the matching *_workspace_bytes() function reports,
+ * except for vcattn_prepare_fp8_noalloc, whose scratch is a fixed 16 MiB
+ * array held inside the library on every GPU that loads it.
  *
  * The reference (bingling360/comfyui_vc_attention) is Python + Triton, so its
  * "FFI" for this path is the Python call boundary; each function below names
@@ -63,6 +65,10 @@ extern "C" {
 
 /* ---- attention flags (TritonConfig, triton_attn.py:93-129) ------------- */
 #define VCATTN_EXPCAST 1        /* write P bytes with ExpCast (expcast.py:52-70) */
+/* With VCATTN_EXPCAST: evaluate ExpCast in the reference's operation order
+ * (expcast.py:67-69) on s = (S * (qs * ks)) * sm_scale instead of the one-FMA
+ * form.  Slower; for parity runs.  vcattn_attn_fp8 only. */
+#define VCATTN_EXPCAST_EXACT 2
 
 /* A strided (B, H, N, D) view: element (b,h,n,d) sits at
  * data + b*sb + h*sh + n*sn + d (strides in elements, d contiguous).  This is
@@ -164,11 +170,16 @@ VCATTN_API int vcattn_prepare_nvfp4(const vcattn_bhnd* q, const vcattn_bhnd* k, 
  * its own pool and forbids plugins to allocate, or a plain FFI binding with no
  * device allocator.  Its scratch is a 16 MiB array inside the library, which
  * every GPU that loads the library holds until the process exits.  Shapes
- * whose scratch exceeds it (G * ceil(N/256) * D * 8 + G * D * 4 bytes when
- * VCATTN_SMOOTH_K is set) are rejected with VCATTN_ERR_ARG before any launch.
+ * whose scratch exceeds it (G * ceil(N/256) * D * 8 + G * D * 4 + G * 8 + 256
+ * bytes when VCATTN_SMOOTH_K is set and k8 is given) are rejected with VCATTN_ERR_ARG before any launch.
  * The first call on a device looks the array's address up (with that device
- * current) and should come before any stream capture.  All calls share the
- * array: calls that overlap on the GPU race and must be serialised. */
+ * current) and should come before any stream capture; the address is cached
+ * per device together with the id of its CUDA context, and looked up again
+ * once that context has changed (after a cudaDeviceReset()).  All calls share
+ * the array: calls that overlap on the GPU race and must be serialised.
+ * Argument checks, host fault injection and error codes are those of
+ * vcattn_prepare_fp8 (Q or K codes may be left out in pairs); shapes that
+ * need no K mean (no VCATTN_SMOOTH_K, or k8 NULL) use no scratch at all. */
 VCATTN_API int vcattn_prepare_fp8_noalloc(const vcattn_bhnd* q, const vcattn_bhnd* k, const vcattn_bhnd* v,
                                           int dtype, int B, int H, int N, int D,
                                           const int32_t* perm, int perm_rows, int block_rows, int flags,
@@ -268,8 +279,9 @@ VCATTN_API int vcattn_attn_fp8_sparse_tc(const uint8_t* q8, const float* q_scale
 /* ---- element codecs, exposed for bit-exact tests ------------------------
  * vcattn_e4m3_encode: quant.py:56-84.  vcattn_fp4_encode: quant.py:144-161
  * (one code per byte).  vcattn_expcast_codes: expcast.py:52-70 on a (rows,
- * cols) score tile and its (rows,) running maxima; mode 0 is the kernel's
- * one-FMA form, mode 1 the reference's operation sequence. */
+ * cols) score tile and its (rows,) running maxima; mode 0 runs the attention
+ * kernels' own one-FMA device routine (same folding of the per-row constants,
+ * unit score scale), mode 1 the reference's operation sequence. */
 VCATTN_API int vcattn_e4m3_encode(const float* x, int64_t n, uint8_t* out, void* stream);
 VCATTN_API int vcattn_fp4_encode(const float* x, int64_t n, uint8_t* out, void* stream);
 VCATTN_API int vcattn_expcast_codes(const float* s, const float* m, int rows, int cols, double beta,

@@ -2,7 +2,7 @@
 
 Run once, where the reference package is importable (read-only source tree):
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py [--reference PATH] [--only base,sparse,nvfp4]
 
 It imports bingling360/comfyui_vc_attention (``vc_attention``), runs the
 reference's own functions on seeded inputs from ``oracle/inputs.py`` and writes
@@ -30,7 +30,10 @@ from oracle.inputs import digest, make_qkv  # noqa: E402
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("VC_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", default="",
+                    help="comma-separated fixture groups to (re)write: base, sparse, nvfp4 (default all)")
     args = ap.parse_args()
+    only = set(filter(None, args.only.split(",")))
     sys.path.insert(0, args.reference)
     import torch
     from vc_attention import quant as Q
@@ -42,6 +45,13 @@ def main() -> int:
     from vc_attention.kernels.triton_attn import _prepare_fast, prepare
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+
+    if not only or "sparse" in only:
+        make_sparse(args.reference)
+    if not only or "nvfp4" in only:
+        make_nvfp4()
+    if only and "base" not in only:
+        return _report()
 
     # ---------------- codecs, fwht, linspace ----------------
     g = torch.Generator().manual_seed(0)
@@ -149,11 +159,171 @@ def main() -> int:
         inputs_digest=np.array(digest(q4, k4, v4)), perm=perm4.numpy(),
         k_mean=pf.k_mean.numpy(), v_mean=pf.v_mean.numpy(), thresh=pf.thresh.numpy())
 
+    return _report()
+
+
+def _report() -> int:
     print("golden vectors written to", HERE)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f"  {f}: {os.path.getsize(os.path.join(HERE, f)) / 1024:.0f} KiB")
     return 0
+
+
+def _psnr(out, ref) -> float:
+    """PSNR of the reference's benchmark (tests/bench_attention.py:55-57)."""
+    import torch
+    mse = ((out.float() - ref.float()) ** 2).mean()
+    return float(10 * torch.log10(ref.float().pow(2).max() / mse.clamp(min=1e-30)))
+
+
+def _kernel_route(q8, qs, k_mean, thresh, n, block_rows, q_block, scale, local=1, sink=0):
+    """The routing decision of the reference's sparse kernel
+    (kernels/triton_attn.py:449-459), evaluated with the kernel's operand
+    precisions: proxy = dot(bf16(q8), bf16(k_mean)) * (qs * sm_scale) per query
+    row, its mean over the q_block rows against the block's threshold, plus the
+    local window and the sink blocks.
+    q8 (G, NP, D) float8_e4m3fn; qs (G, NP); k_mean (G, NB, D); thresh (G, NQB).
+    -> (keep bool (G, NQB, NB), score (G, NQB, NB) fp32)."""
+    import torch
+    g, n_pad, d = q8.shape
+    nb = n_pad // block_rows
+    nqb = n_pad // q_block
+    qb = q8.to(torch.bfloat16).float()
+    kc = k_mean.to(torch.bfloat16).float()
+    proxy = torch.bmm(qb, kc.transpose(1, 2)) * (qs.float() * scale).unsqueeze(-1)   # (G, NP, NB)
+    score = proxy.reshape(g, nqb, q_block, nb).sum(dim=2) / q_block
+    qi = torch.arange(nqb)[:, None]
+    kj = torch.arange(nb)[None, :]
+    qb_kv = (qi * q_block) // block_rows
+    keep = (score > thresh.reshape(g, nqb, 1)) | ((qb_kv - kj).abs() <= local)[None] | (kj < sink)[None]
+    return keep, score
+
+
+def _load_simulate(reference: str):
+    """``simulate`` (and its helper ``dq_fp8``) of the reference's
+    tests/_probe35_phase3.py, lifted out with ``ast`` so that the probe's own
+    imports (ComfyUI, comfy_kitchen, a GPU) are never executed."""
+    import ast
+
+    import torch
+    from vc_attention import quant as Q
+    from vc_attention.kernels import triton_attn as T
+
+    path = os.path.join(reference, "tests", "_probe35_phase3.py")
+    tree = ast.parse(open(path).read(), filename=path)
+    keep = [node for node in tree.body
+            if isinstance(node, ast.FunctionDef) and node.name in ("simulate", "dq_fp8")]
+    keep += [node for node in tree.body if isinstance(node, ast.Assign)
+             and any(isinstance(t, ast.Tuple) and any(getattr(e, "id", "") == "BN" for e in t.elts)
+                     for t in node.targets)]
+    mod = ast.Module(body=keep, type_ignores=[])
+    ns = {"torch": torch, "Q": Q, "T": T}
+    exec(compile(mod, path, "exec"), ns)
+    assert ns["BN"] == 128 and ns["QB"] == 64
+    return ns["simulate"]
+
+
+def make_sparse(reference: str) -> None:
+    """sparse_ref.npz: the reference's own routing decisions and its own
+    sparse-attention simulation on configs[2]-style inputs (spatial grid,
+    V-Smooth k-means perm with block_rows 128, q_block 64, tau 1.3).
+
+    Per case c:
+      c_perm                 reference build_permutation (iters=3) perm
+      c_keep_prep / _score_prep / _thresh_prep
+          the kernel rule of triton_attn.py:449-459 applied to the portable
+          prepare()'s Q codes and scales (:504-579) and to routing statistics
+          computed by the formula of :716-735 from the same fp32 rotated Q/K
+      c_keep_fast / _score_fast / _thresh_fast
+          the same rule on _prepare_fast's outputs (:640-754: bf16 Hadamard,
+          bf16 divide), i.e. the routing the reference's GPU path takes
+      c_sim_out (fp16), c_sim_keep, c_sim_psnr
+          simulate() of tests/_probe35_phase3.py:45-114 (the reference's ground
+          truth for its sparse kernel) and its PSNR against fp32 SDPA
+      c_dense_psnr           vc_attention_reference (fp8, ExpCast off) PSNR
+    """
+    import torch
+    from vc_attention.grouping import GroupingConfig, build_permutation
+    from vc_attention.hadamard import fwht
+    from vc_attention.kernels.reference import RefConfig, vc_attention_reference
+    from vc_attention.kernels.triton_attn import _prepare_fast, prepare
+
+    simulate = _load_simulate(reference)
+    D, BR, QB, TAU = 128, 128, 64, 1.3
+    sc = D ** -0.5
+    cases = {"s2k": (2, 2048, (8, 16, 16), 5, True), "s4k": (4, 4096, (16, 16, 16), 6, False)}
+    out = {}
+    for name, (H, n, grid, seed, with_sim) in cases.items():
+        q, k, v = make_qkv(1, H, n, D, seed=seed, spatial=grid)
+        qt, kt, vt = (torch.from_numpy(a).to(torch.bfloat16) for a in (q, k, v))
+        G = H
+        perm = build_permutation(vt.reshape(G, n, D), GroupingConfig(block_rows=BR, iters=3)).perm
+        # portable prepare + the routing formula on its fp32 rotated tensors
+        prep = prepare(qt, kt, vt, perm, block_rows=BR)
+        qf = qt.reshape(G, n, D).float()
+        kf = kt.reshape(G, n, D).float().gather(1, perm.to(torch.int64).unsqueeze(-1).expand(G, n, D))
+        q_t, k_t = fwht(qf), fwht(kf)
+        k_t = k_t - k_t.mean(dim=1, keepdim=True)
+        nb, nqb = n // BR, n // QB
+        k_mean = k_t.reshape(G, nb, BR, D).mean(dim=2)
+        q_cent = q_t.reshape(G, nqb, QB, D).mean(dim=2)
+        proxy = torch.matmul(q_cent, k_mean.transpose(-1, -2)) * sc
+        thr = (proxy.mean(dim=-1, keepdim=True)
+               + TAU * proxy.std(dim=-1, keepdim=True, unbiased=False)).reshape(G, nqb)
+        keep_p, score_p = _kernel_route(prep.q.reshape(G, n, D), prep.q_scale.reshape(G, n), k_mean, thr,
+                                        n, BR, QB, sc)
+        # the GPU path of the reference: _prepare_fast
+        pf = _prepare_fast(qt, kt, vt, perm, block_rows=BR, hadamard=True, smooth_k=True, sparse=True,
+                           tau=TAU, q_block=QB, scale=sc)
+        keep_f, score_f = _kernel_route(pf.q.reshape(G, n, D), pf.q_scale.reshape(G, n),
+                                        pf.k_mean.reshape(G, nb, D), pf.thresh.reshape(G, nqb), n, BR, QB, sc)
+        out.update({f"{name}_digest": np.array(digest(q, k, v)), f"{name}_perm": perm.numpy(),
+                    f"{name}_keep_prep": keep_p.numpy(), f"{name}_score_prep": score_p.numpy(),
+                    f"{name}_thresh_prep": thr.numpy(),
+                    f"{name}_keep_fast": keep_f.numpy(), f"{name}_score_fast": score_f.numpy(),
+                    f"{name}_thresh_fast": pf.thresh.reshape(G, nqb).numpy()})
+        agree = float((keep_p == keep_f).float().mean())
+        print(f"  {name}: keep(prep) {float(keep_p.float().mean()):.4f}  keep(fast) "
+              f"{float(keep_f.float().mean()):.4f}  agreement {agree:.4f}")
+        if with_sim:
+            sim, ratio = simulate(qt.float(), kt.float(), vt.float(), perm, TAU, sc)
+            sd = torch.nn.functional.scaled_dot_product_attention(qt.float(), kt.float(), vt.float())
+            dense = vc_attention_reference(qt.float(), kt.float(), vt.float(),
+                                           RefConfig(backend="fp8", block_rows=BR, block_m=QB,
+                                                     enable_vsmooth=True), perm=perm)
+            out.update({f"{name}_sim_out": sim.numpy().astype(np.float16),
+                        f"{name}_sim_keep": np.float32(ratio),
+                        f"{name}_sim_psnr": np.float32(_psnr(sim, sd)),
+                        f"{name}_dense_psnr": np.float32(_psnr(dense, sd))})
+            print(f"  {name}: simulate keep {ratio:.4f}  PSNR sim {_psnr(sim, sd):.2f} dB  "
+                  f"dense {_psnr(dense, sd):.2f} dB")
+    np.savez_compressed(os.path.join(HERE, "sparse_ref.npz"), **out)
+
+
+def make_nvfp4() -> None:
+    """nvfp4_ref.npz: the reference's own nvfp4 backend
+    (kernels/reference.py:112-116, 135-152: Q/K, V and P quantised to NVFP4
+    with per-16-token microscales) and its fp8 backend on the same seeded
+    configs[3]-distributed inputs, with their PSNRs against fp32 SDPA."""
+    import torch
+    from vc_attention.grouping import GroupingConfig, build_permutation
+    from vc_attention.kernels.reference import RefConfig, vc_attention_reference
+
+    H, n, D, BR = 2, 2048, 128, 128
+    q, k, v = make_qkv(1, H, n, D, seed=8)
+    qt, kt, vt = (torch.from_numpy(a).to(torch.bfloat16) for a in (q, k, v))
+    perm = build_permutation(vt.reshape(H, n, D), GroupingConfig(block_rows=BR, iters=3)).perm
+    sd = torch.nn.functional.scaled_dot_product_attention(qt.float(), kt.float(), vt.float())
+    res = {"digest": np.array(digest(q, k, v)), "perm": perm.numpy()}
+    for backend in ("nvfp4", "fp8"):
+        o = vc_attention_reference(qt.float(), kt.float(), vt.float(),
+                                   RefConfig(backend=backend, block_rows=BR, block_m=64, enable_vsmooth=True),
+                                   perm=perm)
+        res[f"{backend}_out"] = o.numpy().astype(np.float16)
+        res[f"{backend}_psnr"] = np.float32(_psnr(o, sd))
+        print(f"  reference backend {backend}: PSNR {_psnr(o, sd):.2f} dB")
+    np.savez_compressed(os.path.join(HERE, "nvfp4_ref.npz"), **res)
 
 
 if __name__ == "__main__":

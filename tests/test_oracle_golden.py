@@ -223,3 +223,76 @@ def test_attention_codes_nvfp4_close_to_float64():
     assert O.rel_l2(out, sd) < 0.1
     assert O.rel_l2(out, fp8) < 0.1
     assert O.psnr(out, sd) > 20.0
+
+
+# ---------------------------------------------------------------------------
+# Routing mask and sparse output against the reference's own code
+# (tests/golden/sparse_ref.npz, written by make_golden.py --only sparse)
+# ---------------------------------------------------------------------------
+SPARSE_CASES = {"s2k": (2, 2048, (8, 16, 16), 5), "s4k": (4, 4096, (16, 16, 16), 6)}
+# A routing decision may differ from the reference's only at a tie: the
+# reference sums the per-row proxies and the statistics in fp32 (torch's
+# order), the oracle rounds each sum once.  Measured: the scores agree to
+# 3.4e-5 and the thresholds to 2.4e-7 (max |score| 2.6).  Against _prepare_fast
+# (bf16 Hadamard and divide) they agree to 6.1e-3 and 3.1e-3.
+TIE_PREP = 2e-4       # |score - thresh| of a disagreement, portable-prepare routing
+TIE_FAST = 2e-2       # the same against the bf16 fast-prepare routing
+
+
+@pytest.fixture(scope="module")
+def sparse_ref():
+    return _load("sparse_ref.npz")
+
+
+def sparse_case(g, name):
+    h, n, grid, seed = SPARSE_CASES[name]
+    q, k, v = make_qkv(1, h, n, 128, seed=seed, spatial=grid)
+    assert digest(q, k, v) == str(g[f"{name}_digest"]), "regenerated inputs differ from the fixture's"
+    return q.reshape(h, n, 128), k.reshape(h, n, 128), v.reshape(h, n, 128)
+
+
+def mask_agreement(keep, g, name, tag, tie):
+    """Fraction of routing decisions equal to the reference's; every
+    disagreement must sit within ``tie`` of the reference's threshold."""
+    kr = g[f"{name}_keep_{tag}"].astype(bool)
+    sr = g[f"{name}_score_{tag}"]
+    tr = g[f"{name}_thresh_{tag}"]
+    keep = np.asarray(keep, bool).reshape(kr.shape)
+    dis = np.argwhere(keep != kr)
+    margins = [float(sr[a, i, j] - tr[a, i]) for a, i, j in dis]
+    assert all(abs(m) <= tie for m in margins), f"{name}/{tag}: non-tie disagreements {margins}"
+    return float((keep == kr).mean()), margins
+
+
+@pytest.mark.parametrize("name", list(SPARSE_CASES))
+def test_route_mask_matches_reference_routing(sparse_ref, name):
+    """The oracle's mask (the GPU's, bit for bit) against the reference's
+    routing rule (triton_attn.py:449-459) run by the reference's own torch code
+    on the portable prepare's codes, and on _prepare_fast's."""
+    q, k, v = sparse_case(sparse_ref, name)
+    n = q.shape[1]
+    prep = O.prepare(q, k, v, sparse_ref[f"{name}_perm"], block_rows=128)
+    st = O.route_stats(prep, 128, 64, 1.3, 128 ** -0.5)
+    keep, _ = O.route_mask(prep, st, n, 128, 64, 128 ** -0.5)
+    agree, _ = mask_agreement(keep, sparse_ref, name, "prep", TIE_PREP)
+    assert agree >= 0.999
+    agree_f, _ = mask_agreement(keep, sparse_ref, name, "fast", TIE_FAST)
+    assert agree_f >= 0.999
+    assert 0.05 < keep.mean() < 0.6     # routing is non-trivial on these inputs
+
+
+def test_sparse_oracle_matches_reference_simulation(sparse_ref):
+    """The oracle's sparse-kernel arithmetic against simulate() of the
+    reference's tests/_probe35_phase3.py:45-114 (its ground truth for the
+    fused sparse kernel): rel-L2 within the probe's own 5e-2 gate, and PSNR
+    against fp32 SDPA within 0.3 dB of the simulation's."""
+    q, k, v = sparse_case(sparse_ref, "s2k")
+    n = q.shape[1]
+    prep = O.prepare(q, k, v, sparse_ref["s2k_perm"], block_rows=128)
+    st = O.route_stats(prep, 128, 64, 1.3, 128 ** -0.5)
+    keep, _ = O.route_mask(prep, st, n, 128, 64, 128 ** -0.5)
+    out = O.attention_sparse_codes(prep, st, keep, n, 128, 64, 128 ** -0.5)
+    sim = sparse_ref["s2k_sim_out"].astype(np.float32).reshape(out.shape)
+    assert O.rel_l2(out, sim) <= 5e-2
+    sd = O.sdpa_f32(q, k, v)
+    assert abs(O.psnr(out, sd) - float(sparse_ref["s2k_sim_psnr"])) <= 0.3

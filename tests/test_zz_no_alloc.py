@@ -96,11 +96,30 @@ def test_noalloc_prepare_refuses_shapes_beyond_its_scratch(native):
     lib = native.lib()
     # 512 heads x 65536 tokens needs 512 * 256 * 128 * 8 bytes of partial sums,
     # far above 16 MiB: refused on the host, before pointers are even looked at.
+    # The code and scale pointers are stand-ins that are never dereferenced.
     dummy = native.BHND(None, 0, 0, 0)
+    fake = ctypes.c_void_p(4096)
     rc = lib.vcattn_prepare_fp8_noalloc(ctypes.byref(dummy), ctypes.byref(dummy), ctypes.byref(dummy),
                                         native.DTYPE_BF16, 1, 512, 65536, 128, None, 0, 128,
-                                        native.HADAMARD | native.SMOOTH_K, None, None, None, None,
-                                        None, None, None, None, None, None)
+                                        native.HADAMARD | native.SMOOTH_K, fake, fake, fake, fake,
+                                        fake, fake, fake, None, None, None)
     assert rc == native.ERR_ARG
     msg = lib.vcattn_last_error().decode()
     assert "limit" in msg and "vcattn_prepare_fp8" in msg
+
+
+def test_noalloc_prepare_honours_host_fault_injection(native):
+    """The router's fallback test hook reaches this entry point too: while the
+    fault is set it returns the injected-fault status and launches nothing."""
+    lib = native.lib()
+    dummy = native.BHND(None, 0, 0, 0)
+    lib.vcattn_inject_fault(b"vcattn_prepare_fp8_noalloc")
+    try:
+        rc = lib.vcattn_prepare_fp8_noalloc(ctypes.byref(dummy), ctypes.byref(dummy), ctypes.byref(dummy),
+                                            native.DTYPE_BF16, 1, 1, 128, 128, None, 0, 128,
+                                            native.HADAMARD | native.SMOOTH_K, None, None, None, None,
+                                            None, None, None, None, None, None)
+    finally:
+        lib.vcattn_inject_fault(None)
+    assert rc == native.ERR_INJECTED
+    assert "injected" in lib.vcattn_last_error().decode()
