@@ -14,9 +14,12 @@ its k-means time is reported separately as ``kmeans_ms``).
 ``value`` = effective TFLOPS over all ranks, 4*B*H*N^2*D per call / time, with
 inputs resident in HBM; ``e2e`` = the same through the public entry point with
 pinned-host inputs copied in and the output copied back inside the timed
-region.  Multi-GPU runs (torchrun, one rank per GPU) give every rank its own
-independent (batch, head) units of the same size: weak scaling, no collective
-in the data path; the time is the max over ranks.
+region.  Multi-GPU runs (torchrun, one rank per GPU) split the same job's
+(batch, head) units over the ranks (strong scaling: the total work is the
+N=1 workload's) and NCCL all-gathers assemble the full output on every rank,
+in rounds that overlap the remaining compute; the time is the max over
+ranks.  ``--replicas`` instead gives every rank its own full-size copy of
+the workload (weak scaling, no collective).
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle
 restatement of vc_attention_reference, oracle/) on the host cores on a
@@ -263,10 +266,21 @@ def run_reference_arm(args, w, rank):
 
 # ----------------------------------------------------------------- main ----
 
+def _default_chunk(w, world):
+    """Units per rank per round of the chunked all-gather layout."""
+    G = w["B"] * w["H"]
+    if w.get("sharded"):
+        return -(-G // (4 * world))                  # configs[4]: four rounds per rank
+    return max(1, -(-G // (8 * world)))              # about eight rounds per rank
+
+
 def run_sharded(args, w, rank, world, local) -> int:
-    """the job's (batch, head) units split over the ranks (strong
-    scaling), each rank running prepare + attention on its units and one NCCL
-    all-gather assembling the full bf16 output on every rank."""
+    """The job's (batch, head) units split over the ranks (strong scaling:
+    the total work is the single-GPU workload's), each rank running prepare +
+    attention on its units and NCCL all-gathers assembling the full bf16
+    output on every rank.  The units are dealt in rounds; each round's
+    all-gather overlaps the next round's compute.  configs[4] always runs
+    here; the other workloads run here when N > 1."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -274,24 +288,31 @@ def run_sharded(args, w, rank, world, local) -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     from comfyui_vc_attention_b200.vc_attention import _native as N
     from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
-    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import TritonConfig
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_status,
+                                                                          vc_attention_cuda, vc_attention_host)
     from comfyui_vc_attention_b200.vc_attention.sharded import rank_units, vc_attention_sharded
     N.lib()
     q, k, v = make_inputs_gpu(w, 1234, dev)          # the same inputs on every rank
     B, H, NT, D = q.shape
     G = B * H
-    # four rounds of units per rank: each round's all-gather overlaps the next
-    # round's prepare + attention
-    chunk = -(-G // (4 * world)) if world > 1 else None
+    chunk = (args.chunk or _default_chunk(w, world)) if world > 1 else None
     mine = rank_units(G, world, rank, chunk)
+    n_mine = sum(hi - lo for lo, hi in mine)
     perm = torch.zeros((G, NT), dtype=torch.int32, device=dev)
     gcfg = GroupingConfig(block_rows=w["block_rows"], iters=3, max_clusters=w["k"])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
     for lo, hi in mine:
         perm[lo:hi] = build_permutation(v.view(G, NT, D)[lo:hi], gcfg).perm
-    cfg = TritonConfig(block_n=w["block_rows"], enable_expcast=w["expcast"])
+    e1.record()
+    torch.cuda.synchronize()
+    kmeans_ms = e0.elapsed_time(e1)
+    cfg = TritonConfig(block_n=w["block_rows"], enable_expcast=w["expcast"], sparse=w["sparse"],
+                       tau=w.get("tau", 1.3), qk_fp4=w.get("qk_fp4", False))
     scale = D ** -0.5
 
     def step():
@@ -314,62 +335,100 @@ def run_sharded(args, w, rank, world, local) -> int:
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps
+    # the same units without the all-gathers: the compute share of a step
+    t2, t3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t2.record()
+    for _ in range(args.steps):
+        vc_attention_sharded(q, k, v, perm, cfg, scale, gather=False, chunk=chunk)
+    t3.record()
+    torch.cuda.synchronize()
+    ms_compute = t2.elapsed_time(t3) / args.steps
     if world > 1:
-        t = torch.tensor([ms], device=dev)
+        t = torch.tensor([ms, ms_compute], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, ms_compute = (float(x) for x in t.tolist())
     fl = flops_per_call(w)
     value = fl / (ms / 1e3) / 1e12
-    # e2e: this rank's unit slabs from pinned host memory, the gathered
-    # output back to the host
-    g_h = [[t.reshape(G, NT, D)[lo:hi].cpu().pin_memory() for lo, hi in mine] for t in (q, k, v)]
-    o_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    n_mine = sum(hi - lo for lo, hi in mine)
+
+    # ---- the sharded output equals single-GPU calls (not timed) ----------
+    # Heads are independent and every kernel is deterministic, so a sampled
+    # unit recomputed alone on this GPU (its permutation rebuilt here) must
+    # equal the gathered output bit for bit.
+    check_units = sorted({0, G // 2 + 1, G - 1})
+    mismatches = 0
+    for u in check_units:
+        pu = build_permutation(v.view(G, NT, D)[u:u + 1], gcfg).perm
+        ou = vc_attention_cuda(q.view(G, NT, D)[u:u + 1].unsqueeze(0), k.view(G, NT, D)[u:u + 1].unsqueeze(0),
+                               v.view(G, NT, D)[u:u + 1].unsqueeze(0), pu, cfg, scale)
+        if not torch.equal(ou.reshape(NT, D), out.reshape(G, NT, D)[u]):
+            mismatches += 1
+    torch.cuda.synchronize()
+    status = attention_status()
+
+    # ---- e2e: each rank streams its own units from pinned host memory
+    # through the public host entry point and writes their output rows back
+    # to the host (no device all-gather: the host receives every unit once)
+    q_h = [q.view(G, NT, D)[lo:hi].unsqueeze(0).cpu().pin_memory() for lo, hi in mine]
+    k_h = [k.view(G, NT, D)[lo:hi].unsqueeze(0).cpu().pin_memory() for lo, hi in mine]
+    v_h = [v.view(G, NT, D)[lo:hi].unsqueeze(0).cpu().pin_memory() for lo, hi in mine]
+    o_h = [torch.empty_like(t).pin_memory() for t in q_h]
+    p_d = [perm[lo:hi] for lo, hi in mine]
 
     def e2e_step():
-        for srcs, dst in zip(g_h, (q, k, v)):
-            for src, (lo, hi) in zip(srcs, mine):
-                dst.reshape(G, NT, D)[lo:hi].copy_(src, non_blocking=True)
-        o = step()
-        o_h.copy_(o, non_blocking=True)
+        for qq, kk, vv, oo, pp in zip(q_h, k_h, v_h, o_h, p_d):
+            vc_attention_host(qq, kk, vv, pp, cfg, scale, out=oo)
 
     e2e_step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = 3
     a.record()
-    for _ in range(2):
+    for _ in range(e2e_steps):
         e2e_step()
     b_.record()
     torch.cuda.synchronize()
-    e2e_ms = a.elapsed_time(b_) / 2
+    e2e_ms = a.elapsed_time(b_) / e2e_steps
     if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
+        t = torch.tensor([e2e_ms, float(mismatches), float(status[0])], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        e2e_ms, mismatches, st_code = float(t[0]), int(t[1]), int(t[2])
+    else:
+        st_code = status[0]
+    psnr = None
+    if rank == 0 and not args.no_psnr and NT <= 16384:
+        psnr = psnr_vs_sdpa(out, q, k, v)
     peaks, peak_kind = measured_peaks()
     fp8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    rounds = len(mine)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp8-e4m3 (fp32 accumulate)",
-            "data": "synthetic (seeded configs[4] distributions, generated on device)",
+            "data": "synthetic (seeded configs distributions, generated on device)",
             "config": {"workload": w["desc"], "B": B, "H": H, "N": NT, "D": D, "block_rows": w["block_rows"],
+                       "kmeans_k": w["k"], "expcast": w["expcast"], "sparse": w["sparse"],
                        "units_per_rank": n_mine,
-                       "parallelism": f"(batch, head) units over {world} ranks, dealt in rounds of "
-                                      f"{chunk} per rank; each round's NCCL all-gather of the output "
-                                      f"overlaps the next round's compute",
+                       "parallelism": (f"(batch, head) units over {world} ranks (strong scaling), dealt in "
+                                       f"{rounds} rounds of {chunk} per rank; each round's NCCL all-gather of "
+                                       f"the bf16 output overlaps the next round's compute"
+                                       if world > 1 else "one GPU"),
                        "l2": "inputs larger than L2"},
+            "ms_compute": ms_compute, "ms_gather_exposed": max(0.0, ms - ms_compute), "kmeans_ms": kmeans_ms,
+            "psnr_db": psnr,
+            "sharded_equals_single_gpu": {"units_checked": check_units, "mismatches": mismatches,
+                                          "device_status": st_code},
             "roofline": {"bound": "tensor", "achieved": value / world, "peak": fp8_peak, "unit": "TFLOP/s",
                          "frac": value / world / fp8_peak, "traffic": None,
-                         "kernel": "whole step per GPU (prepare + attn_tc_kernel + all-gather)",
+                         "kernel": "whole step per GPU (prepare + attention + all-gather)",
                          "peak_note": f"dense FP8 = 2 x {peak_kind} bf16 burst"},
             "e2e": {"value": fl / (e2e_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_call": e2e_ms,
-                    "h2d_bytes_per_step": 3 * n_mine * NT * D * q.element_size(),
-                    "d2h_bytes_per_step": out.numel() * out.element_size()},
-            "gpu_launches": 8 * args.steps,
+                    "h2d_bytes_per_step": 3 * G * NT * D * q.element_size(),
+                    "d2h_bytes_per_step": G * NT * D * q.element_size(),
+                    "note": "all ranks together; each rank copies only its own units"},
+            "gpu_launches": (5 + 1) * rounds * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -388,6 +447,10 @@ def main() -> int:
     ap.add_argument("--workload", default="c1", choices=sorted(WORKLOADS))
     ap.add_argument("--cpu-rows", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chunk", type=int, default=0, help="units per rank per all-gather round (N > 1)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: independent full-size replicas per rank instead of the sharded split")
+    ap.add_argument("--no-psnr", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, PSNR or CPU baseline): the command profiled by ncu")
     args = ap.parse_args()
@@ -398,7 +461,7 @@ def main() -> int:
 
     if args.impl == "reference":
         return run_reference_arm(args, w, rank)
-    if w.get("sharded"):
+    if w.get("sharded") or (world > 1 and not args.replicas):
         return run_sharded(args, w, rank, world, local)
 
     import torch
@@ -569,7 +632,8 @@ def main() -> int:
         "data": "synthetic (seeded configs[1] distributions, generated on device)",
         "config": {"workload": w["desc"], "B": B, "H": H, "N": NT, "D": D, "block_rows": w["block_rows"],
                    "kmeans_k": res.k, "expcast": w["expcast"], "sparse": w["sparse"],
-                   "parallelism": f"(batch, head) units x{world} ranks, independent, no collective",
+                   "parallelism": (f"(batch, head) units x{world} ranks, independent replicas, no collective"
+                                   if world > 1 else "one GPU"),
                    "l2": "inputs larger than L2 (Q/K/V 235 MB each)",
                    "keep_fraction": keep_frac,
                    "block_skip_ratio": None if keep_frac is None else 1.0 - keep_frac,

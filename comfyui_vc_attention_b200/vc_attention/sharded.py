@@ -16,7 +16,10 @@ Two layouts:
   [i*P*c + r*c, i*P*c + (r+1)*c) of round i.  Round i's slabs then sit next to
   each other in the output, so its all-gather writes them in place, and it is
   issued asynchronously while round i+1 computes: the transfer overlaps the
-  remaining heads and only the last round's gather is exposed.
+  remaining heads and only the last round's gather is exposed.  Consecutive
+  rounds compute on two alternating streams, so the last wave of one round's
+  attention kernel (one CTA per SM, 128 query rows each) shares the GPU with
+  the first wave of the next instead of leaving SMs idle at every round's end.
 
 Padding units (past U) are never computed; their output rows are zeros in
 the padded buffer and are never returned.
@@ -61,8 +64,22 @@ def rank_units(units: int, world: int, rank: int, chunk: Optional[int] = None) -
     return out
 
 
-def _compute_units(q, k, v, perm, lo, hi, compute, dst):
-    """Run ``compute`` on units [lo, hi) and write them to ``dst`` (hi - lo, N, D)."""
+_ROUND_STREAMS = {}
+
+
+def _round_streams(dev: torch.device):
+    """Two compute streams per device for the rounds of the chunked layout
+    (kept for the process: the caching allocator keeps freed blocks per stream)."""
+    key = dev.index
+    if key not in _ROUND_STREAMS:
+        _ROUND_STREAMS[key] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _ROUND_STREAMS[key]
+
+
+def _compute_units(q, k, v, perm, lo, hi, compute, dst, cfg=None, scale=None):
+    """Attention of units [lo, hi), written to ``dst`` (hi - lo, N, D): by
+    ``compute`` when given (tests), else by the CUDA kernels straight into
+    ``dst``."""
     b, h, n, d = q.shape
     g = b * h
     ql = q.reshape(g, n, d)[lo:hi].unsqueeze(0)
@@ -71,7 +88,11 @@ def _compute_units(q, k, v, perm, lo, hi, compute, dst):
     pl = None
     if perm is not None:
         pl = perm if perm.shape[0] == 1 else perm[lo:hi]
-    dst.copy_(compute(ql, kl, vl, pl).reshape(hi - lo, n, d))
+    if compute is None:
+        from .kernels.cuda_attn import _attention_into
+        _attention_into(ql, kl, vl, pl, cfg, scale, dst.unsqueeze(0))
+    else:
+        dst.copy_(compute(ql, kl, vl, pl).reshape(hi - lo, n, d))
 
 
 def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
@@ -93,12 +114,6 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     """
     import torch.distributed as dist
 
-    if compute is None:
-        from .kernels.cuda_attn import vc_attention_cuda
-
-        def compute(ql, kl, vl, pl):
-            return vc_attention_cuda(ql, kl, vl, pl, cfg, scale)
-
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     b, h, n, d = q.shape
@@ -108,9 +123,10 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if chunk is None:
         lo, hi = shard_units(units, world, rank)
         per = -(-units // world)
-        local = torch.zeros((per, n, d), dtype=q.dtype, device=q.device)
+        local = torch.empty((per, n, d), dtype=q.dtype, device=q.device)
+        local[max(0, hi - lo):].zero_()
         if hi > lo:
-            _compute_units(q, k, v, perm, lo, hi, compute, local[: hi - lo])
+            _compute_units(q, k, v, perm, lo, hi, compute, local[: hi - lo], cfg, scale)
         if not gather:
             return local[: hi - lo]
         if world == 1:
@@ -123,20 +139,40 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     full = torch.empty((rounds * world * chunk, n, d), dtype=q.dtype, device=q.device) if gather else None
     mine = []
     works = []
+    cur = torch.cuda.current_stream(q.device) if q.is_cuda else None
+    streams = _round_streams(q.device) if q.is_cuda else None
+    if streams is not None:
+        for st in streams:
+            st.wait_stream(cur)
     for i in range(rounds):
         base = i * world * chunk
         lo = min(units, base + rank * chunk)
         hi = min(units, lo + chunk)
-        slab = torch.zeros((chunk, n, d), dtype=q.dtype, device=q.device)
-        if hi > lo:
-            _compute_units(q, k, v, perm, lo, hi, compute, slab[: hi - lo])
-            mine.append(slab[: hi - lo])
-        if gather:
-            # every rank issues every round, in the same order, with equal slabs
-            works.append((dist.all_gather_into_tensor(full[base: base + world * chunk], slab, group=group,
-                                                      async_op=True), slab))
+        ctx = torch.cuda.stream(streams[i % 2]) if streams is not None else _nullctx()
+        with ctx:
+            slab = torch.empty((chunk, n, d), dtype=q.dtype, device=q.device)
+            slab[max(0, hi - lo):].zero_()
+            if hi > lo:
+                _compute_units(q, k, v, perm, lo, hi, compute, slab[: hi - lo], cfg, scale)
+                mine.append(slab[: hi - lo])
+            if gather:
+                # every rank issues every round, in the same order, with equal
+                # slabs; NCCL orders the transfer after this round's compute
+                works.append((dist.all_gather_into_tensor(full[base: base + world * chunk], slab, group=group,
+                                                          async_op=True), slab))
     for w, _ in works:
         w.wait()
+    if streams is not None:
+        for st in streams:
+            cur.wait_stream(st)
     if not gather:
         return torch.cat(mine, 0) if mine else torch.zeros((0, n, d), dtype=q.dtype, device=q.device)
     return full[:units].reshape(b, h, n, d)
+
+
+class _nullctx:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
