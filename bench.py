@@ -267,11 +267,15 @@ def run_reference_arm(args, w, rank):
 # ----------------------------------------------------------------- main ----
 
 def _default_chunk(w, world):
-    """Units per rank per round of the chunked all-gather layout."""
+    """Units per rank per all-gather round: a divisor of the rank's unit count
+    (every round gives every rank the same work) leaving at least four
+    rounds, so that each gather hides under the next rounds' attention; with
+    the rounds on two alternating streams their grid tails overlap, so larger
+    rounds buy nothing beyond that."""
     G = w["B"] * w["H"]
-    if w.get("sharded"):
-        return -(-G // (4 * world))                  # configs[4]: four rounds per rank
-    return max(1, -(-G // (8 * world)))              # about eight rounds per rank
+    per_rank = -(-G // world)
+    cands = [c for c in range(1, per_rank + 1) if per_rank % c == 0 and per_rank // c >= 4]
+    return max(cands) if cands else 1
 
 
 def run_sharded(args, w, rank, world, local) -> int:
@@ -288,7 +292,11 @@ def run_sharded(args, w, rank, world, local) -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        # The gathers run on a high-priority NCCL stream: when an attention
+        # CTA retires, a waiting NCCL CTA gets the SM first.
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = not args.nccl_normal_priority
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev, pg_options=opts)
     from comfyui_vc_attention_b200.vc_attention import _native as N
     from comfyui_vc_attention_b200.vc_attention.grouping import GroupingConfig, build_permutation
     from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_status,
@@ -315,11 +323,35 @@ def run_sharded(args, w, rank, world, local) -> int:
                        tau=w.get("tau", 1.3), qk_fp4=w.get("qk_fp4", False))
     scale = D ** -0.5
 
-    def step():
-        return vc_attention_sharded(q, k, v, perm, cfg, scale, gather=True, chunk=chunk)
+    def step(gather=True):
+        return vc_attention_sharded(q, k, v, perm, cfg, scale, gather=gather, chunk=chunk,
+                                    overlap_rounds=not args.serial_rounds)
 
     for _ in range(max(3, args.warmup)):
         out = step()
+    torch.cuda.synchronize()
+
+    # One step per CUDA graph replay (all rounds, both compute streams and
+    # the NCCL all-gathers captured): a round's host work (argument checks,
+    # tensor-map encoding, allocator calls) is of the order of its GPU time
+    # once a rank holds only a few heads.
+    graphs = {}
+    if not args.eager:
+        for gather in (True, False):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                res_g = step(gather)
+            graphs[gather] = (gr, res_g)
+        torch.cuda.synchronize()
+
+    def run(gather=True):
+        if graphs:
+            graphs[gather][0].replay()
+            return graphs[gather][1]
+        return step(gather)
+
+    for _ in range(2):
+        out = run()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -328,10 +360,12 @@ def run_sharded(args, w, rank, world, local) -> int:
     time.sleep(0.3)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    h0 = time.perf_counter()
     t0.record()
     for _ in range(args.steps):
-        out = step()
+        out = run()
     t1.record()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps
@@ -339,7 +373,7 @@ def run_sharded(args, w, rank, world, local) -> int:
     t2, t3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t2.record()
     for _ in range(args.steps):
-        vc_attention_sharded(q, k, v, perm, cfg, scale, gather=False, chunk=chunk)
+        run(False)
     t3.record()
     torch.cuda.synchronize()
     ms_compute = t2.elapsed_time(t3) / args.steps
@@ -412,11 +446,14 @@ def run_sharded(args, w, rank, world, local) -> int:
                        "kmeans_k": w["k"], "expcast": w["expcast"], "sparse": w["sparse"],
                        "units_per_rank": n_mine,
                        "parallelism": (f"(batch, head) units over {world} ranks (strong scaling), dealt in "
-                                       f"{rounds} rounds of {chunk} per rank; each round's NCCL all-gather of "
-                                       f"the bf16 output overlaps the next round's compute"
+                                       f"{rounds} rounds of {chunk} per rank, prepared once per rank; each "
+                                       f"round's NCCL all-gather of the bf16 output (high-priority stream: "
+                                       f"{not args.nccl_normal_priority}) overlaps the next round's attention "
+                                       f"(rounds on two streams: {not args.serial_rounds})"
                                        if world > 1 else "one GPU"),
                        "l2": "inputs larger than L2"},
             "ms_compute": ms_compute, "ms_gather_exposed": max(0.0, ms - ms_compute), "kmeans_ms": kmeans_ms,
+            "host_enqueue_ms": host_ms, "cuda_graph": bool(graphs),
             "psnr_db": psnr,
             "sharded_equals_single_gpu": {"units_checked": check_units, "mismatches": mismatches,
                                           "device_status": st_code},
@@ -432,6 +469,8 @@ def run_sharded(args, w, rank, world, local) -> int:
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
+    graphs.clear()          # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -451,6 +490,10 @@ def main() -> int:
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent full-size replicas per rank instead of the sharded split")
     ap.add_argument("--no-psnr", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="N > 1: launch every round eagerly (no CUDA graph)")
+    ap.add_argument("--serial-rounds", action="store_true",
+                    help="N > 1: rounds in order on one stream (default: two alternating streams)")
+    ap.add_argument("--nccl-normal-priority", action="store_true", help="N > 1: NCCL on a normal-priority stream")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, PSNR or CPU baseline): the command profiled by ncu")
     args = ap.parse_args()

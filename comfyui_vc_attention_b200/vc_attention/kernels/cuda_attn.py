@@ -27,8 +27,8 @@ import torch
 from .. import _native as N
 from ..grouping import _dtype_code, as_bhnd
 
-__all__ = ["TritonConfig", "Prepared", "has_triton", "has_kernel", "prepare", "restore", "vc_attention_host",
-           "vc_attention_cuda", "vc_attention_triton", "route_mask"]
+__all__ = ["TritonConfig", "Prepared", "has_triton", "has_kernel", "prepare", "prepare_for", "slice_prepared",
+           "restore", "vc_attention_host", "vc_attention_cuda", "vc_attention_triton", "route_mask"]
 
 LOG2E = 1.4426950408889634
 P_SCALE = 448.0
@@ -303,25 +303,61 @@ def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return _attention_into(q, k, v, perm, cfg, scale, None)
 
 
-def _attention_into(q, k, v, perm, cfg, scale, out):
-    """vc_attention_cuda writing into ``out`` ((B, H, N, D) view of q's dtype,
-    d contiguous), or into a new buffer when ``out`` is None."""
+def _call_config(cfg, d):
     cfg = cfg or TritonConfig()
-    _check_qkv(q, k, v)
-    b, h, n, d = q.shape
-    if scale is None:
-        scale = d ** -0.5
     if cfg.qk_fp4 and cfg.sparse:
         cfg = TritonConfig(**{**cfg.__dict__, "qk_fp4": False})
+    if cfg.qk_fp4 and (d != 128 or cfg.block_n != 128):
+        raise ValueError("the NVFP4 QK kernel needs D = 128 and block_n = 128")
+    return cfg
+
+
+def prepare_for(q, k, v, perm, cfg: Optional[TritonConfig] = None, scale: Optional[float] = None) -> Prepared:
+    """The operands vc_attention_cuda prepares for ``cfg`` (the kernel family
+    that will read them decides the V layout)."""
+    _check_qkv(q, k, v)
+    b, h, n, d = q.shape
+    cfg = _call_config(cfg, d)
+    if scale is None:
+        scale = d ** -0.5
     br = cfg.block_n
     sparse = bool(cfg.sparse)
     fp4 = bool(cfg.qk_fp4)
-    if fp4 and (d != 128 or br != 128):
-        raise ValueError("the NVFP4 QK kernel needs D = 128 and block_n = 128")
     use_tc = d == 128 and (not sparse or sparse_tc_applies(d, br, cfg.block_m, cfg.group, n))
-    p = prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
-                tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=use_tc, want_v_t=not use_tc,
-                local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks, qk_fp4=fp4, fp8_qk=not fp4)
+    return prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
+                   tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=use_tc, want_v_t=not use_tc,
+                   local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks, qk_fp4=fp4, fp8_qk=not fp4)
+
+
+_BH_FIELDS = ("q", "q_scale", "k", "k_scale", "v", "v_scale", "mu", "q4", "q4_scale", "k4", "k4_scale",
+              "k_mean", "v_mean", "thresh")
+_G_FIELDS = ("v_t", "ap_tiles", "q_cent", "q_bar", "keep", "q4_g", "k4_g", "q4_sf_mma", "k4_sf_mma")
+
+
+def slice_prepared(p: Prepared, i: int) -> Prepared:
+    """Batch entry ``i`` of a Prepared as a Prepared of batch 1 (views, no copy)."""
+    b, h = (p.q if p.q is not None else p.v).shape[:2]
+    upd = {}
+    for name in _BH_FIELDS:
+        t = getattr(p, name)
+        if t is not None:
+            upd[name] = t[i:i + 1]
+    for name in _G_FIELDS:
+        t = getattr(p, name)
+        if t is not None:
+            upd[name] = t[i * h:(i + 1) * h]
+    return p._replace(**upd)
+
+
+def _attention_into(q, k, v, perm, cfg, scale, out):
+    """vc_attention_cuda writing into ``out`` ((B, H, N, D) view of q's dtype,
+    d contiguous), or into a new buffer when ``out`` is None."""
+    _check_qkv(q, k, v)
+    b, h, n, d = q.shape
+    cfg = _call_config(cfg, d)
+    if scale is None:
+        scale = d ** -0.5
+    p = prepare_for(q, k, v, perm, cfg, scale)
     if out is None:
         out = _out_view(q, q.dtype)
     elif out.shape != q.shape or out.dtype != q.dtype or out.stride(-1) != 1:

@@ -16,10 +16,12 @@ Two layouts:
   [i*P*c + r*c, i*P*c + (r+1)*c) of round i.  Round i's slabs then sit next to
   each other in the output, so its all-gather writes them in place, and it is
   issued asynchronously while round i+1 computes: the transfer overlaps the
-  remaining heads and only the last round's gather is exposed.  Consecutive
-  rounds compute on two alternating streams, so the last wave of one round's
-  attention kernel (one CTA per SM, 128 query rows each) shares the GPU with
-  the first wave of the next instead of leaving SMs idle at every round's end.
+  remaining heads and only the last round's gather is exposed.  The rank's
+  units of all rounds are prepared in one call up front (a strided view of
+  Q/K/V), so the rounds run only the attention kernel.  The attention CTA
+  holds a whole SM (its registers), so an NCCL kernel runs only on SMs the
+  attention leaves idle or as attention CTAs retire: a high-priority NCCL
+  stream makes the waiting NCCL CTAs take those SMs first.
 
 Padding units (past U) are never computed; their output rows are zeros in
 the padded buffer and are never returned.
@@ -98,7 +100,7 @@ def _compute_units(q, k, v, perm, lo, hi, compute, dst, cfg=None, scale=None):
 def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                          perm: Optional[torch.Tensor] = None, cfg=None, scale: Optional[float] = None,
                          group=None, gather: bool = True, chunk: Optional[int] = None,
-                         compute: Optional[Callable] = None) -> torch.Tensor:
+                         compute: Optional[Callable] = None, overlap_rounds: bool = True) -> torch.Tensor:
     """VC-Attention over this rank's (b, h) units, optionally all-gathered.
 
     q, k, v: (B, H, N, D), the same full tensors on every rank (views are
@@ -110,7 +112,14 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     this rank's units stacked in output order, (units, N, D), as listed by
     :func:`rank_units`.  ``compute`` (tests only) replaces the CUDA
     attention call; it receives (1, units, N, D) tensors and the matching
-    permutation rows.
+    permutation rows.  In the chunked layout the rank's units are prepared
+    once up front and each round runs the attention kernel into its slab;
+    ``overlap_rounds`` runs consecutive rounds on two streams, so one
+    round's last partial wave of attention CTAs shares the GPU with the next
+    round's first; the NCCL kernels then get SMs only as attention CTAs
+    retire, which is prompt when the process group's NCCL stream has high
+    priority (``ProcessGroupNCCL.Options.is_high_priority_stream``).  Without
+    it the rounds run in order on the caller's stream.
     """
     import torch.distributed as dist
 
@@ -140,10 +149,11 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     mine = []
     works = []
     cur = torch.cuda.current_stream(q.device) if q.is_cuda else None
-    streams = _round_streams(q.device) if q.is_cuda else None
+    streams = _round_streams(q.device) if (q.is_cuda and overlap_rounds) else None
     if streams is not None:
         for st in streams:
             st.wait_stream(cur)
+    preps = _prepare_rounds(q, k, v, perm, cfg, scale, world, rank, chunk) if compute is None else None
     for i in range(rounds):
         base = i * world * chunk
         lo = min(units, base + rank * chunk)
@@ -153,7 +163,12 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
             slab = torch.empty((chunk, n, d), dtype=q.dtype, device=q.device)
             slab[max(0, hi - lo):].zero_()
             if hi > lo:
-                _compute_units(q, k, v, perm, lo, hi, compute, slab[: hi - lo], cfg, scale)
+                if preps is None:
+                    _compute_units(q, k, v, perm, lo, hi, compute, slab[: hi - lo], cfg, scale)
+                else:
+                    from .kernels.cuda_attn import _call_config, attention_prepared
+                    attention_prepared(preps(i), n, slab[: hi - lo].unsqueeze(0), scale if scale else d ** -0.5,
+                                       _call_config(cfg, d))
                 mine.append(slab[: hi - lo])
             if gather:
                 # every rank issues every round, in the same order, with equal
@@ -168,6 +183,41 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if not gather:
         return torch.cat(mine, 0) if mine else torch.zeros((0, n, d), dtype=q.dtype, device=q.device)
     return full[:units].reshape(b, h, n, d)
+
+
+def _prepare_rounds(q, k, v, perm, cfg, scale, world, rank, chunk):
+    """Prepare this rank's units of every round up front, in one call for the
+    full rounds (a strided (rounds, chunk, N, D) view of Q/K/V, no copy) and
+    one for a partial last round: the prepare kernels then run on all of the
+    rank's heads at once instead of a few heads per round, and the rounds run
+    only the attention kernel.  Returns round index -> Prepared of that round."""
+    from .kernels.cuda_attn import prepare_for, slice_prepared
+    b, h, n, d = q.shape
+    units = b * h
+    span = world * chunk
+    r_full = units // span
+    out = {}
+    if r_full:
+        def rows(t):
+            return t.reshape(units, n, d)[: r_full * span].view(r_full, world, chunk, n, d)[:, rank]
+        pv = None
+        if perm is not None:
+            pv = (perm.expand(units, n) if perm.shape[0] == 1 else perm)[: r_full * span]
+            pv = pv.view(r_full, world, chunk, n)[:, rank].reshape(r_full * chunk, n)
+        p_all = prepare_for(rows(q), rows(k), rows(v), pv, cfg, scale)
+        for i in range(r_full):
+            out[i] = (p_all, i)
+    lo = min(units, r_full * span + rank * chunk)
+    hi = min(units, lo + chunk)
+    if hi > lo:
+        sl = [t.reshape(units, n, d)[lo:hi].unsqueeze(0) for t in (q, k, v)]
+        pl = None if perm is None else (perm if perm.shape[0] == 1 else perm[lo:hi])
+        out[r_full] = (prepare_for(*sl, pl, cfg, scale), 0)
+
+    def get(i):
+        p, j = out[i]
+        return slice_prepared(p, j)
+    return get
 
 
 class _nullctx:
