@@ -61,6 +61,9 @@ WORKLOADS = {
     "c1nv": dict(desc="NVFP4 QK^T + FP8 PV at the configs[1] shape: B1 H56 N16384 D128, ExpCast on, V-Smooth k=64",
                  B=1, H=56, N=16384, D=128, expcast=True, sparse=False, k=64, block_rows=128, spatial=None,
                  qk_fp4=True),
+    "c1nvh16": dict(desc="profiling slice of the NVFP4 QK^T path at the configs[1] shape: B1 H16 N16384 D128",
+                    B=1, H=16, N=16384, D=128, expcast=True, sparse=False, k=64, block_rows=128, spatial=None,
+                    qk_fp4=True),
     "c4": dict(desc="configs[4]: dense FP8 VC-Attention, B2 (CFG pair) H56 N65536 D128, (batch, head) units "
                     "sharded over the ranks, NCCL all-gather of the bf16 output, ExpCast on, V-Smooth k=512",
                B=2, H=56, N=65536, D=128, expcast=True, sparse=False, k=512, block_rows=128, spatial=None,
