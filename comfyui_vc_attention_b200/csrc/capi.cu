@@ -340,12 +340,9 @@ int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8, 
   p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
   p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
   p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
-  const bool two_tiles = attn_tc2_supported(p) && !(flags & VCATTN_ONE_QTILE);
-  const cudaError_t e = two_tiles ? launch_attn_tc2(p, static_cast<cudaStream_t>(stream))
-                                  : launch_attn_tc(p, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = launch_attn_tc(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess)
-    return fail(VCATTN_ERR_CUDA, std::string("vcattn_attn_fp8: ") + cudaGetErrorString(e) + " [" +
-                                     (two_tiles ? attn_tc2_diag() : attn_tc_diag()) + "]");
+    return fail(VCATTN_ERR_CUDA, std::string("vcattn_attn_fp8: ") + cudaGetErrorString(e) + " [" + attn_tc_diag() + "]");
   return VCATTN_OK;
 }
 
@@ -392,13 +389,6 @@ int vcattn_attn_status(int* code, int* where, int* block, int reset) {
     *code = c4;
     *where = 300 + w4;   // and those of the tensor-core k-means assignment as 300 + site
     *block = b4;
-  }
-  int c5 = 0, w5 = 0, b5 = 0;
-  if (e == cudaSuccess) e = attn_tc2_status(&c5, &w5, &b5, reset != 0);
-  if (e == cudaSuccess && *code == 0 && c5 != 0) {
-    *code = c5;
-    *where = 400 + w5;   // and those of the two-query-tile dense kernel as 400 + site
-    *block = b5;
   }
   return cuda_status(e, "vcattn_attn_status");
 }

@@ -94,11 +94,6 @@ cudaError_t attn_nvfp4_status(int* code, int* where, int* block, bool reset);
 const char* attn_nvfp4_diag();
 cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset);
 const char* attn_tc_diag();
-// Two query tiles per CTA, O accumulated in tensor memory (attn_tc2.cu).
-bool attn_tc2_supported(const AttnParams& p);
-cudaError_t launch_attn_tc2(const AttnParams& p, cudaStream_t st);
-cudaError_t attn_tc2_status(int* code, int* where, int* block, bool reset);
-const char* attn_tc2_diag();
 cudaError_t launch_attn_sparse_mma(const AttnParams& p, cudaStream_t st);
 bool attn_sparse_tc_supported(const AttnParams& p);
 cudaError_t launch_attn_sparse_tc(const AttnParams& p, cudaStream_t st);

@@ -35,7 +35,6 @@ SMOOTH_K = 2
 V_MMA_ORDER = 4
 EXPCAST = 1
 EXPCAST_EXACT = 2
-ONE_QTILE = 4
 
 
 class NativeUnavailable(RuntimeError):

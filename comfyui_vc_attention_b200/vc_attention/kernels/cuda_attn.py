@@ -369,10 +369,7 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
                        cfg: TritonConfig, kernel: str = "auto") -> torch.Tensor:
     """Run the attention kernel on prepared operands, writing into ``out``.
 
-    kernel: "tc" (tcgen05, D = 128, needs ``p.v``; dense with block_n = 128:
-    two query tiles per CTA, O accumulated in tensor memory), "tc1" (the
-    dense tcgen05 kernel with one query tile per CTA and O in registers, the
-    arithmetic order the sparse tcgen05 kernel shares), "mma" (register MMA,
+    kernel: "tc" (tcgen05, D = 128, needs ``p.v``), "mma" (register MMA,
     needs ``p.v_t``) or "auto" (tcgen05 whenever it applies), for the dense
     and the sparse path alike.
     """
@@ -422,9 +419,6 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
         return out
     if kernel == "auto":
         kernel = "tc" if (d == 128 and p.v is not None and not p.v_mma_order) else "mma"
-    if kernel == "tc1":
-        flags |= N.ONE_QTILE
-        kernel = "tc"
     if kernel == "tc":
         if p.v is None or p.v_mma_order:
             raise ValueError("the dense tcgen05 kernel reads V codes in token order (want_v=True, v_mma_order=False)")

@@ -69,11 +69,6 @@ extern "C" {
  * (expcast.py:67-69) on s = (S * (qs * ks)) * sm_scale instead of the one-FMA
  * form.  Slower; for parity runs.  vcattn_attn_fp8 only. */
 #define VCATTN_EXPCAST_EXACT 2
-/* vcattn_attn_fp8 with block_rows = 128 runs the kernel with two 128-row
- * query tiles per CTA and O accumulated in tensor memory; this flag selects
- * the kernel with one query tile per CTA and O in registers instead (the
- * only one for block_rows = 64).  No counterpart in the reference. */
-#define VCATTN_ONE_QTILE 4
 
 /* A strided (B, H, N, D) view: element (b,h,n,d) sits at
  * data + b*sb + h*sh + n*sn + d (strides in elements, d contiguous).  This is
@@ -215,8 +210,7 @@ VCATTN_API int vcattn_attn_nvfp4(const uint8_t* q4, const uint8_t* q4_sf_mma, co
                                  int64_t out_sh, int64_t out_sn, void* stream);
 
 /* ---- fused dense FP8 attention: triton_attn.py:203-322 (+ launch :831-844)
- * The tcgen05 kernels (D = 128, block_rows 64 or 128; with 128, two query
- * tiles per CTA and O in tensor memory unless VCATTN_ONE_QTILE).  Consumes the prepare
+ * The tcgen05 kernel (D = 128, block_rows 64 or 128).  Consumes the prepare
  * outputs in the Prepared layout (v8 row-major (G,NP,D) in token order, i.e.
  * prepared without VCATTN_V_MMA_ORDER); writes O (B,H,N,D)
  * through the out view (out_dtype one of the three dtypes; strides in
@@ -241,8 +235,7 @@ VCATTN_API int vcattn_attn_fp8_mma(const uint8_t* q8, const float* q_scale, cons
 /* Device status word of the tcgen05 kernels: code 0 = ok, 1 = a bounded wait
  * expired (the kernel gave up and returned); where = which wait (NVFP4
  * attention 100 + site, sparse attention 200 + site, the tensor-core k-means
- * assignment of vcattn_kmeans 300 + site, the two-query-tile dense kernel
- * 400 + site); block = the first failing CTA.
+ * assignment of vcattn_kmeans 300 + site); block = the first failing CTA.
  * Synchronises the current device.  reset != 0 clears it. */
 VCATTN_API int vcattn_attn_status(int* code, int* where, int* block, int reset);
 

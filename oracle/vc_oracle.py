@@ -651,7 +651,7 @@ def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_
 
 def attention_codes_units(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_m: int,
                           sm_scale: float, expcast: bool = False, beta: float = -0.35,
-                          floor_exp: int = -120, running_floor: bool = False) -> np.ndarray:
+                          floor_exp: int = -120) -> np.ndarray:
     """attention_codes (triton_attn.py:203-322) with the output accumulated the
     way a kernel that lets the P.V tensor-core MMA add into O itself must: in
     units of the current value block's scale.  With u_j = max(vs_j, floor) per
@@ -662,11 +662,7 @@ def attention_codes_units(prep: Dict[str, np.ndarray], n: int, block_rows: int, 
     block's scale sits at the amax clamp (a constant channel); such a block's
     codes are then counted at the floor's scale.  The result differs from
     attention_codes only by float32 rounding (and, for floored blocks, by at
-    most 448 * 2^floor_exp of max|V_c|).  With ``running_floor`` (the rule of
-    the two-query-tile tcgen05 kernel, which has no pre-pass over the head) the
-    floor of block j is 2^floor_exp times the running maximum over blocks
-    0..j of the bound |mu_i * vs_i| + 448 * vs_i, rounded as float32
-    operations.  Returns (G, N, D) float32.
+    most 448 * 2^floor_exp of max|V_c|).  Returns (G, N, D) float32.
     """
     q8 = e4m3_decode(prep["q"])
     k8 = e4m3_decode(prep["k"])
@@ -686,7 +682,6 @@ def attention_codes_units(prep: Dict[str, np.ndarray], n: int, block_rows: int, 
             l_i = np.zeros(rows, np.float32)
             oh = np.zeros((rows, d), np.float32)
             u_prev = r_prev = mu_prev = None
-            mrun = np.zeros(d, np.float32)
             for j in range(nb):
                 js, je = j * block_rows, (j + 1) * block_rows
                 sd = np.matmul(q8[gi, sm:em], k8[gi, js:je].T).astype(np.float32)
@@ -694,13 +689,7 @@ def attention_codes_units(prep: Dict[str, np.ndarray], n: int, block_rows: int, 
                 sc = (sc * F32(sm_scale)).astype(np.float32)
                 m_new, alpha, p8 = _tile_softmax(sc, np.arange(js, je) < n, m_i, expcast, beta)
                 r = p8.sum(-1, dtype=np.float32)                 # un-normalised row sum
-                if running_floor:
-                    vb = (np.abs((mu[gi, j] * vs[gi, j]).astype(np.float32))
-                          + (F32(P_SCALE) * vs[gi, j]).astype(np.float32)).astype(np.float32)
-                    mrun = np.maximum(mrun, vb)
-                    u = np.maximum(vs[gi, j], (mrun * F32(2.0 ** floor_exp)).astype(np.float32)).astype(np.float32)
-                else:
-                    u = np.maximum(vs[gi, j], floor).astype(np.float32)
+                u = np.maximum(vs[gi, j], floor).astype(np.float32)
                 if u_prev is not None:
                     oh = (oh + (r_prev[:, None] * mu_prev[None, :]).astype(np.float32)).astype(np.float32)
                     f = (alpha[:, None] * (u_prev / u).astype(np.float32)[None, :]).astype(np.float32)

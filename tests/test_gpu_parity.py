@@ -264,7 +264,7 @@ def _attn_gpu(q, k, v, perm, br, dev, expcast=False, out_dtype=torch.float32, ke
     cfg = TritonConfig(block_n=br, enable_expcast=expcast)
     attention_prepared(p, n, out, d ** -0.5, cfg, kernel=kernel)
     torch.cuda.synchronize()
-    if kernel in ("tc", "tc1"):
+    if kernel == "tc":
         assert attention_status() == (0, 0, 0), "a bounded wait of the tcgen05 kernel expired"
     return out.float().cpu().numpy().reshape(b * h, n, d)
 
@@ -273,7 +273,7 @@ def _kernels(d):
     return ["tc", "mma"] if d == 128 else ["mma"]
 
 
-@pytest.mark.parametrize("kernel", ["tc", "tc1", "mma"])
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
 @pytest.mark.parametrize("expcast", [False, True])
 def test_attention_config0(dev, expcast, kernel):
     g = _load("config0.npz")
@@ -315,51 +315,6 @@ def test_attention_shapes(dev, n, br, d, h, kernel):
         assert O.rel_l2(got, ref) <= REL_L2_REF
     sd = O.sdpa_f32(qg, kg, vg)
     assert abs(O.psnr(got, sd) - O.psnr(ref, sd)) <= PSNR_DB
-
-
-def _degenerate_qkv(seed, big=False):
-    """Inputs whose value blocks have a channel scale at the amax clamp (a
-    constant channel, a block of identical rows), optionally with |V| in the
-    thousands: the two-query-tile kernel's O accumulator (block-scale units)
-    needs its unit floor there."""
-    rng = np.random.default_rng(seed)
-    g, n, d = 2, 1000, 128
-    q = rng.standard_normal((g, n, d)).astype(np.float32)
-    k = (rng.standard_normal((g, n, d)) + rng.normal(0, 2, (g, 1, d))).astype(np.float32)
-    centres = rng.standard_normal((g, 64, d)) * (4096.0 if big else 1.0)
-    v = (centres[:, rng.integers(0, 64, n)] + 0.3 * rng.standard_normal((g, n, d))).astype(np.float32)
-    v[:, 128:256, 5] = 3000.0 if big else 3.0
-    v[:, 256:384, :] = v[:, 256:257, :]
-    perm = np.tile(np.arange(n, dtype=np.int32), (g, 1))
-    q, k, v = (O.bf16_round(x).reshape(1, g, n, d) for x in (q, k, v))
-    return q, k, v, perm
-
-
-@pytest.mark.parametrize("case", ["plain", "degenerate", "degenerate_big"])
-@pytest.mark.parametrize("expcast", [False, True])
-def test_two_query_tile_kernel_block_scale_units(dev, case, expcast):
-    """The default dense tcgen05 kernel (two query tiles per CTA, O in tensor
-    memory in units of the current value block's scale, running-max unit
-    floor) against the oracle of that order of operations, against the
-    code-unit oracle, and against the one-query-tile kernel."""
-    if case == "plain":
-        q, k, v = make_qkv(1, 2, 1000, 128, seed=77)
-        perm = np.stack([np.random.default_rng(70 + i).permutation(1000) for i in range(2)]).astype(np.int32)
-    else:
-        q, k, v, perm = _degenerate_qkv(78, big=(case == "degenerate_big"))
-    h, n, d = 2, 1000, 128
-    got = _attn_gpu(q, k, v, perm, 128, dev, expcast=expcast, kernel="tc")
-    one = _attn_gpu(q, k, v, perm, 128, dev, expcast=expcast, kernel="tc1")
-    assert np.isfinite(got).all()
-    prep = O.prepare(*(a.reshape(h, n, d) for a in (q, k, v)), perm, block_rows=128)
-    if case != "plain":
-        assert float(prep["v_scale"].min()) < 1e-30
-    units = O.attention_codes_units(prep, n, 128, 128, d ** -0.5, expcast=expcast, running_floor=True,
-                                    floor_exp=-80)
-    codes = O.attention_codes(prep, n, 128, 128, d ** -0.5, expcast=expcast)
-    assert O.rel_l2(got, units) <= 1e-4
-    assert O.rel_l2(got, codes) <= REL_L2_CODES
-    assert O.rel_l2(got, one) <= 1e-4
 
 
 def test_attention_bf16_output_and_layouts(dev):
@@ -524,19 +479,13 @@ def test_sparse_attention_matches_oracle(dev, expcast, kernel):
 @pytest.mark.parametrize("kernel", ["tc", "mma"])
 def test_sparse_keep_all_equals_dense(dev, kernel):
     """tau -> -inf keeps every block: the sparse kernel must reproduce the
-    dense kernel of the same arithmetic order bit for bit (exact tiles, same
-    order): the register-MMA pair, and the tcgen05 sparse kernel against the
-    one-query-tile dense kernel.  The two-query-tile dense kernel accumulates
-    O in block-scale units, so it matches to the code-unit tolerance."""
+    dense kernel of the same family bit for bit (exact tiles, same order)."""
     n, h = 1024, 2
     q, k, v, perm = _sparse_case(n, h)
     sparse, p = _sparse_gpu(q, k, v, perm, dev, tau=-1000.0, kernel=kernel)
     assert p.keep.bool().all()
-    dense = _attn_gpu(q, k, v, perm, 128, dev, kernel="tc1" if kernel == "tc" else kernel)
+    dense = _attn_gpu(q, k, v, perm, 128, dev, kernel=kernel)
     assert np.array_equal(sparse, dense)
-    if kernel == "tc":
-        dense2 = _attn_gpu(q, k, v, perm, 128, dev, kernel="tc")
-        assert O.rel_l2(sparse, dense2) <= REL_L2_CODES
 
 
 @pytest.mark.parametrize("kernel", ["tc", "mma"])
