@@ -87,6 +87,7 @@ struct TcSmem {
   alignas(8) uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  int kvn;   // keys taking part in this CTA's head
 };
 
 struct TcArgs {
@@ -99,6 +100,7 @@ struct TcArgs {
   float c120;   // 64 + 56 + beta (ExpCast)
   void* out;
   int64_t osb, osh, osn;
+  const int32_t* kv_len;   // (B,) keys taking part per batch entry, or null (all N)
 };
 
 // ECM: 0 = E4M3 of exp2, 1 = one-FMA ExpCast, 2 = ExpCast in the reference's
@@ -119,6 +121,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nb = a.nb;
 
   if (tid == 0) {
+    // Keys at (permuted) positions >= kvn take no part (reference.py
+    // valid_len, padding sorted to the tail by grouping.py:181-183); only the
+    // tiles holding keys below kvn are visited.
+    sm.kvn = a.kv_len ? min(a.N, max(1, a.kv_len[g / a.H])) : a.N;
+
     sm.abort = 0;
     mbar_init(&sm.q_full, 1);
     for (int s = 0; s < kStages; ++s) {
@@ -151,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tbase = sm.tmem_base;
   volatile int* abort = &sm.abort;
+#define VC_TILES_VISITED ((sm.kvn + BR - 1) / BR)
 
   if (warp < 4) {
   // Register budget per warpgroup (launched at 168 x 384 = 64512):
@@ -166,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_expect_tx(&sm.q_full, kBM * 128);
       tma_load_2d(sm.q, &tm_q, 0, g * a.n_pad + row0, &sm.q_full);
       const uint32_t tile_bytes = 2u * BR * 128u + BR * 4u + 2u * kD * 4u;
-      for (int j = 0; j < nb; ++j) {
+      for (int j = 0; j < VC_TILES_VISITED; ++j) {
         const int s = j % kStages;
         if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, status, 1)) break;
         mbar_expect_tx(&sm.kv_full[s], tile_bytes);
@@ -199,8 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t q_addr = smem_u32(sm.q);
       const uint32_t ones_addr = smem_u32(sm.ones);
       bool ok = mbar_wait(&sm.q_full, 0, abort, status, 2);
-      for (int j = 0; ok && j <= nb; ++j) {
-        if (j < nb) {
+      for (int j = 0; ok && j <= VC_TILES_VISITED; ++j) {
+        if (j < VC_TILES_VISITED) {
           // S_b was last read as P by PV_{j-2}, issued earlier by this thread
           // (tcgen05.mma from one thread run in order), after p_full(j-2).
           const int s = j % kStages, b = j & 1;
@@ -245,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ per-tile factors
     const int c2 = tid - 64;   // 0..63
-    for (int j = 0; j < nb; ++j) {
+    for (int j = 0; j < VC_TILES_VISITED; ++j) {
       const int s = j % kStages, ring = j % kRing;
       if (!mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 13)) break;
       if (j >= kRing && !mbar_wait(&sm.f_free[ring], ((j / kRing) + 1) & 1, abort, status, 14)) break;
@@ -278,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The row max is kept in x units (x = S * ks), or in score units s for ECM 2.
     const float Ae = (ECM == 2) ? kLog2e : __fmul_rn(qsm, kLog2e);
     float m = -INFINITY;
-    for (int j = 0; j < nb; ++j) {
+    for (int j = 0; j < VC_TILES_VISITED; ++j) {
       const int b = j & 1, ring = j % kRing, s = j % kStages;
       // ks of tile j came with its K/V stage (bulk copy completed on kv_full)
       if (!mbar_wait2(&sm.s_full[b], (j >> 1) & 1, &sm.kv_full[s], (j / kStages) & 1, abort, status, 7)) break;
@@ -310,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mul2(x[4 * q + 2], x[4 * q + 3], kv.z, kv.w);
         }
       }
-      const int valid = a.N - j * BR;                 // keys >= valid are padding
+      const int valid = sm.kvn - j * BR;                 // keys >= valid are padding or masked
       if (valid < BR) {
 #pragma unroll
         for (int c = 0; c < BR; ++c)
@@ -394,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int c = 0; c < kD; ++c) o[c] = 0.f;
     float l = 0.f;
     bool ok = true;
-    for (int i = 0; i < nb; ++i) {
+    for (int i = 0; i < VC_TILES_VISITED; ++i) {
       const int ring = i % kRing, tb = i & 1;
       ok = mbar_wait(&sm.t_full[tb], (i >> 1) & 1, abort, status, 11);
       if (!ok) break;
@@ -479,6 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) tmem_dealloc(tbase, 512);
 }
+#undef VC_TILES_VISITED
 
 // ---- host side ---------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -523,6 +532,7 @@ cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
   a.sm_scale = p.sm_scale;
   a.c120 = static_cast<float>(64.0 + 56.0 + p.beta);
   a.out = p.out; a.osb = p.osb; a.osh = p.osh; a.osn = p.osn;
+  a.kv_len = p.kv_len;
   const size_t smem = sizeof(TcSmem<BR>) + 1024;
   auto k = attn_tc_kernel<BR, EC, ODT>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

@@ -346,6 +346,33 @@ int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8, 
   return VCATTN_OK;
 }
 
+int vcattn_attn_fp8_masked(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
+                           const uint8_t* v8, const float* v_scale, const float* mu, const int32_t* kv_len, int B,
+                           int H, int N, int n_pad, int D, int block_rows, float sm_scale, int flags,
+                           double expcast_beta, void* out, int out_dtype, int64_t out_sb, int64_t out_sh,
+                           int64_t out_sn, void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_attn_fp8_masked")) return fail(VCATTN_ERR_INJECTED, "vcattn_attn_fp8_masked: injected fault");
+  const int rc = attn_common_checks("vcattn_attn_fp8_masked", q8, q_scale, k8, k_scale, v8, v_scale, mu, B, H, N,
+                                    n_pad, D, block_rows, out, out_dtype);
+  if (rc != VCATTN_OK) return rc;
+  VC_CHECK(kv_len != nullptr, "vcattn_attn_fp8_masked: null kv_len");
+  VC_CHECK(D == 128, "vcattn_attn_fp8_masked: needs D = 128 (the tcgen05 kernel)");
+  VC_CHECK(aligned16(out) && (out_sn % 8) == 0 && (out_sh % 8) == 0 && (out_sb % 8) == 0,
+           "vcattn_attn_fp8_masked: out must be 16-byte aligned with 8-element multiple strides");
+  AttnParams p{};
+  p.q8 = q8; p.k8 = k8; p.v8 = v8; p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
+  p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
+  p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
+  p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
+  p.kv_len = kv_len;
+  const cudaError_t e = launch_attn_tc(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(VCATTN_ERR_CUDA,
+                std::string("vcattn_attn_fp8_masked: ") + cudaGetErrorString(e) + " [" + attn_tc_diag() + "]");
+  return VCATTN_OK;
+}
+
 int vcattn_attn_fp8_mma(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
                         const uint8_t* v8t, const float* v_scale, const float* mu, int B, int H, int N, int n_pad,
                         int D, int block_rows, float sm_scale, int flags, double expcast_beta, void* out,

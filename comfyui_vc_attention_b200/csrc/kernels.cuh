@@ -68,6 +68,7 @@ struct AttnParams {
   void* out;
   int out_dtype;
   int64_t osb, osh, osn;
+  const int32_t* kv_len;   // (B,) keys taking part per batch entry (dense tcgen05 kernel), or nullptr
 };
 
 size_t prepare_workspace_bytes(int G, int N, int D);

@@ -91,6 +91,9 @@ _SIGNATURES = {
     "vcattn_attn_fp8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_double,
                                 c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p]),
+    "vcattn_attn_fp8_masked": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int,
+                                       c_double, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p]),
     "vcattn_attn_fp8_mma": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
                                     c_int, c_double, c_void_p, c_int, c_int64, c_int64, c_int64,

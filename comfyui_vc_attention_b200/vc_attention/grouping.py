@@ -121,16 +121,34 @@ def kmeans(v: torch.Tensor, k: int, cfg: GroupingConfig,
 
 def build_permutation(v: torch.Tensor, cfg: GroupingConfig, tags: Optional[torch.Tensor] = None,
                       centroids: Optional[torch.Tensor] = None,
-                      valid_len: Optional[int] = None) -> GroupingResult:
+                      valid_len: Optional[int] = None,
+                      pad_mask: Optional[torch.Tensor] = None) -> GroupingResult:
     """V-Smooth permutation of one value tensor (G, N, D).
 
     ``tags`` (N,) modality tags are a secondary key when ``cfg.modality_aware``
     (pad tag -1 sorts last); rows >= ``valid_len`` are pushed to the tail.
+    ``pad_mask`` (N,) bool (this build; may live on the device) generalises
+    ``valid_len`` to any set of padding rows: they get the same pad key
+    (grouping.py:181-183), so they sort to the tail in their original order.
     """
     if v.dim() == 4:
         v = v.reshape(-1, v.shape[-2], v.shape[-1]) if not v.is_contiguous() else v.view(-1, v.shape[-2], v.shape[-1])
     g, n, d = v.shape
     k = num_clusters(n, cfg)
+    if pad_mask is not None:
+        if valid_len is not None:
+            raise ValueError("give valid_len or pad_mask, not both")
+        if pad_mask.shape != (n,):
+            raise ValueError(f"pad_mask must be ({n},)")
+        off = pad_mask.to(device=v.device, dtype=torch.int32) * (16 * (k + 1))
+        nkeys = 16 * (k + 1) + k
+        if cfg.modality_aware and tags is not None:
+            tag = tags.detach().to(v.device, torch.int64).clamp(min=-1)
+            tag = torch.where(tag < 0, torch.full_like(tag, 8), tag)
+            off = off + (tag * (k + 1)).to(torch.int32)
+            nkeys += 8 * (k + 1)
+        labels, cent, perm = kmeans(v, k, cfg, centroids, off, nkeys)
+        return GroupingResult(perm=perm, centroids=cent, k=k, labels=labels)
     key_offset = None
     nkeys = k
     if (cfg.modality_aware and tags is not None) or (valid_len is not None and valid_len < n):

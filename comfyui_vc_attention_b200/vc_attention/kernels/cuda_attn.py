@@ -293,14 +293,18 @@ def _out_view(q: torch.Tensor, dtype: torch.dtype):
 
 def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                       perm: Optional[torch.Tensor] = None, cfg: Optional[TritonConfig] = None,
-                      scale: Optional[float] = None) -> torch.Tensor:
+                      scale: Optional[float] = None, kv_len: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Fused VC-Attention (triton_attn.py:757-855 semantics, no fallback).
 
     q, k, v: (B, H, N, D) CUDA bf16/fp16/fp32 (strided views accepted);
     perm: (G, N) or (1, N) int32 V-Smooth permutation or None.
+    kv_len: None, or a (B,) int32 CUDA tensor: in batch entry b only the
+    first kv_len[b] keys of the permuted order take part (key padding,
+    reference.py ``valid_len``); the permutation must have sorted the
+    excluded keys to the tail.  Dense FP8, D = 128 only.
     Returns (B, H, N, D) in q.dtype.
     """
-    return _attention_into(q, k, v, perm, cfg, scale, None)
+    return _attention_into(q, k, v, perm, cfg, scale, None, kv_len)
 
 
 def _call_config(cfg, d):
@@ -349,7 +353,7 @@ def slice_prepared(p: Prepared, i: int) -> Prepared:
     return p._replace(**upd)
 
 
-def _attention_into(q, k, v, perm, cfg, scale, out):
+def _attention_into(q, k, v, perm, cfg, scale, out, kv_len=None):
     """vc_attention_cuda writing into ``out`` ((B, H, N, D) view of q's dtype,
     d contiguous), or into a new buffer when ``out`` is None."""
     _check_qkv(q, k, v)
@@ -362,16 +366,18 @@ def _attention_into(q, k, v, perm, cfg, scale, out):
         out = _out_view(q, q.dtype)
     elif out.shape != q.shape or out.dtype != q.dtype or out.stride(-1) != 1:
         raise ValueError("out must be a (B, H, N, D) view of q's dtype with d contiguous")
-    return attention_prepared(p, n, out, scale, cfg)
+    return attention_prepared(p, n, out, scale, cfg, kv_len=kv_len)
 
 
 def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
-                       cfg: TritonConfig, kernel: str = "auto") -> torch.Tensor:
+                       cfg: TritonConfig, kernel: str = "auto",
+                       kv_len: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Run the attention kernel on prepared operands, writing into ``out``.
 
     kernel: "tc" (tcgen05, D = 128, needs ``p.v``), "mma" (register MMA,
     needs ``p.v_t``) or "auto" (tcgen05 whenever it applies), for the dense
-    and the sparse path alike.
+    and the sparse path alike.  ``kv_len`` ((B,) int32 on the device) runs
+    the key-padding masked dense tcgen05 kernel (vcattn_attn_fp8_masked).
     """
     lib = N.lib()
     b, h, n_pad, d = (p.q if p.q is not None else p.v).shape
@@ -380,6 +386,18 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
         flags |= N.EXPCAST_EXACT
     odt = _dtype_code(out)
     st = _stream(out)
+    if kv_len is not None:
+        if cfg.sparse or cfg.qk_fp4 or d != 128 or p.v is None or p.v_mma_order or kernel not in ("auto", "tc"):
+            raise ValueError("masked attention runs on the dense FP8 tcgen05 kernel (D = 128, token-order V)")
+        kl = kv_len.to(device=out.device, dtype=torch.int32).contiguous()
+        if kl.shape != (b,):
+            raise ValueError(f"kv_len must be ({b},), got {tuple(kl.shape)}")
+        N.check("vcattn_attn_fp8_masked", lib.vcattn_attn_fp8_masked(
+            p.q.view(torch.uint8).data_ptr(), p.q_scale.data_ptr(), p.k.view(torch.uint8).data_ptr(),
+            p.k_scale.data_ptr(), p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(),
+            kl.data_ptr(), b, h, n, n_pad, d, p.block_rows, float(scale), flags, float(cfg.expcast_beta),
+            out.data_ptr(), odt, out.stride(0), out.stride(1), out.stride(2), st))
+        return out
     if cfg.qk_fp4 and not cfg.sparse:
         if p.q4 is None or p.v is None or p.v_mma_order:
             raise ValueError("the NVFP4 kernel needs prepare(qk_fp4=True, want_v=True, v_mma_order=False)")

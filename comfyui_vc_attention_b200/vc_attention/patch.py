@@ -90,6 +90,7 @@ class VCAttentionRuntime:
                                       min_tokens=self.config.min_tokens)
         self.tracker = StepTracker(total_steps_hint=self.config.total_steps_hint)
         self.cache = PermutationCache()
+        self._mask_cache: Dict[tuple, tuple] = {}
         self.tags: Optional[torch.Tensor] = None
         self.stats: Dict[str, int] = {"calls": 0, "used": 0, "skipped": 0, "grouped": 0}
 
@@ -103,6 +104,7 @@ class VCAttentionRuntime:
     def reset(self) -> None:
         self.tracker.reset()
         self.cache.clear()
+        self._mask_cache.clear()
 
     def set_tags(self, tags: Optional[torch.Tensor]) -> None:
         self.tags = tags
@@ -135,7 +137,7 @@ class VCAttentionRuntime:
         """VC-Attention output, or None to defer to the original attention."""
         self.stats["calls"] += 1
         cfg = self.config
-        if not cfg.enabled or is_causal or attn_mask is not None or (dropout_p or 0.0) > 0.0:
+        if not cfg.enabled or is_causal or (dropout_p or 0.0) > 0.0:
             self.stats["skipped"] += 1
             return None
         if not all(isinstance(t, torch.Tensor) for t in (q, k, v)) or q.dim() != 4 \
@@ -150,6 +152,14 @@ class VCAttentionRuntime:
         if q.device.type != "cuda" or not fast_path_available(q.device):
             self.stats["skipped"] += 1
             return None
+        if attn_mask is not None:
+            # Key padding only (the reference defers on any mask, README.md:514-515)
+            keep = key_padding_mask(attn_mask, b, n)
+            if keep is None or d != 128:
+                self.stats["skipped"] += 1
+                return None
+            self.stats["used"] += 1
+            return self._masked_attention(q, k, v, keep.to(q.device), attn_mask, scale)
         perm = self.permutation(v)
         if perm is not None:
             self.stats["grouped"] += 1
@@ -166,6 +176,72 @@ class VCAttentionRuntime:
             sink_blocks=max(0, int(cfg.sink_tokens) // max(1, cfg.block_rows)),
         )
         return vc_attention_triton(q, k, v, perm=perm, cfg=tcfg, scale=scale)
+
+    def _masked_attention(self, q, k, v, keep: torch.Tensor, mask_key: torch.Tensor,
+                          scale: Optional[float]) -> torch.Tensor:
+        """Dense FP8 VC-Attention with key padding: per batch entry the masked
+        keys get the pad key of grouping.py:181-183 (sorted to the tail of the
+        V-Smooth permutation) and the kernel stops at the count of kept keys
+        (reference.py ``valid_len``).  The permutation and counts are cached
+        for the same mask tensor within a grouping window."""
+        cfg = self.config
+        b, h, n, d = q.shape
+        step = self.tracker.current
+        group = cfg.enable_vsmooth and self.schedule.should_group(step, self.tracker.total_steps)
+        key = (self.schedule.window_index(step) if group else -1, n, b * h, mask_key.data_ptr(),
+               mask_key._version, tuple(mask_key.shape))
+        cached = self._mask_cache.get(key)
+        if cached is None or (group and self.schedule.should_recompute(step)):
+            pad = ~keep
+            perms = []
+            for bi in range(b):
+                if group:
+                    gcfg = GroupingConfig(block_rows=cfg.block_rows, iters=cfg.kmeans_iters,
+                                          warm_iters=cfg.warm_iters, modality_aware=cfg.modality_aware)
+                    perms.append(build_permutation(v[bi:bi + 1], gcfg, tags=self.tags, pad_mask=pad[bi]).perm)
+                else:
+                    order = torch.argsort(pad[bi].to(torch.int32), stable=True).to(torch.int32)
+                    perms.append(order.unsqueeze(0).expand(h, n))
+            cached = (torch.cat(perms, 0).contiguous(), keep.sum(-1).to(torch.int32))
+            if len(self._mask_cache) >= 8:
+                self._mask_cache.pop(next(iter(self._mask_cache)))
+            self._mask_cache[key] = cached
+        if group:
+            self.stats["grouped"] += 1
+        perm, kv_len = cached
+        from .kernels.cuda_attn import TritonConfig, vc_attention_triton
+        tcfg = TritonConfig(block_m=cfg.block_m, block_n=cfg.block_rows,
+                            enable_expcast=bool(cfg.enable_expcast), sparse=False)
+        return vc_attention_triton(q, k, v, perm=perm, cfg=tcfg, scale=scale, kv_len=kv_len)
+
+
+def key_padding_mask(attn_mask: Any, b: int, n: int) -> Optional[torch.Tensor]:
+    """(B, N) bool keep-mask when ``attn_mask`` (SDPA convention: bool True =
+    attend, or additive float with 0 / -inf) only masks keys, the same for
+    every head and query; None for any other mask.  2-D and 3-D masks follow
+    ComfyUI's reshaping (L, S) -> (1, L, S) -> (B, 1, L, S)."""
+    m = attn_mask
+    if not isinstance(m, torch.Tensor) or m.dim() == 0 or m.dim() > 4:
+        return None
+    if m.dim() == 1:
+        m = m.view(1, 1, 1, -1)
+    if m.dim() == 2:
+        m = m.unsqueeze(0)
+    if m.dim() == 3:
+        m = m.unsqueeze(1)
+    if m.shape[-1] != n or m.shape[1] != 1 or m.shape[2] != 1 or m.shape[0] not in (1, b):
+        return None
+    m = m[:, 0, 0, :]
+    if m.dtype == torch.bool:
+        keep = m
+    elif m.is_floating_point():
+        neg = torch.isneginf(m)
+        if not bool(((m == 0) | neg).all()):
+            return None
+        keep = ~neg
+    else:
+        return None
+    return keep.expand(b, n)
 
 
 def fast_path_available(device: Optional[torch.device] = None) -> bool:
@@ -209,13 +285,13 @@ def _try_vc(runtime: VCAttentionRuntime, q, k, v, heads: int, mask=None,
     (B, H, N, D) without a copy (the kernels read strided views) and the
     output comes back in the caller's layout.
     """
-    if not runtime.config.enabled or mask is not None:
+    if not runtime.config.enabled:
         return None
     if not all(isinstance(t, torch.Tensor) for t in (q, k, v)):
         return None
     if q.dim() == 4:
         b, h_, s_, d_ = q.shape
-        out = runtime.attention(q, k, v)
+        out = runtime.attention(q, k, v, attn_mask=mask)
         if out is None:
             return None
         return out if skip_output_reshape else out.transpose(1, 2).reshape(b, s_, h_ * d_)
@@ -226,7 +302,7 @@ def _try_vc(runtime: VCAttentionRuntime, q, k, v, heads: int, mask=None,
     q4 = q.view(b, n, heads, d).transpose(1, 2)
     k4 = k.view(k.shape[0], k.shape[1], heads, d).transpose(1, 2)
     v4 = v.view(v.shape[0], v.shape[1], heads, d).transpose(1, 2)
-    out = runtime.attention(q4, k4, v4)
+    out = runtime.attention(q4, k4, v4, attn_mask=mask)
     if out is None:
         return None
     return out if skip_output_reshape else out.transpose(1, 2).reshape(b, n, heads * d)

@@ -222,6 +222,22 @@ VCATTN_API int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const ui
                     void* out, int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn,
                     void* stream);
 
+/* ---- masked (key-padding) dense FP8 attention: reference.py:162-294 with
+ * valid_len (keys at positions >= valid_len masked out), per batch entry.
+ * The reference applies valid_len to the permuted key order, after
+ * build_permutation(valid_len=...) has sorted the padding keys to the tail
+ * (grouping.py:176-183); its Triton path does not run masked attention
+ * (README.md:514-515).  Same operands as vcattn_attn_fp8; kv_len is a device
+ * array (B,) int32: in batch entry b only keys 0 .. kv_len[b]-1 of the
+ * (permuted) order take part (values below 1 count as 1, above N as N), and
+ * KV tiles past the last such key are not visited.  D = 128. */
+VCATTN_API int vcattn_attn_fp8_masked(const uint8_t* q8, const float* q_scale, const uint8_t* k8,
+                    const float* k_scale, const uint8_t* v8, const float* v_scale,
+                    const float* mu, const int32_t* kv_len, int B, int H, int N, int n_pad, int D,
+                    int block_rows, float sm_scale, int flags, double expcast_beta,
+                    void* out, int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn,
+                    void* stream);
+
 /* Same computation on the register-MMA (mma.sync m16n8k32) kernel, for head
  * dims 64 and 128; V as the block-transposed v8t (G,NB,D,block_rows).  P bytes
  * follow the reference's ExpCast operation order exactly. */

@@ -496,11 +496,13 @@ def expcast_codes(s: np.ndarray, m: np.ndarray, beta: float = -0.35) -> np.ndarr
 
 def attention_reference(q, k, v, perm=None, block_rows=128, block_m=64, expcast=False,
                         beta=-0.35, scale=None, vsmooth=True, hadamard=True,
-                        smooth_k=True, q_rows=None) -> np.ndarray:
+                        smooth_k=True, q_rows=None, valid_len=None) -> np.ndarray:
     """vc_attention_reference (kernels/reference.py:162-294), backend fp8, in
     fp32 value units.  q,k,v: (G,N,D) float32.  Returns (G,N,D) float32, or
     (G,q_rows,D) when only the first ``q_rows`` query rows are wanted (the
-    CPU-baseline sample; every query row costs the same).
+    CPU-baseline sample; every query row costs the same).  ``valid_len``
+    (reference.py:197, 251-256): keys at permuted positions >= valid_len are
+    masked out (score -1e30), like the zero padding past N.
     """
     g, n, d = q.shape
     if scale is None:
@@ -543,8 +545,9 @@ def attention_reference(q, k, v, perm=None, block_rows=128, block_m=64, expcast=
         for j in range(nb):
             js, je = j * block_rows, (j + 1) * block_rows
             s = np.matmul(qb, k_hat[:, js:je, :].transpose(0, 2, 1)).astype(np.float32)
-            if n < n_pad:
-                s = np.where((np.arange(js, je) >= n)[None, None, :], F32(-1e30), s)
+            n_valid = n if valid_len is None else valid_len
+            if n_valid < n_pad:
+                s = np.where((np.arange(js, je) >= n_valid)[None, None, :], F32(-1e30), s)
             m_new = np.maximum(mb, s.max(-1))
             m_new = np.where(np.isneginf(m_new), F32(0), m_new).astype(np.float32)
             if expcast:
@@ -618,12 +621,16 @@ def _row_starts(n: int, block_m: int, row_blocks: Optional[Sequence[int]]):
 
 def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_m: int,
                     sm_scale: float, expcast: bool = False, beta: float = -0.35,
-                    row_blocks: Optional[Sequence[int]] = None) -> np.ndarray:
+                    row_blocks: Optional[Sequence[int]] = None,
+                    kv_len: Optional[Sequence[int]] = None) -> np.ndarray:
     """The fused kernel's arithmetic in code units (triton_attn.py:203-322):
     s = dot(q8,k8) * (qs*ks) * sm_scale ; P as E4M3 (exp2*448 cast or ExpCast);
     r = sum(P)/448 ; acc = alpha*acc + (P@V8)*vs/448 + r*mu*vs ; O = acc/l.
     Consumes prepare() output; returns (G, N, D) float32.  ``row_blocks``
     restricts the evaluation to those query blocks (full-size spot checks).
+    ``kv_len`` (G,): per head, only keys below it take part (key padding,
+    reference.py valid_len); KV tiles entirely past it are not visited, which
+    leaves every value as if they had been visited with all keys masked.
     """
     q8 = e4m3_decode(prep["q"])
     k8 = e4m3_decode(prep["k"])
@@ -639,11 +646,12 @@ def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_
             m_i = np.full(rows, -np.inf, np.float32)
             l_i = np.zeros(rows, np.float32)
             acc = np.zeros((rows, d), np.float32)
-            for j in range(nb):
+            kv = n if kv_len is None else max(1, min(n, int(kv_len[gi])))
+            for j in range(-(-kv // block_rows)):
                 js, je = j * block_rows, (j + 1) * block_rows
                 m_i, l_i, acc = _exact_tile(
                     q8[gi, sm:em], qs[gi, sm:em], k8[gi, js:je], ks[gi, js:je], v8[gi, js:je],
-                    vs[gi, j], mu[gi, j], np.arange(js, je) < n, sm_scale, m_i, l_i, acc,
+                    vs[gi, j], mu[gi, j], np.arange(js, je) < kv, sm_scale, m_i, l_i, acc,
                     expcast, beta)
             out[gi, sm:em] = acc / l_i[:, None]
     return out

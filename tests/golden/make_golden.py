@@ -2,7 +2,7 @@
 
 Run once, where the reference package is importable (read-only source tree):
 
-    python tests/golden/make_golden.py [--reference PATH] [--only base,sparse,nvfp4]
+    python tests/golden/make_golden.py [--reference PATH] [--only base,sparse,nvfp4,masked]
 
 It imports bingling360/comfyui_vc_attention (``vc_attention``), runs the
 reference's own functions on seeded inputs from ``oracle/inputs.py`` and writes
@@ -31,7 +31,7 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("VC_REFERENCE", "/root/reference"))
     ap.add_argument("--only", default="",
-                    help="comma-separated fixture groups to (re)write: base, sparse, nvfp4 (default all)")
+                    help="comma-separated fixture groups to (re)write: base, sparse, nvfp4, masked (default all)")
     args = ap.parse_args()
     only = set(filter(None, args.only.split(",")))
     sys.path.insert(0, args.reference)
@@ -50,6 +50,8 @@ def main() -> int:
         make_sparse(args.reference)
     if not only or "nvfp4" in only:
         make_nvfp4()
+    if not only or "masked" in only:
+        make_masked()
     if only and "base" not in only:
         return _report()
 
@@ -325,6 +327,35 @@ def make_nvfp4() -> None:
         print(f"  reference backend {backend}: PSNR {_psnr(o, sd):.2f} dB")
     np.savez_compressed(os.path.join(HERE, "nvfp4_ref.npz"), **res)
 
+
+
+def make_masked() -> None:
+    """masked.npz: key padding as the reference defines it.  build_permutation
+    with valid_len (grouping.py:150-186: padding rows get the pad key and sort
+    to the tail) and vc_attention_reference with the same valid_len
+    (reference.py:162-294: keys at permuted positions >= valid_len masked),
+    plain and ExpCast, with their PSNR against fp32 SDPA whose boolean mask
+    drops the same keys (tokens >= valid_len in the original order)."""
+    import torch
+    from vc_attention.grouping import GroupingConfig, build_permutation
+    from vc_attention.kernels.reference import RefConfig, vc_attention_reference
+
+    H, n, D, BR, VL = 2, 1024, 128, 128, 800
+    q, k, v = make_qkv(1, H, n, D, seed=9)
+    qt, kt, vt = (torch.from_numpy(a).to(torch.bfloat16) for a in (q, k, v))
+    perm = build_permutation(vt.reshape(H, n, D), GroupingConfig(block_rows=BR, iters=3), valid_len=VL).perm
+    keep = torch.arange(n) < VL
+    sd = torch.nn.functional.scaled_dot_product_attention(qt.float(), kt.float(), vt.float(),
+                                                          attn_mask=keep[None, None, None, :])
+    res = {"digest": np.array(digest(q, k, v)), "perm": perm.numpy(), "valid_len": np.int32(VL)}
+    for name, ec in (("plain", False), ("expcast", True)):
+        o = vc_attention_reference(qt.float(), kt.float(), vt.float(),
+                                   RefConfig(backend="fp8", block_rows=BR, block_m=64, enable_vsmooth=True,
+                                             enable_expcast=ec), perm=perm, valid_len=VL)
+        res[f"out_{name}"] = o.numpy()
+        res[f"psnr_{name}"] = np.float32(_psnr(o, sd))
+        print(f"  masked reference ({name}): PSNR {_psnr(o, sd):.2f} dB vs masked SDPA")
+    np.savez_compressed(os.path.join(HERE, "masked.npz"), **res)
 
 if __name__ == "__main__":
     sys.exit(main())

@@ -133,10 +133,11 @@ def test_try_vc_reshapes_3d_and_4d(monkeypatch):
     class RT:
         config = VCAttentionConfig()
 
-        def attention(self, q, k, v):
+        def attention(self, q, k, v, attn_mask=None):
             seen["shape"] = tuple(q.shape)
             seen["stride"] = q.stride()
-            return q * 2
+            seen["mask"] = attn_mask
+            return None if attn_mask is not None else q * 2
 
     q3 = torch.randn(2, 10, 4 * 8)
     out = _try_vc(RT(), q3, q3, q3, 4)
@@ -144,7 +145,8 @@ def test_try_vc_reshapes_3d_and_4d(monkeypatch):
     assert torch.allclose(out, q3 * 2)
     q4 = torch.randn(2, 4, 10, 8)
     assert torch.allclose(_try_vc(RT(), q4, q4, q4, 4, skip_output_reshape=True), q4 * 2)
-    assert _try_vc(RT(), q3, q3, q3, 4, mask=torch.ones(1)) is None
+    m = torch.ones(1)
+    assert _try_vc(RT(), q3, q3, q3, 4, mask=m) is None and seen["mask"] is m   # handed to the runtime
     assert _try_vc(RT(), q3, q3, q3, 5) is None
 
 
@@ -201,3 +203,24 @@ def test_host_chunk_bounds_cover_every_unit_once():
             if g > 1:
                 assert b[-1][1] - b[-1][0] == 1
     assert [hi - lo for lo, hi in _chunk_bounds(56, 4)] == [4] * 13 + [2, 1, 1]
+
+
+def test_key_padding_mask_forms():
+    """Which attention masks the router accepts: key padding only (the same
+    for every head and query), as bool (True = attend) or additive 0/-inf."""
+    from comfyui_vc_attention_b200.vc_attention.patch import key_padding_mask
+    b, n = 2, 8
+    keep = torch.ones(b, n, dtype=torch.bool)
+    keep[0, 6:] = False
+    keep[1, 3] = False
+    got = key_padding_mask(keep[:, None, None, :], b, n)
+    assert torch.equal(got, keep)
+    add = torch.zeros(b, 1, n)
+    add[:, 0][~keep] = float("-inf")
+    assert torch.equal(key_padding_mask(add, b, n), keep)              # (B, 1, S) -> (B, 1, 1, S)
+    assert torch.equal(key_padding_mask(keep[0], b, n), keep[0].expand(b, n))   # (S,) broadcast
+    assert key_padding_mask(torch.zeros(b, 1, n) + 0.5, b, n) is None      # a real bias
+    assert key_padding_mask(torch.ones(b, 1, 4, n, dtype=torch.bool), b, n) is None   # varies by query
+    assert key_padding_mask(torch.ones(b, 3, 1, n, dtype=torch.bool), b, n) is None   # varies by head
+    assert key_padding_mask(torch.ones(b, 1, 1, n + 1, dtype=torch.bool), b, n) is None
+    assert key_padding_mask(torch.ones(b, n, dtype=torch.int32), b, n) is None

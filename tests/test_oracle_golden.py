@@ -296,3 +296,29 @@ def test_sparse_oracle_matches_reference_simulation(sparse_ref):
     assert O.rel_l2(out, sim) <= 5e-2
     sd = O.sdpa_f32(q, k, v)
     assert abs(O.psnr(out, sd) - float(sparse_ref["s2k_sim_psnr"])) <= 0.3
+
+
+# ---------------------------------------------------------------------------
+# Key padding (valid_len) against the reference (tests/golden/masked.npz)
+# ---------------------------------------------------------------------------
+
+def test_masked_attention_oracle_matches_reference():
+    """reference.py's valid_len: keys at permuted positions >= valid_len take
+    no part; the permutation (build_permutation(valid_len=...)) has sorted the
+    padding rows to the tail.  The oracle's permutation with the same pad key
+    and its attention both match the reference."""
+    g = _load("masked.npz")
+    h, n, d = 2, 1024, 128
+    q, k, v = make_qkv(1, h, n, d, seed=9)
+    assert digest(q, k, v) == str(g["digest"])
+    vl = int(g["valid_len"])
+    qg, kg, vg = (a.reshape(h, n, d) for a in (q, k, v))
+    perm, _, _, _ = O.build_permutation(vg, block_rows=128, iters=3, valid_len=vl)
+    assert np.array_equal(perm, g["perm"])
+    assert (g["perm"][:, vl:] >= vl).all()          # padding rows sit at the tail
+    for name, ec in (("plain", False), ("expcast", True)):
+        out = O.attention_reference(qg, kg, vg, g["perm"], block_rows=128, block_m=64, expcast=ec, valid_len=vl)
+        assert O.rel_l2(out, g[f"out_{name}"].reshape(out.shape)) <= 2e-4
+    prep = O.prepare(qg, kg, vg, g["perm"], block_rows=128)
+    codes = O.attention_codes(prep, n, 128, 64, d ** -0.5, kv_len=[vl, vl])
+    assert O.rel_l2(codes, g["out_plain"].reshape(codes.shape)) <= 2e-3
