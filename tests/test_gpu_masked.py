@@ -40,15 +40,18 @@ def _bf16(a, dev):
 
 
 def _masked_gpu(q, k, v, perm, kv_len, dev, expcast=False):
-    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_status,
-                                                                          vc_attention_cuda)
-    out = vc_attention_cuda(_bf16(q, dev), _bf16(k, dev), _bf16(v, dev),
-                            torch.from_numpy(np.ascontiguousarray(perm)).to(dev),
-                            TritonConfig(block_n=128, enable_expcast=expcast), None,
-                            kv_len=torch.tensor(kv_len, dtype=torch.int32, device=dev))
+    """The masked kernel on prepared operands, fp32 output."""
+    from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
+                                                                          attention_status, prepare_for)
+    qt, kt, vt = _bf16(q, dev), _bf16(k, dev), _bf16(v, dev)
+    cfg = TritonConfig(block_n=128, enable_expcast=expcast)
+    p = prepare_for(qt, kt, vt, torch.from_numpy(np.ascontiguousarray(perm)).to(dev), cfg)
+    out = torch.empty(qt.shape, dtype=torch.float32, device=dev)
+    attention_prepared(p, qt.shape[2], out, qt.shape[3] ** -0.5, cfg,
+                       kv_len=torch.tensor(kv_len, dtype=torch.int32, device=dev))
     torch.cuda.synchronize()
     assert attention_status() == (0, 0, 0)
-    return out.float().cpu().numpy()
+    return out.cpu().numpy()
 
 
 @pytest.mark.parametrize("expcast", [False, True])
@@ -107,7 +110,7 @@ def test_router_takes_key_padding_masks(dev):
     mask = keep[:, None, None, :].to(dev)
     rt = VCAttentionRuntime(VCAttentionConfig(min_tokens=1024, enable_sparsity=True))
     out = rt.attention(q, k, v, attn_mask=mask)
-    assert out is not None and rt.stats["used"] == 1
+    assert out is not None and out.dtype == torch.bfloat16 and rt.stats["used"] == 1
     sd = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), attn_mask=mask)
     assert O.psnr(out.float().cpu().numpy(), sd.cpu().numpy()) > 35.0
     again = rt.attention(q, k, v, attn_mask=mask)               # cached permutation, same result
