@@ -33,6 +33,7 @@
 // VCATTN_V_MMA_ORDER).  Q, K use the 128-byte swizzle K-major, V MN-major.
 // Every wait is bounded.
 #include <cuda.h>
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 
@@ -48,6 +49,10 @@ namespace {
 
 using namespace tc;
 char g_tc_diag[256];
+// Bounded-wait test hook (vcattn_inject_stall): host-side settings applied
+// to the launches that follow.
+int g_wait_limit_k = kWaitK;
+int g_stall_tile = -1;
 
 constexpr int kBM = 128;
 constexpr int kD = 128;
@@ -87,7 +92,8 @@ struct TcSmem {
   alignas(8) uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  int kvn;   // keys taking part in this CTA's head
+  int kvn;     // keys taking part in this CTA's head
+  int nload;   // KV tiles the producer loads (fewer only under vcattn_inject_stall)
 };
 
 struct TcArgs {
@@ -101,6 +107,8 @@ struct TcArgs {
   void* out;
   int64_t osb, osh, osn;
   const int32_t* kv_len;   // (B,) keys taking part per batch entry, or null (all N)
+  int wait_limit_k;        // bounded-wait limit in units of 1024 SM clocks
+  int stall_tile;          // tests: the producer stops before this KV tile (-1: never)
 };
 
 // ECM: 0 = E4M3 of exp2, 1 = one-FMA ExpCast, 2 = ExpCast in the reference's
@@ -125,6 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // valid_len, padding sorted to the tail by grouping.py:181-183); only the
     // tiles holding keys below kvn are visited.
     sm.kvn = a.kv_len ? min(a.N, max(1, a.kv_len[g / a.H])) : a.N;
+    const int tiles = (sm.kvn + BR - 1) / BR;
+    sm.nload = a.stall_tile >= 0 ? min(tiles, a.stall_tile) : tiles;
 
     sm.abort = 0;
     mbar_init(&sm.q_full, 1);
@@ -174,9 +184,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_expect_tx(&sm.q_full, kBM * 128);
       tma_load_2d(sm.q, &tm_q, 0, g * a.n_pad + row0, &sm.q_full);
       const uint32_t tile_bytes = 2u * BR * 128u + BR * 4u + 2u * kD * 4u;
-      for (int j = 0; j < VC_TILES_VISITED; ++j) {
+      // (under vcattn_inject_stall the copies of tile nload on never come,
+      // and the waits on them time out)
+      for (int j = 0; j < sm.nload; ++j) {
         const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, status, 1)) break;
+        if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, status, 1, a.wait_limit_k)) break;
         mbar_expect_tx(&sm.kv_full[s], tile_bytes);
         const int krow = g * a.n_pad + j * BR;
         tma_load_2d(sm.k[s], &tm_k, 0, krow, &sm.kv_full[s]);
@@ -191,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*abort) {
         for (int j = max(0, issued - kStages); j < issued; ++j) {
           const long long t0 = clock64();
-          while (!mbar_try_wait(&sm.kv_full[j % kStages], (j / kStages) & 1) && clock64() - t0 < kWaitCycles / 4) {
+          while (!mbar_try_wait(&sm.kv_full[j % kStages], (j / kStages) & 1) && clock64() - t0 < (static_cast<long long>(a.wait_limit_k) << 8)) {
           }
         }
       }
@@ -206,13 +218,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_r = idesc_e4m3(kBM, 16, false);
       const uint32_t q_addr = smem_u32(sm.q);
       const uint32_t ones_addr = smem_u32(sm.ones);
-      bool ok = mbar_wait(&sm.q_full, 0, abort, status, 2);
+      bool ok = mbar_wait(&sm.q_full, 0, abort, status, 2, a.wait_limit_k);
       for (int j = 0; ok && j <= VC_TILES_VISITED; ++j) {
         if (j < VC_TILES_VISITED) {
           // S_b was last read as P by PV_{j-2}, issued earlier by this thread
           // (tcgen05.mma from one thread run in order), after p_full(j-2).
           const int s = j % kStages, b = j & 1;
-          ok = mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 3);
+          ok = mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 3, a.wait_limit_k);
           if (!ok) break;
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sm.k[s]);
@@ -226,8 +238,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int i = j - 1, bi = i & 1, si = i % kStages;
           // T_bi last held T_{i-2} and R_{i-1}; R_i goes over the first
           // quarter of T_{i-1}: all three read once tile i-1 is released.
-          ok = i >= 1 ? mbar_wait2(&sm.p_full[bi], (i >> 1) & 1, &sm.t_rel, (i - 1) & 1, abort, status, 5)
-                      : mbar_wait(&sm.p_full[bi], (i >> 1) & 1, abort, status, 5);
+          ok = i >= 1 ? mbar_wait2(&sm.p_full[bi], (i >> 1) & 1, &sm.t_rel, (i - 1) & 1, abort, status, 5, a.wait_limit_k)
+                      : mbar_wait(&sm.p_full[bi], (i >> 1) & 1, abort, status, 5, a.wait_limit_k);
           if (!ok) break;
           tc_fence_after();
           const uint32_t v_addr = smem_u32(sm.v[si]);
@@ -246,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Every MMA issued must finish before TMEM is released.
       tc_commit_if(&sm.drain, leader);
       const long long t0 = clock64();
-      while (!mbar_try_wait(&sm.drain, 0) && clock64() - t0 < kWaitCycles) {
+      while (!mbar_try_wait(&sm.drain, 0) && clock64() - t0 < (static_cast<long long>(a.wait_limit_k) << 10)) {
       }
     }
     __syncwarp();
@@ -255,8 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int c2 = tid - 64;   // 0..63
     for (int j = 0; j < VC_TILES_VISITED; ++j) {
       const int s = j % kStages, ring = j % kRing;
-      if (!mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 13)) break;
-      if (j >= kRing && !mbar_wait(&sm.f_free[ring], ((j / kRing) + 1) & 1, abort, status, 14)) break;
+      if (!mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 13, a.wait_limit_k)) break;
+      if (j >= kRing && !mbar_wait(&sm.f_free[ring], ((j / kRing) + 1) & 1, abort, status, 14, a.wait_limit_k)) break;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = c2 + 64 * h;
@@ -289,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < VC_TILES_VISITED; ++j) {
       const int b = j & 1, ring = j % kRing, s = j % kStages;
       // ks of tile j came with its K/V stage (bulk copy completed on kv_full)
-      if (!mbar_wait2(&sm.s_full[b], (j >> 1) & 1, &sm.kv_full[s], (j / kStages) & 1, abort, status, 7)) break;
+      if (!mbar_wait2(&sm.s_full[b], (j >> 1) & 1, &sm.kv_full[s], (j / kStages) & 1, abort, status, 7, a.wait_limit_k)) break;
       tc_fence_after();
       const uint32_t sb = lane_base + kColS + b * 128;
       float x[BR];
@@ -384,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       warp_arrive(&sm.p_full[b], lane);
-      if (j >= kRing && !mbar_wait(&sm.a_free[ring], ((j / kRing) + 1) & 1, abort, status, 10)) break;
+      if (j >= kRing && !mbar_wait(&sm.a_free[ring], ((j / kRing) + 1) & 1, abort, status, 10, a.wait_limit_k)) break;
       sm.alpha[ring][t] = al;
       warp_arrive(&sm.a_full[ring], lane);
       m = mn;
@@ -404,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int i = 0; i < VC_TILES_VISITED; ++i) {
       const int ring = i % kRing, tb = i & 1;
-      ok = mbar_wait(&sm.t_full[tb], (i >> 1) & 1, abort, status, 11);
+      ok = mbar_wait(&sm.t_full[tb], (i >> 1) & 1, abort, status, 11, a.wait_limit_k);
       if (!ok) break;
       tc_fence_after();
       const uint32_t tcol = kColT + tb * 128;
@@ -418,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence(xb);
       tc_fence_before();
       warp_arrive(&sm.t_rel, lane);   // PV_{i+1} may write T_{(i+1)&1}, R_{i+1} the first quarter of T_i
-      ok = mbar_wait2(&sm.a_full[ring], (i / kRing) & 1, &sm.f_full[ring], (i / kRing) & 1, abort, status, 12);
+      ok = mbar_wait2(&sm.a_full[ring], (i / kRing) & 1, &sm.f_full[ring], (i / kRing) & 1, abort, status, 12, a.wait_limit_k);
       if (!ok) break;
       const float al = sm.alpha[ring][r];
       warp_arrive(&sm.a_free[ring], lane);
@@ -533,6 +545,8 @@ cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
   a.c120 = static_cast<float>(64.0 + 56.0 + p.beta);
   a.out = p.out; a.osb = p.osb; a.osh = p.osh; a.osn = p.osn;
   a.kv_len = p.kv_len;
+  a.wait_limit_k = g_wait_limit_k;
+  a.stall_tile = g_stall_tile;
   const size_t smem = sizeof(TcSmem<BR>) + 1024;
   auto k = attn_tc_kernel<BR, EC, ODT>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -575,6 +589,12 @@ cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t st) {
 }
 
 const char* attn_tc_diag() { return g_tc_diag; }
+
+void set_attn_tc_stall(int tile, long long wait_cycles) {
+  g_stall_tile = tile;
+  g_wait_limit_k = wait_cycles > 0 ? static_cast<int>(std::min<long long>(wait_cycles, tc::kWaitCycles) >> 10) + 1
+                                   : tc::kWaitK;
+}
 
 cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset) {
   tc::DevStatus s{};

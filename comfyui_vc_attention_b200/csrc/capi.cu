@@ -185,6 +185,11 @@ void vcattn_inject_fault(const char* entry_point) {
   g_inject = entry_point ? entry_point : "";
 }
 
+void vcattn_inject_stall(int tile, long long wait_cycles) {
+  std::lock_guard<std::mutex> lk(g_inject_mu);
+  set_attn_tc_stall(tile, wait_cycles);
+}
+
 size_t vcattn_kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys) {
   if (G <= 0 || N <= 0 || D <= 0 || k <= 0) return 0;
   return kmeans_workspace_bytes(G, N, D, k, nkeys);

@@ -98,6 +98,15 @@ VCATTN_API const char* vcattn_last_error(void);
  * named entry point (e.g. "vcattn_attn_fp8") returns VCATTN_ERR_INJECTED
  * without launching anything.  NULL or "" clears it. */
 VCATTN_API void vcattn_inject_fault(const char* entry_point);
+/* Bounded-wait test hook (no counterpart in the reference).  While set
+ * (tile >= 0), the dense tcgen05 kernel of vcattn_attn_fp8 and
+ * vcattn_attn_fp8_masked issues no copies from KV tile `tile` on, so the
+ * waits on that tile find nothing to wait for: each gives up after
+ * wait_cycles SM clocks (the kernel's default, about 2 s, when <= 0), the CTA
+ * drains its copies and MMAs, frees its tensor memory and returns, and
+ * vcattn_attn_status() reports code 1 and the wait that gave up.  No fault,
+ * trap or unbounded wait is involved.  tile = -1 restores normal launches. */
+VCATTN_API void vcattn_inject_stall(int tile, long long wait_cycles);
 
 /* ---- V-Smooth grouping: grouping.py:127-147 (kmeans) + :150-186
  *      (build_permutation) ------------------------------------------------
