@@ -27,7 +27,7 @@ import torch
 
 from .device import detect_profile, is_supported, resolve_backend
 from .grouping import GroupingConfig, build_permutation
-from .schedule import GroupSchedule, PermutationCache, StepTracker
+from .schedule import GroupSchedule, PermutationCache, StepTracker, TauSchedule
 
 __all__ = [
     "VCAttentionConfig", "VCAttentionRuntime", "get_runtime", "install", "uninstall",
@@ -63,6 +63,10 @@ class VCAttentionConfig:
     smooth_k: bool = True
     enable_sparsity: bool = True
     tau: float = 1.3
+    # (this build) tau across denoising steps: (tau_start, tau_end, dense_steps)
+    # runs the first dense_steps dense, then moves tau linearly from tau_start
+    # to tau_end (PLAN_sparse_fusion.md:115-118); None keeps `tau` every step.
+    tau_schedule: Optional[tuple] = None
     sparsity_min_tokens: int = 8192
     sink_tokens: int = 512
     local_blocks: int = 1
@@ -89,6 +93,7 @@ class VCAttentionRuntime:
                                       total_steps_hint=self.config.total_steps_hint,
                                       min_tokens=self.config.min_tokens)
         self.tracker = StepTracker(total_steps_hint=self.config.total_steps_hint)
+        self.tau_schedule = TauSchedule(*self.config.tau_schedule) if self.config.tau_schedule else None
         self.cache = PermutationCache()
         self._mask_cache: Dict[tuple, tuple] = {}
         self.tags: Optional[torch.Tensor] = None
@@ -165,17 +170,31 @@ class VCAttentionRuntime:
             self.stats["grouped"] += 1
         self.stats["used"] += 1
         from .kernels.cuda_attn import TritonConfig, vc_attention_triton
+        sparse, tau = self.sparsity(n)
         tcfg = TritonConfig(
             block_m=cfg.block_m,
             block_n=cfg.block_rows,
             enable_expcast=bool(cfg.enable_expcast and self.backend == "fp8"),
             qk_fp4=(self.backend == "nvfp4"),
-            sparse=bool(cfg.enable_sparsity and n >= cfg.sparsity_min_tokens),
-            tau=cfg.tau,
+            sparse=sparse,
+            tau=tau,
             local_blocks=cfg.local_blocks,
             sink_blocks=max(0, int(cfg.sink_tokens) // max(1, cfg.block_rows)),
         )
         return vc_attention_triton(q, k, v, perm=perm, cfg=tcfg, scale=scale)
+
+    def sparsity(self, n: int):
+        """(sparse, tau) for a call of n tokens at the current step."""
+        cfg = self.config
+        sparse = bool(cfg.enable_sparsity and n >= cfg.sparsity_min_tokens)
+        tau = cfg.tau
+        if sparse and self.tau_schedule is not None:
+            t = self.tau_schedule.tau(self.tracker.current, self.tracker.total_steps or cfg.total_steps_hint)
+            if t is None:
+                sparse = False
+            else:
+                tau = t
+        return sparse, tau
 
     def _masked_attention(self, q, k, v, keep: torch.Tensor, mask_key: torch.Tensor,
                           scale: Optional[float]) -> torch.Tensor:

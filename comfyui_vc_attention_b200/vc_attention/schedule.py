@@ -15,7 +15,7 @@ from collections import OrderedDict
 from dataclasses import dataclass, field
 from typing import Optional, Tuple
 
-__all__ = ["GroupSchedule", "StepTracker", "PermutationCache"]
+__all__ = ["GroupSchedule", "StepTracker", "PermutationCache", "TauSchedule"]
 
 
 @dataclass
@@ -106,3 +106,28 @@ class PermutationCache:
 
     def __len__(self) -> int:
         return len(self._store)
+
+
+@dataclass
+class TauSchedule:
+    """The sparsity threshold across denoising steps: the schedule Sol-Attn
+    uses, which the reference plans but does not build
+    (PLAN_sparse_fusion.md:115-118): the first ``dense_steps`` steps run
+    dense, then tau falls linearly from ``tau_start`` at the first sparse step
+    to ``tau_end`` at the last step (a larger tau keeps fewer blocks)."""
+
+    tau_start: float = 1.0
+    tau_end: float = 2.0
+    dense_steps: int = 0
+
+    def tau(self, step_index: int, total_steps: Optional[int]) -> Optional[float]:
+        """tau for this step, or None for a dense step."""
+        if step_index < self.dense_steps:
+            return None
+        total = max(total_steps or 0, step_index + 1)
+        span = total - 1 - self.dense_steps
+        if span <= 0:
+            return float(self.tau_end)
+        t = min(1.0, (step_index - self.dense_steps) / span)
+        return float(self.tau_start + (self.tau_end - self.tau_start) * t)
+

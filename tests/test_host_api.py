@@ -224,3 +224,24 @@ def test_key_padding_mask_forms():
     assert key_padding_mask(torch.ones(b, 3, 1, n, dtype=torch.bool), b, n) is None   # varies by head
     assert key_padding_mask(torch.ones(b, 1, 1, n + 1, dtype=torch.bool), b, n) is None
     assert key_padding_mask(torch.ones(b, n, dtype=torch.int32), b, n) is None
+
+
+def test_tau_schedule_across_steps():
+    """Dense for the first steps, then tau moving linearly to its end value;
+    the runtime hands each step's (sparse, tau) to the kernel config."""
+    from comfyui_vc_attention_b200.vc_attention.schedule import TauSchedule
+    ts = TauSchedule(tau_start=1.0, tau_end=2.0, dense_steps=2)
+    assert ts.tau(0, 8) is None and ts.tau(1, 8) is None
+    assert ts.tau(2, 8) == 1.0 and ts.tau(7, 8) == 2.0
+    assert abs(ts.tau(5, 8) - 1.6) < 1e-12
+    assert ts.tau(9, 8) == 2.0                      # past the announced total: stays at the end
+    rt = VCAttentionRuntime(VCAttentionConfig(tau_schedule=(1.0, 2.0, 2), total_steps_hint=8))
+    got = []
+    for _ in range(8):
+        rt.begin_step()
+        got.append(rt.sparsity(16384))
+    assert got[0] == (False, 1.3) and got[1] == (False, 1.3)
+    assert got[2] == (True, 1.0) and got[7] == (True, 2.0)
+    assert rt.sparsity(1024)[0] is False            # below sparsity_min_tokens: always dense
+    plain = VCAttentionRuntime(VCAttentionConfig())
+    assert plain.sparsity(16384) == (True, 1.3)
