@@ -61,6 +61,9 @@ WORKLOADS = {
     "c1nv": dict(desc="NVFP4 QK^T + FP8 PV at the configs[1] shape: B1 H56 N16384 D128, ExpCast on, V-Smooth k=64",
                  B=1, H=56, N=16384, D=128, expcast=True, sparse=False, k=64, block_rows=128, spatial=None,
                  qk_fp4=True),
+    "c1d64": dict(desc="head dim 64 at the configs[1] width: dense FP8 VC-Attention, B1 H112 N16384 D64, ExpCast on, "
+                       "V-Smooth k=64", B=1, H=112, N=16384, D=64, expcast=True, sparse=False, k=64, block_rows=128,
+                  spatial=None),
     "c1nvh16": dict(desc="profiling slice of the NVFP4 QK^T path at the configs[1] shape: B1 H16 N16384 D128",
                     B=1, H=16, N=16384, D=128, expcast=True, sparse=False, k=64, block_rows=128, spatial=None,
                     qk_fp4=True),

@@ -30,10 +30,10 @@
 // least one MMA back, so the in-order tensor pipe never drains while a
 // handshake completes.
 // P is in key order, so V rows are read in token order (prepared without
-// VCATTN_V_MMA_ORDER).  Q, K use the 128-byte swizzle K-major, V MN-major.
+// VCATTN_V_MMA_ORDER).  Q, K K-major, V MN-major, in the 128-byte swizzle for
+// head dim 128 and the 64-byte swizzle for head dim 64.
 // Every wait is bounded.
 #include <cuda.h>
-#include <algorithm>
 #include <cstdio>
 #include <mutex>
 
@@ -49,13 +49,11 @@ namespace {
 
 using namespace tc;
 char g_tc_diag[256];
-// Bounded-wait test hook (vcattn_inject_stall): host-side settings applied
-// to the launches that follow.
-int g_wait_limit_k = kWaitK;
+// Bounded-wait test hook (vcattn_inject_stall): the producer stops before
+// this KV tile in the launches that follow (-1: never).
 int g_stall_tile = -1;
 
 constexpr int kBM = 128;
-constexpr int kD = 128;
 constexpr int kStages = 4;
 constexpr int kRing = 4;        // per-tile factor / alpha hand-off depth
 constexpr int kThreads = 384;   // 12 warps = 3 warpgroups
@@ -64,17 +62,19 @@ constexpr uint32_t kColS = 0, kColT = 256;
 // reads are contiguous, groups 36 floats apart so their float4 reads fall
 // in different banks.
 
-template <int BR>
+// D = 128: Q, K, V rows of 128 bytes in the 128-byte swizzle; D = 64: rows
+// of 64 bytes in the 64-byte swizzle (8-row atoms of 512 bytes).
+template <int BR, int D>
 struct TcSmem {
   // q, k and v are contiguous: after the last tile they stage the output.
-  alignas(1024) uint8_t q[kBM * 128];
-  alignas(1024) uint8_t k[kStages][BR * 128];
-  alignas(1024) uint8_t v[kStages][BR * 128];
+  alignas(1024) uint8_t q[kBM * D];
+  alignas(1024) uint8_t k[kStages][BR * D];
+  alignas(1024) uint8_t v[kStages][BR * D];
   alignas(1024) uint8_t ones[16 * 128];
   alignas(16) float ks[kStages][BR];
-  alignas(16) float vs[kStages][kD];
-  alignas(16) float mu[kStages][kD];
-  alignas(16) float cm[kRing][2][kD];            // vs / 448 and mu * vs per channel
+  alignas(16) float vs[kStages][D];
+  alignas(16) float mu[kStages][D];
+  alignas(16) float cm[kRing][2][D];             // vs / 448 and mu * vs per channel
   alignas(16) float alpha[kRing][kBM];            // per query row
   alignas(8) uint64_t q_full;
   alignas(8) uint64_t kv_full[kStages];
@@ -107,20 +107,28 @@ struct TcArgs {
   void* out;
   int64_t osb, osh, osn;
   const int32_t* kv_len;   // (B,) keys taking part per batch entry, or null (all N)
-  int wait_limit_k;        // bounded-wait limit in units of 1024 SM clocks
   int stall_tile;          // tests: the producer stops before this KV tile (-1: never)
 };
 
 // ECM: 0 = E4M3 of exp2, 1 = one-FMA ExpCast, 2 = ExpCast in the reference's
 // operation order on s = (S * (qs * ks)) * sm_scale (parity runs).
-template <int BR, int ECM, int ODT>
+template <int D>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t saddr) {
+  // the same descriptor serves K-major Q/K and MN-major V (the instruction
+  // descriptor carries the major-ness): one swizzle atom across the row
+  if constexpr (D == 128) return desc_kmajor(saddr);
+  else return desc_kmajor64(saddr);
+}
+
+template <int BR, int D, int ECM, int ODT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
   constexpr int NCH = BR / 32;   // 32-key chunks per tile
+  constexpr int kD = D;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  TcSmem<BR>& sm = *reinterpret_cast<TcSmem<BR>*>(smem_raw + pad);
+  TcSmem<BR, D>& sm = *reinterpret_cast<TcSmem<BR, D>*>(smem_raw + pad);
   DevStatus* status = &g_attn_tc_status;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -181,14 +189,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
-      mbar_expect_tx(&sm.q_full, kBM * 128);
+      mbar_expect_tx(&sm.q_full, kBM * kD);
       tma_load_2d(sm.q, &tm_q, 0, g * a.n_pad + row0, &sm.q_full);
-      const uint32_t tile_bytes = 2u * BR * 128u + BR * 4u + 2u * kD * 4u;
+      const uint32_t tile_bytes = 2u * BR * kD + BR * 4u + 2u * kD * 4u;
       // (under vcattn_inject_stall the copies of tile nload on never come,
       // and the waits on them time out)
       for (int j = 0; j < sm.nload; ++j) {
         const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, status, 1, a.wait_limit_k)) break;
+        if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, status, 1)) break;
         mbar_expect_tx(&sm.kv_full[s], tile_bytes);
         const int krow = g * a.n_pad + j * BR;
         tma_load_2d(sm.k[s], &tm_k, 0, krow, &sm.kv_full[s]);
@@ -203,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*abort) {
         for (int j = max(0, issued - kStages); j < issued; ++j) {
           const long long t0 = clock64();
-          while (!mbar_try_wait(&sm.kv_full[j % kStages], (j / kStages) & 1) && clock64() - t0 < (static_cast<long long>(a.wait_limit_k) << 8)) {
+          while (!mbar_try_wait(&sm.kv_full[j % kStages], (j / kStages) & 1) && clock64() - t0 < kWaitCycles / 4) {
           }
         }
       }
@@ -218,36 +226,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_r = idesc_e4m3(kBM, 16, false);
       const uint32_t q_addr = smem_u32(sm.q);
       const uint32_t ones_addr = smem_u32(sm.ones);
-      bool ok = mbar_wait(&sm.q_full, 0, abort, status, 2, a.wait_limit_k);
+      bool ok = mbar_wait(&sm.q_full, 0, abort, status, 2);
       for (int j = 0; ok && j <= VC_TILES_VISITED; ++j) {
         if (j < VC_TILES_VISITED) {
           // S_b was last read as P by PV_{j-2}, issued earlier by this thread
           // (tcgen05.mma from one thread run in order), after p_full(j-2).
           const int s = j % kStages, b = j & 1;
-          ok = mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 3, a.wait_limit_k);
+          ok = mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 3);
           if (!ok) break;
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sm.k[s]);
 #pragma unroll
           for (int kk = 0; kk < kD / 32; ++kk)
-            mma_f8_if(tbase + kColS + b * 128, desc_kmajor(q_addr + kk * 32), desc_kmajor(k_addr + kk * 32), id_qk,
-                   kk > 0, leader);
+            mma_f8_if(tbase + kColS + b * 128, operand_desc<D>(q_addr + kk * 32), operand_desc<D>(k_addr + kk * 32),
+                      id_qk, kk > 0, leader);
           tc_commit_if(&sm.s_full[b], leader);
         }
         if (j >= 1) {
           const int i = j - 1, bi = i & 1, si = i % kStages;
           // T_bi last held T_{i-2} and R_{i-1}; R_i goes over the first
           // quarter of T_{i-1}: all three read once tile i-1 is released.
-          ok = i >= 1 ? mbar_wait2(&sm.p_full[bi], (i >> 1) & 1, &sm.t_rel, (i - 1) & 1, abort, status, 5, a.wait_limit_k)
-                      : mbar_wait(&sm.p_full[bi], (i >> 1) & 1, abort, status, 5, a.wait_limit_k);
+          ok = i >= 1 ? mbar_wait2(&sm.p_full[bi], (i >> 1) & 1, &sm.t_rel, (i - 1) & 1, abort, status, 5)
+                      : mbar_wait(&sm.p_full[bi], (i >> 1) & 1, abort, status, 5);
           if (!ok) break;
           tc_fence_after();
           const uint32_t v_addr = smem_u32(sm.v[si]);
           const uint32_t p_t = tbase + kColS + bi * 128;   // A positions [32kk, 32kk+32) at columns 8kk..8kk+7
 #pragma unroll
           for (int kk = 0; kk < BR / 32; ++kk)
-            mma_f8_ts_if(tbase + kColT + bi * 128, p_t + 8 * kk, desc_mnmajor(v_addr + kk * 32 * 128), id_pv,
-                      kk > 0, leader);
+            mma_f8_ts_if(tbase + kColT + bi * 128, p_t + 8 * kk, operand_desc<D>(v_addr + kk * 32 * kD), id_pv,
+                         kk > 0, leader);
 #pragma unroll
           for (int kk = 0; kk < BR / 32; ++kk)
             mma_f8_ts_if(tbase + kColT + (bi ^ 1) * 128, p_t + 8 * kk, desc_kmajor(ones_addr + kk * 32), id_r, kk > 0, leader);
@@ -258,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Every MMA issued must finish before TMEM is released.
       tc_commit_if(&sm.drain, leader);
       const long long t0 = clock64();
-      while (!mbar_try_wait(&sm.drain, 0) && clock64() - t0 < (static_cast<long long>(a.wait_limit_k) << 10)) {
+      while (!mbar_try_wait(&sm.drain, 0) && clock64() - t0 < kWaitCycles) {
       }
     }
     __syncwarp();
@@ -267,10 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int c2 = tid - 64;   // 0..63
     for (int j = 0; j < VC_TILES_VISITED; ++j) {
       const int s = j % kStages, ring = j % kRing;
-      if (!mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 13, a.wait_limit_k)) break;
-      if (j >= kRing && !mbar_wait(&sm.f_free[ring], ((j / kRing) + 1) & 1, abort, status, 14, a.wait_limit_k)) break;
+      if (!mbar_wait(&sm.kv_full[s], (j / kStages) & 1, abort, status, 13)) break;
+      if (j >= kRing && !mbar_wait(&sm.f_free[ring], ((j / kRing) + 1) & 1, abort, status, 14)) break;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < kD / 64; ++h) {
         const int c = c2 + 64 * h;
         const float vsc = sm.vs[s][c];
         sm.cm[ring][0][c] = __fdiv_rn(vsc, 448.0f);
@@ -301,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < VC_TILES_VISITED; ++j) {
       const int b = j & 1, ring = j % kRing, s = j % kStages;
       // ks of tile j came with its K/V stage (bulk copy completed on kv_full)
-      if (!mbar_wait2(&sm.s_full[b], (j >> 1) & 1, &sm.kv_full[s], (j / kStages) & 1, abort, status, 7, a.wait_limit_k)) break;
+      if (!mbar_wait2(&sm.s_full[b], (j >> 1) & 1, &sm.kv_full[s], (j / kStages) & 1, abort, status, 7)) break;
       tc_fence_after();
       const uint32_t sb = lane_base + kColS + b * 128;
       float x[BR];
@@ -396,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       warp_arrive(&sm.p_full[b], lane);
-      if (j >= kRing && !mbar_wait(&sm.a_free[ring], ((j / kRing) + 1) & 1, abort, status, 10, a.wait_limit_k)) break;
+      if (j >= kRing && !mbar_wait(&sm.a_free[ring], ((j / kRing) + 1) & 1, abort, status, 10)) break;
       sm.alpha[ring][t] = al;
       warp_arrive(&sm.a_full[ring], lane);
       m = mn;
@@ -404,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 248;\n" ::: "memory");
     // ------------------------------------------------------------ correction
-    // Thread = query row r = 32 (w%4) + lane (TMEM lane r), O[128] in
+    // Thread = query row r = 32 (w%4) + lane (TMEM lane r), O[D] in
     // registers; T read with the 32x32b shape, 64 columns per load batch.
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
@@ -416,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int i = 0; i < VC_TILES_VISITED; ++i) {
       const int ring = i % kRing, tb = i & 1;
-      ok = mbar_wait(&sm.t_full[tb], (i >> 1) & 1, abort, status, 11, a.wait_limit_k);
+      ok = mbar_wait(&sm.t_full[tb], (i >> 1) & 1, abort, status, 11);
       if (!ok) break;
       tc_fence_after();
       const uint32_t tcol = kColT + tb * 128;
@@ -430,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence(xb);
       tc_fence_before();
       warp_arrive(&sm.t_rel, lane);   // PV_{i+1} may write T_{(i+1)&1}, R_{i+1} the first quarter of T_i
-      ok = mbar_wait2(&sm.a_full[ring], (i / kRing) & 1, &sm.f_full[ring], (i / kRing) & 1, abort, status, 12, a.wait_limit_k);
+      ok = mbar_wait2(&sm.a_full[ring], (i / kRing) & 1, &sm.f_full[ring], (i / kRing) & 1, abort, status, 12);
       if (!ok) break;
       const float al = sm.alpha[ring][r];
       warp_arrive(&sm.a_free[ring], lane);
@@ -439,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float4* f4 = reinterpret_cast<const float4*>(sm.cm[ring][0]);
       const float4* g4 = reinterpret_cast<const float4*>(sm.cm[ring][1]);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int half = 0; half < kD / 64; ++half) {
         if (half == 1) {
           tmem_ld32(lb + tcol + 64, xa);
           tmem_ld32(lb + tcol + 96, xb);
@@ -471,8 +479,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // whole 16-byte row chunks.
       constexpr int ES = (ODT == VCATTN_DTYPE_F32) ? 4 : 2;
       constexpr int RS = kD * ES + 16;
-      static_assert(kBM * RS <= static_cast<int>(sizeof(TcSmem<BR>::q) + sizeof(TcSmem<BR>::k) +
-                                                 sizeof(TcSmem<BR>::v)),
+      static_assert(kBM * RS <= static_cast<int>(sizeof(TcSmem<BR, D>::q) + sizeof(TcSmem<BR, D>::k) +
+                                                 sizeof(TcSmem<BR, D>::v)),
                     "output staging must fit in the operand buffers");
       uint8_t* stage = sm.q + wq * 32 * RS;
 #pragma unroll
@@ -519,24 +527,26 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D map over (rows, 128 bytes) with a (box_rows x 128) box and 128-byte swizzle.
-bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows) {
+// 2-D map over (rows, D bytes) with a (box_rows x D) box: the 128-byte
+// swizzle for D = 128, the 64-byte swizzle for D = 64.
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows, int D) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[2] = {128, rows};
-  cuuint64_t strides[1] = {128};
-  cuuint32_t box[2] = {128, box_rows};
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), rows};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(D), box_rows};
   cuuint32_t es[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_INTERLEAVE_NONE, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BR, int EC, int ODT>
+template <int BR, int D, int EC, int ODT>
 cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   const uint64_t rows = static_cast<uint64_t>(p.B) * p.H * p.n_pad;
-  if (!make_map(&mq, p.q8, rows, kBM) || !make_map(&mk, p.k8, rows, BR) || !make_map(&mv, p.v8, rows, BR))
+  if (!make_map(&mq, p.q8, rows, kBM, D) || !make_map(&mk, p.k8, rows, BR, D) ||
+      !make_map(&mv, p.v8, rows, BR, D))
     return cudaErrorInvalidValue;
   TcArgs a{};
   a.q_scale = p.q_scale; a.k_scale = p.k_scale; a.v_scale = p.v_scale; a.mu = p.mu;
@@ -545,10 +555,9 @@ cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
   a.c120 = static_cast<float>(64.0 + 56.0 + p.beta);
   a.out = p.out; a.osb = p.osb; a.osh = p.osh; a.osn = p.osn;
   a.kv_len = p.kv_len;
-  a.wait_limit_k = g_wait_limit_k;
   a.stall_tile = g_stall_tile;
-  const size_t smem = sizeof(TcSmem<BR>) + 1024;
-  auto k = attn_tc_kernel<BR, EC, ODT>;
+  const size_t smem = sizeof(TcSmem<BR, D>) + 1024;
+  auto k = attn_tc_kernel<BR, D, EC, ODT>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const dim3 grid((p.n_pad + kBM - 1) / kBM, p.B * p.H);
@@ -565,36 +574,36 @@ cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
   return e;
 }
 
-template <int BR>
+template <int BR, int D>
 cudaError_t dispatch_tc(const AttnParams& p, cudaStream_t st) {
   const int ec = (p.flags & VCATTN_EXPCAST) ? ((p.flags & VCATTN_EXPCAST_EXACT) ? 2 : 1) : 0;
   switch (p.out_dtype) {
     case VCATTN_DTYPE_BF16:
-      return ec == 1 ? launch_tc<BR, 1, VCATTN_DTYPE_BF16>(p, st)
-                     : ec == 2 ? launch_tc<BR, 2, VCATTN_DTYPE_BF16>(p, st) : launch_tc<BR, 0, VCATTN_DTYPE_BF16>(p, st);
+      return ec == 1 ? launch_tc<BR, D, 1, VCATTN_DTYPE_BF16>(p, st)
+                     : ec == 2 ? launch_tc<BR, D, 2, VCATTN_DTYPE_BF16>(p, st)
+                               : launch_tc<BR, D, 0, VCATTN_DTYPE_BF16>(p, st);
     case VCATTN_DTYPE_F16:
-      return ec == 1 ? launch_tc<BR, 1, VCATTN_DTYPE_F16>(p, st)
-                     : ec == 2 ? launch_tc<BR, 2, VCATTN_DTYPE_F16>(p, st) : launch_tc<BR, 0, VCATTN_DTYPE_F16>(p, st);
+      return ec == 1 ? launch_tc<BR, D, 1, VCATTN_DTYPE_F16>(p, st)
+                     : ec == 2 ? launch_tc<BR, D, 2, VCATTN_DTYPE_F16>(p, st)
+                               : launch_tc<BR, D, 0, VCATTN_DTYPE_F16>(p, st);
     default:
-      return ec == 1 ? launch_tc<BR, 1, VCATTN_DTYPE_F32>(p, st)
-                     : ec == 2 ? launch_tc<BR, 2, VCATTN_DTYPE_F32>(p, st) : launch_tc<BR, 0, VCATTN_DTYPE_F32>(p, st);
+      return ec == 1 ? launch_tc<BR, D, 1, VCATTN_DTYPE_F32>(p, st)
+                     : ec == 2 ? launch_tc<BR, D, 2, VCATTN_DTYPE_F32>(p, st)
+                               : launch_tc<BR, D, 0, VCATTN_DTYPE_F32>(p, st);
   }
 }
 
 }  // namespace
 
 cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t st) {
-  if (p.D != 128) return cudaErrorNotSupported;
-  return p.block_rows == 128 ? dispatch_tc<128>(p, st) : dispatch_tc<64>(p, st);
+  if (p.D == 128) return p.block_rows == 128 ? dispatch_tc<128, 128>(p, st) : dispatch_tc<64, 128>(p, st);
+  if (p.D == 64) return p.block_rows == 128 ? dispatch_tc<128, 64>(p, st) : dispatch_tc<64, 64>(p, st);
+  return cudaErrorNotSupported;
 }
 
 const char* attn_tc_diag() { return g_tc_diag; }
 
-void set_attn_tc_stall(int tile, long long wait_cycles) {
-  g_stall_tile = tile;
-  g_wait_limit_k = wait_cycles > 0 ? static_cast<int>(std::min<long long>(wait_cycles, tc::kWaitCycles) >> 10) + 1
-                                   : tc::kWaitK;
-}
+void set_attn_tc_stall(int tile) { g_stall_tile = tile; }
 
 cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset) {
   tc::DevStatus s{};

@@ -185,9 +185,9 @@ void vcattn_inject_fault(const char* entry_point) {
   g_inject = entry_point ? entry_point : "";
 }
 
-void vcattn_inject_stall(int tile, long long wait_cycles) {
+void vcattn_inject_stall(int tile) {
   std::lock_guard<std::mutex> lk(g_inject_mu);
-  set_attn_tc_stall(tile, wait_cycles);
+  set_attn_tc_stall(tile);
 }
 
 size_t vcattn_kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys) {
@@ -337,7 +337,6 @@ int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8, 
   const int rc = attn_common_checks("vcattn_attn_fp8", q8, q_scale, k8, k_scale, v8, v_scale, mu, B, H, N, n_pad,
                                     D, block_rows, out, out_dtype);
   if (rc != VCATTN_OK) return rc;
-  VC_CHECK(D == 128, "vcattn_attn_fp8: the tcgen05 kernel needs D = 128 (use vcattn_attn_fp8_mma for D = 64)");
   VC_CHECK(aligned16(out) && (out_sn % 8) == 0 && (out_sh % 8) == 0 && (out_sb % 8) == 0,
            "vcattn_attn_fp8: out must be 16-byte aligned with 8-element multiple strides");
   AttnParams p{};
@@ -362,7 +361,6 @@ int vcattn_attn_fp8_masked(const uint8_t* q8, const float* q_scale, const uint8_
                                     n_pad, D, block_rows, out, out_dtype);
   if (rc != VCATTN_OK) return rc;
   VC_CHECK(kv_len != nullptr, "vcattn_attn_fp8_masked: null kv_len");
-  VC_CHECK(D == 128, "vcattn_attn_fp8_masked: needs D = 128 (the tcgen05 kernel)");
   VC_CHECK(aligned16(out) && (out_sn % 8) == 0 && (out_sh % 8) == 0 && (out_sb % 8) == 0,
            "vcattn_attn_fp8_masked: out must be 16-byte aligned with 8-element multiple strides");
   AttnParams p{};

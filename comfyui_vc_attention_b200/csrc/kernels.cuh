@@ -96,7 +96,7 @@ const char* attn_nvfp4_diag();
 cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset);
 const char* attn_tc_diag();
 // Bounded-wait test hook of the dense tcgen05 kernel (vcattn_inject_stall).
-void set_attn_tc_stall(int tile, long long wait_cycles);
+void set_attn_tc_stall(int tile);
 cudaError_t launch_attn_sparse_mma(const AttnParams& p, cudaStream_t st);
 bool attn_sparse_tc_supported(const AttnParams& p);
 cudaError_t launch_attn_sparse_tc(const AttnParams& p, cudaStream_t st);

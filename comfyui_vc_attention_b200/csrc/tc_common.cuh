@@ -57,18 +57,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait.  `abort` is a CTA-shared word: once any thread gives up,
 // every other waiter stops too.  Returns false when the wait was abandoned.
-// `limit_k` (units of 1024 SM clocks) defaults to kWaitCycles; tests pass a
-// short one.
-constexpr int kWaitK = static_cast<int>(kWaitCycles >> 10);
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          DevStatus* status, int where, int limit_k = kWaitK) {
-  const long long limit = static_cast<long long>(limit_k) << 10;
+                                          DevStatus* status, int where) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > limit) {
+    if (clock64() - t0 > kWaitCycles) {
       *abort = 1;
       if (status != nullptr && atomicCAS(&status->code, 0, 1) == 0) {
         status->where = where;
@@ -82,8 +78,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Bounded wait on two barriers at once: both probes are in flight together,
 // so an already-complete pair costs one shared-memory round trip.
 __device__ __forceinline__ bool mbar_wait2(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb, volatile int* abort,
-                                           DevStatus* status, int where, int limit_k = kWaitK) {
-  const long long limit = static_cast<long long>(limit_k) << 10;
+                                           DevStatus* status, int where) {
   bool da = mbar_try_wait(a, pa);
   bool db = mbar_try_wait(b, pb);
   if (da && db) return true;
@@ -93,7 +88,7 @@ __device__ __forceinline__ bool mbar_wait2(uint64_t* a, uint32_t pa, uint64_t* b
     if (!db) db = mbar_try_wait(b, pb);
     if (da && db) return true;
     if (*abort) return false;
-    if (clock64() - t0 > limit) {
+    if (clock64() - t0 > kWaitCycles) {
       *abort = 1;
       if (status != nullptr && atomicCAS(&status->code, 0, 1) == 0) {
         status->where = where;

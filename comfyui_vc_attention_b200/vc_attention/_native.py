@@ -65,7 +65,7 @@ _SIGNATURES = {
     "vcattn_abi_version": (c_int, []),
     "vcattn_last_error": (c_char_p, []),
     "vcattn_inject_fault": (None, [c_char_p]),
-    "vcattn_inject_stall": (None, [c_int, c_int64]),
+    "vcattn_inject_stall": (None, [c_int]),
     "vcattn_kmeans_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "vcattn_kmeans": (c_int, [POINTER(BHND), c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                               c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
@@ -172,11 +172,11 @@ def inject_fault(entry_point: Optional[str]) -> None:
     lib().vcattn_inject_fault(entry_point.encode() if entry_point else None)
 
 
-def inject_stall(tile: int, wait_cycles: int = 0) -> None:
+def inject_stall(tile: int) -> None:
     """Bounded-wait test hook: the dense tcgen05 kernel issues no copies from
-    KV tile ``tile`` on, so the waits on it give up after ``wait_cycles`` SM
-    clocks and report through vcattn_attn_status; ``tile=-1`` clears it."""
-    lib().vcattn_inject_stall(int(tile), int(wait_cycles))
+    KV tile ``tile`` on, so the waits on it give up (after about 2 s) and
+    report through vcattn_attn_status; ``tile=-1`` clears it."""
+    lib().vcattn_inject_stall(int(tile))
 
 
 def declared_symbols(header: str = HEADER_PATH):

@@ -301,7 +301,7 @@ def vc_attention_cuda(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     kv_len: None, or a (B,) int32 CUDA tensor: in batch entry b only the
     first kv_len[b] keys of the permuted order take part (key padding,
     reference.py ``valid_len``); the permutation must have sorted the
-    excluded keys to the tail.  Dense FP8, D = 128 only.
+    excluded keys to the tail.  Dense FP8 only.
     Returns (B, H, N, D) in q.dtype.
     """
     return _attention_into(q, k, v, perm, cfg, scale, None, kv_len)
@@ -327,7 +327,7 @@ def prepare_for(q, k, v, perm, cfg: Optional[TritonConfig] = None, scale: Option
     br = cfg.block_n
     sparse = bool(cfg.sparse)
     fp4 = bool(cfg.qk_fp4)
-    use_tc = d == 128 and (not sparse or sparse_tc_applies(d, br, cfg.block_m, cfg.group, n))
+    use_tc = (not sparse) or sparse_tc_applies(d, br, cfg.block_m, cfg.group, n)
     return prepare(q, k, v, perm, block_rows=br, hadamard=True, smooth_k=True, sparse=sparse,
                    tau=cfg.tau, q_block=cfg.block_m, scale=scale, want_v=use_tc, want_v_t=not use_tc,
                    local_blocks=cfg.local_blocks, sink_blocks=cfg.sink_blocks, qk_fp4=fp4, fp8_qk=not fp4)
@@ -374,7 +374,7 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
                        kv_len: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Run the attention kernel on prepared operands, writing into ``out``.
 
-    kernel: "tc" (tcgen05, D = 128, needs ``p.v``), "mma" (register MMA,
+    kernel: "tc" (tcgen05, needs ``p.v``), "mma" (register MMA,
     needs ``p.v_t``) or "auto" (tcgen05 whenever it applies), for the dense
     and the sparse path alike.  ``kv_len`` ((B,) int32 on the device) runs
     the key-padding masked dense tcgen05 kernel (vcattn_attn_fp8_masked).
@@ -387,8 +387,8 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
     odt = _dtype_code(out)
     st = _stream(out)
     if kv_len is not None:
-        if cfg.sparse or cfg.qk_fp4 or d != 128 or p.v is None or p.v_mma_order or kernel not in ("auto", "tc"):
-            raise ValueError("masked attention runs on the dense FP8 tcgen05 kernel (D = 128, token-order V)")
+        if cfg.sparse or cfg.qk_fp4 or p.v is None or p.v_mma_order or kernel not in ("auto", "tc"):
+            raise ValueError("masked attention runs on the dense FP8 tcgen05 kernel (token-order V)")
         kl = kv_len.to(device=out.device, dtype=torch.int32).contiguous()
         if kl.shape != (b,):
             raise ValueError(f"kv_len must be ({b},), got {tuple(kl.shape)}")
@@ -436,7 +436,7 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
             out.stride(0), out.stride(1), out.stride(2), st))
         return out
     if kernel == "auto":
-        kernel = "tc" if (d == 128 and p.v is not None and not p.v_mma_order) else "mma"
+        kernel = "tc" if (p.v is not None and not p.v_mma_order) else "mma"
     if kernel == "tc":
         if p.v is None or p.v_mma_order:
             raise ValueError("the dense tcgen05 kernel reads V codes in token order (want_v=True, v_mma_order=False)")

@@ -160,7 +160,7 @@ class VCAttentionRuntime:
         if attn_mask is not None:
             # Key padding only (the reference defers on any mask, README.md:514-515)
             keep = key_padding_mask(attn_mask, b, n)
-            if keep is None or d != 128:
+            if keep is None:
                 self.stats["skipped"] += 1
                 return None
             self.stats["used"] += 1
@@ -169,8 +169,14 @@ class VCAttentionRuntime:
         if perm is not None:
             self.stats["grouped"] += 1
         self.stats["used"] += 1
-        from .kernels.cuda_attn import TritonConfig, vc_attention_triton
+        from .kernels.cuda_attn import TritonConfig, sparse_tc_applies, vc_attention_triton
         sparse, tau = self.sparsity(n)
+        if sparse and not sparse_tc_applies(d, cfg.block_rows, cfg.block_m, 16, n):
+            # the tcgen05 sparse kernel takes head dim 128, 128-row value
+            # blocks and 64-row query blocks; other shapes run the exact
+            # dense tcgen05 kernel, which is faster than the register-MMA
+            # sparse kernel (10.9 ms vs 6.1 ms at the configs[2] size)
+            sparse = False
         tcfg = TritonConfig(
             block_m=cfg.block_m,
             block_n=cfg.block_rows,

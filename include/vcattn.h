@@ -101,12 +101,12 @@ VCATTN_API void vcattn_inject_fault(const char* entry_point);
 /* Bounded-wait test hook (no counterpart in the reference).  While set
  * (tile >= 0), the dense tcgen05 kernel of vcattn_attn_fp8 and
  * vcattn_attn_fp8_masked issues no copies from KV tile `tile` on, so the
- * waits on that tile find nothing to wait for: each gives up after
- * wait_cycles SM clocks (the kernel's default, about 2 s, when <= 0), the CTA
- * drains its copies and MMAs, frees its tensor memory and returns, and
- * vcattn_attn_status() reports code 1 and the wait that gave up.  No fault,
- * trap or unbounded wait is involved.  tile = -1 restores normal launches. */
-VCATTN_API void vcattn_inject_stall(int tile, long long wait_cycles);
+ * waits on that tile find nothing to wait for: each gives up after its limit
+ * (about 2 s of SM clocks), the CTA drains its copies and MMAs, frees its
+ * tensor memory and returns, and vcattn_attn_status() reports code 1 and the
+ * wait that gave up.  No fault, trap or unbounded wait is involved.
+ * tile = -1 restores normal launches. */
+VCATTN_API void vcattn_inject_stall(int tile);
 
 /* ---- V-Smooth grouping: grouping.py:127-147 (kmeans) + :150-186
  *      (build_permutation) ------------------------------------------------
@@ -219,7 +219,7 @@ VCATTN_API int vcattn_attn_nvfp4(const uint8_t* q4, const uint8_t* q4_sf_mma, co
                                  int64_t out_sh, int64_t out_sn, void* stream);
 
 /* ---- fused dense FP8 attention: triton_attn.py:203-322 (+ launch :831-844)
- * The tcgen05 kernel (D = 128, block_rows 64 or 128).  Consumes the prepare
+ * The tcgen05 kernel (D = 64 or 128, block_rows 64 or 128).  Consumes the prepare
  * outputs in the Prepared layout (v8 row-major (G,NP,D) in token order, i.e.
  * prepared without VCATTN_V_MMA_ORDER); writes O (B,H,N,D)
  * through the out view (out_dtype one of the three dtypes; strides in
@@ -239,7 +239,7 @@ VCATTN_API int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const ui
  * (README.md:514-515).  Same operands as vcattn_attn_fp8; kv_len is a device
  * array (B,) int32: in batch entry b only keys 0 .. kv_len[b]-1 of the
  * (permuted) order take part (values below 1 count as 1, above N as N), and
- * KV tiles past the last such key are not visited.  D = 128. */
+ * KV tiles past the last such key are not visited.  D = 64 or 128. */
 VCATTN_API int vcattn_attn_fp8_masked(const uint8_t* q8, const float* q_scale, const uint8_t* k8,
                     const float* k_scale, const uint8_t* v8, const float* v_scale,
                     const float* mu, const int32_t* kv_len, int B, int H, int N, int n_pad, int D,
@@ -249,7 +249,9 @@ VCATTN_API int vcattn_attn_fp8_masked(const uint8_t* q8, const float* q_scale, c
 
 /* Same computation on the register-MMA (mma.sync m16n8k32) kernel, for head
  * dims 64 and 128; V as the block-transposed v8t (G,NB,D,block_rows).  P bytes
- * follow the reference's ExpCast operation order exactly. */
+ * follow the reference's ExpCast operation order exactly.  Not on the
+ * product path (the router and vc_attention_cuda use the tcgen05 kernels);
+ * kept as a second, independently written implementation for the tests. */
 VCATTN_API int vcattn_attn_fp8_mma(const uint8_t* q8, const float* q_scale, const uint8_t* k8,
                     const float* k_scale, const uint8_t* v8t, const float* v_scale,
                     const float* mu, int B, int H, int N, int n_pad, int D,

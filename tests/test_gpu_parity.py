@@ -270,7 +270,7 @@ def _attn_gpu(q, k, v, perm, br, dev, expcast=False, out_dtype=torch.float32, ke
 
 
 def _kernels(d):
-    return ["tc", "mma"] if d == 128 else ["mma"]
+    return ["tc", "mma"]
 
 
 @pytest.mark.parametrize("kernel", ["tc", "mma"])
