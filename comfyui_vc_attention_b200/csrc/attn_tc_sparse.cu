@@ -11,7 +11,8 @@
 // ascending order.  Skipped blocks are never loaded.
 //
 // One CTA = 128 query rows = two routing query blocks (A: rows 0-63, B: rows
-// 64-127).  The CTA walks one step list: per group an approximation step if
+// 64-127).  KV tiles are value blocks of BR = 128 or 64 keys; head dims 128
+// (128-byte swizzled operand rows) and 64 (64-byte swizzle) are built.  The CTA walks one step list: per group an approximation step if
 // either query block approximates a block of it, then the union of both
 // blocks' kept tiles.  A warp's rows lie in one query block (TMEM quadrants
 // 0-1 are block A, 2-3 block B), so a step that does not concern a warp's
@@ -48,14 +49,12 @@ using namespace tc;
 char g_sp_diag[256];
 
 constexpr int kBM = 128;
-constexpr int kBR = 128;
-constexpr int kD = 128;
 constexpr int kGroup = 16;
 constexpr int kQBlock = 64;
 constexpr int kStages = 4;
 constexpr int kRing = 4;
 constexpr int kThreads = 512;
-constexpr int kMaxSteps = 1024 + 64;    // nb + groups for N up to 128K tokens
+constexpr int kMaxSteps = 1024 + 64;    // nb + groups: N up to 128K tokens (BR = 128), 64K (BR = 64)
 constexpr uint32_t kColS = 0, kColT = 256;
 constexpr int kFStride = 36;
 __host__ __device__ constexpr int ks_index(int k) {
@@ -63,6 +62,13 @@ __host__ __device__ constexpr int ks_index(int k) {
 }
 // Byte offset of (row r, byte c) in a 128-byte-swizzled tile with 128-byte rows.
 __host__ __device__ constexpr int sw128(int r, int c) { return r * 128 + ((((c >> 4) ^ (r & 7)) & 7) << 4) + (c & 15); }
+// Q, K and V operand descriptors: one swizzle atom across the row (the
+// instruction descriptor carries the major-ness).
+template <int D>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t saddr) {
+  if constexpr (D == 128) return desc_kmajor(saddr);
+  else return desc_kmajor64(saddr);
+}
 
 // Step list entry: info = index (block or group) | kind << 31 (1 = approximation);
 // mask = kept bits (bit 0 block A, bit 1 block B) of an exact step, or the
@@ -73,15 +79,16 @@ struct Step {
 __device__ __forceinline__ bool step_is_ap(const Step& s) { return (s.info >> 31) != 0; }
 __device__ __forceinline__ int step_index(const Step& s) { return static_cast<int>(s.info & 0xffffu); }
 
+template <int BR, int D>
 struct SpSmem {
-  alignas(1024) uint8_t q[kBM * 128];
-  alignas(1024) uint8_t k[kStages][kBR * 128];   // exact: K codes; proxy: bf16 k_mean tile (4 KB)
-  alignas(1024) uint8_t v[kStages][kBR * 128];   // exact: V codes; proxy: bf16 v_mean tile (4 KB)
-  alignas(1024) uint8_t qb[2][kBM * 128];         // Q as bf16, two 64-element K atoms
+  alignas(1024) uint8_t q[kBM * D];
+  alignas(1024) uint8_t k[kStages][BR * D];   // exact: K codes; proxy: bf16 k_mean tile (D * 32 bytes)
+  alignas(1024) uint8_t v[kStages][BR * D];   // exact: V codes; proxy: bf16 v_mean tile (D * 32 bytes)
+  alignas(1024) uint8_t qb[D / 64][kBM * 128];   // Q as bf16, 64-element K atoms
   alignas(1024) uint8_t ones[16 * 128];
-  alignas(16) float ks[kStages][kBR];
-  alignas(16) float vs[kStages][kD];
-  alignas(16) float mu[kStages][kD];
+  alignas(16) float ks[kStages][BR];
+  alignas(16) float vs[kStages][D];
+  alignas(16) float mu[kStages][D];
   alignas(16) float cm[kRing][2][4 * kFStride];
   alignas(16) float ksf[kRing][4 * kFStride];
   alignas(16) float alpha[kRing][kBM];   // per query row
@@ -106,9 +113,9 @@ struct SpSmem {
   int abort;
 };
 
-static_assert(sizeof(SpSmem) + 1024 <= 232448, "shared memory of the sparse kernel exceeds 227 KB");
 
 struct SpArgs {
+  const uint8_t* q8;   // (G, NP, D) codes, read directly only by the D = 64 proxy conversion
   const float* q_scale;
   const float* k_scale;
   const float* v_scale;
@@ -164,14 +171,22 @@ __device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, float (&v)[8]
                : "memory");
 }
 
-template <bool EXPCAST, int ODT>
+// P codes of one tile (NCH chunks of 32 keys, 8 columns each) into TMEM.
+template <int NCH>
+__device__ __forceinline__ void store_p(uint32_t taddr, const uint32_t (&r)[4 * NCH]) {
+  if constexpr (NCH == 4) tmem_st_16x256b_x4(taddr, r);
+  else tmem_st_16x256b_x2(taddr, r);
+}
+
+template <int BR, int D, bool EXPCAST, int ODT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_sparse_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const SpArgs a) {
-  constexpr int NCH = kBR / 32;
+  constexpr int NCH = BR / 32;   // 32-key chunks per tile
+  static_assert(sizeof(SpSmem<BR, D>) + 1024 <= 232448, "shared memory of the sparse kernel exceeds 227 KB");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  SpSmem& sm = *reinterpret_cast<SpSmem*>(smem_raw + pad);
+  SpSmem<BR, D>& sm = *reinterpret_cast<SpSmem<BR, D>*>(smem_raw + pad);
   DevStatus* status = &g_attn_sparse_tc_status;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -292,28 +307,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
-      mbar_expect_tx(&sm.q_full, kBM * 128);
+      mbar_expect_tx(&sm.q_full, kBM * D);
       tma_load_2d(sm.q, &tm_q, 0, g * a.n_pad + row0, &sm.q_full);
-      const uint32_t tile_bytes = 2u * kBR * 128u + kBR * 4u + 2u * kD * 4u;
+      const uint32_t tile_bytes = 2u * BR * D + BR * 4u + 2u * D * 4u;
       for (int j = 0; j < nst; ++j) {
         const int s = j % kStages;
         if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, status, 1)) break;
         const Step st = sm.steps[j];
         if (step_is_ap(st)) {
+          // the first D / 64 atoms of the tile's k_mean and v_mean halves
           const uint8_t* tile = a.ap_tiles + (static_cast<int64_t>(g) * a.ngroups + step_index(st)) * 8192;
-          mbar_expect_tx(&sm.kv_full[s], 8192u);
-          bulk_load(sm.k[s], tile, 4096, &sm.kv_full[s]);
-          bulk_load(sm.v[s], tile + 4096, 4096, &sm.kv_full[s]);
+          mbar_expect_tx(&sm.kv_full[s], 64u * D);
+          bulk_load(sm.k[s], tile, 32 * D, &sm.kv_full[s]);
+          bulk_load(sm.v[s], tile + 4096, 32 * D, &sm.kv_full[s]);
         } else {
           const int blk = step_index(st);
           mbar_expect_tx(&sm.kv_full[s], tile_bytes);
-          const int krow = g * a.n_pad + blk * kBR;
+          const int krow = g * a.n_pad + blk * BR;
           tma_load_2d(sm.k[s], &tm_k, 0, krow, &sm.kv_full[s]);
           tma_load_2d(sm.v[s], &tm_v, 0, krow, &sm.kv_full[s]);
-          bulk_load(sm.ks[s], a.k_scale + static_cast<int64_t>(krow), kBR * 4, &sm.kv_full[s]);
-          const int64_t vo = (static_cast<int64_t>(g) * nb + blk) * kD;
-          bulk_load(sm.vs[s], a.v_scale + vo, kD * 4, &sm.kv_full[s]);
-          bulk_load(sm.mu[s], a.mu + vo, kD * 4, &sm.kv_full[s]);
+          bulk_load(sm.ks[s], a.k_scale + static_cast<int64_t>(krow), BR * 4, &sm.kv_full[s]);
+          const int64_t vo = (static_cast<int64_t>(g) * nb + blk) * D;
+          bulk_load(sm.vs[s], a.v_scale + vo, D * 4, &sm.kv_full[s]);
+          bulk_load(sm.mu[s], a.mu + vo, D * 4, &sm.kv_full[s]);
         }
         issued = j + 1;
       }
@@ -330,8 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     {
       const uint32_t leader = elect_one();
-      const uint32_t id_qk = idesc_e4m3(kBM, kBR, false);
-      const uint32_t id_pv = idesc_e4m3(kBM, kD, true);
+      const uint32_t id_qk = idesc_e4m3(kBM, BR, false);
+      const uint32_t id_pv = idesc_e4m3(kBM, D, true);
       const uint32_t id_r = idesc_e4m3(kBM, 16, false);
       const uint32_t id_qka = idesc_bf16(kBM, kGroup, false);
       const uint32_t id_pva = idesc_bf16(kBM, 64, true);
@@ -353,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t kmb_addr = smem_u32(sm.k[s]);
 #pragma unroll
-            for (int kk = 0; kk < kD / 16; ++kk)
+            for (int kk = 0; kk < D / 16; ++kk)
               mma_bf16_if(tbase + kColS + b * 128, desc_kmajor(qb_addr + (kk >> 2) * (kBM * 128) + (kk & 3) * 32),
                           desc_kmajor(kmb_addr + (kk >> 2) * (kGroup * 128) + (kk & 3) * 32), id_qka, kk > 0,
                           leader);
@@ -361,9 +377,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t k_addr = smem_u32(sm.k[s]);
 #pragma unroll
-            for (int kk = 0; kk < kD / 32; ++kk)
-              mma_f8_if(tbase + kColS + b * 128, desc_kmajor(q_addr + kk * 32), desc_kmajor(k_addr + kk * 32), id_qk,
-                        kk > 0, leader);
+            for (int kk = 0; kk < D / 32; ++kk)
+              mma_f8_if(tbase + kColS + b * 128, operand_desc<D>(q_addr + kk * 32), operand_desc<D>(k_addr + kk * 32),
+                        id_qk, kk > 0, leader);
           }
           tc_commit_if(&sm.s_full[b], leader);
         }
@@ -378,14 +394,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (step_is_ap(st)) {
             const uint32_t vmb_addr = smem_u32(sm.v[si]);
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < D / 64; ++h)
               mma_bf16_ts_if(tbase + kColT + bi * 128 + 64 * h, p_t, desc_mnmajor(vmb_addr + 2048 * h), id_pva, 0,
                              leader);
           } else {
             const uint32_t v_addr = smem_u32(sm.v[si]);
 #pragma unroll
             for (int kk = 0; kk < NCH; ++kk)
-              mma_f8_ts_if(tbase + kColT + bi * 128, p_t + 8 * kk, desc_mnmajor(v_addr + kk * 32 * 128), id_pv, kk > 0,
+              mma_f8_ts_if(tbase + kColT + bi * 128, p_t + 8 * kk, operand_desc<D>(v_addr + kk * 32 * D), id_pv, kk > 0,
                            leader);
 #pragma unroll
             for (int kk = 0; kk < NCH; ++kk)
@@ -412,14 +428,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Step st = sm.steps[j];
       if (!step_is_ap(st)) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < D / 64; ++h) {
           const int c = c2 + 64 * h;
           const float vsc = sm.vs[s][c];
           sm.cm[ring][0][c] = __fdiv_rn(vsc, 448.0f);
           sm.cm[ring][1][c] = __fmul_rn(sm.mu[s][c], vsc);
         }
 #pragma unroll
-        for (int kc = c2; kc < kBR; kc += 64) sm.ksf[ring][ks_index(kc)] = sm.ks[s][kc];
+        for (int kc = c2; kc < BR; kc += 64) sm.ksf[ring][ks_index(kc)] = sm.ks[s][kc];
       }
       warp_arrive(&sm.f_full[ring], lane);
       warp_arrive(&sm.kv_empty[s], lane);
@@ -443,12 +459,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool run = true;
     if (sm.has_ap) {
       // Q codes -> bf16 operand of the proxy MMA (K-major, 128-byte swizzle,
-      // two 64-element atoms): each thread converts four 16-byte chunks.
+      // D / 64 atoms of 64 elements): each thread converts D / 32 16-byte
+      // chunks.  D = 128 reads the TMA-loaded tile; D = 64 reads the codes
+      // from global memory (L2), rows past the head's padded end as zeros.
+      constexpr int CPR = D / 16;   // 16-byte code chunks per row
       run = mbar_wait(&sm.q_full, 0, abort, status, 19);
-      const int t = run ? tid - 128 : kBM * 8;
-      for (int ci = t; ci < kBM * 8; ci += 256) {
-        const int r = ci >> 3, c = ci & 7;
-        const uint4 raw = *reinterpret_cast<const uint4*>(sm.q + sw128(r, 16 * c));
+      const int t = run ? tid - 128 : kBM * CPR;
+      for (int ci = t; ci < kBM * CPR; ci += 256) {
+        const int r = ci / CPR, c = ci % CPR;
+        uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (D == 128) {
+          raw = *reinterpret_cast<const uint4*>(sm.q + sw128(r, 16 * c));
+        } else if (row0 + r < a.n_pad) {
+          raw = *reinterpret_cast<const uint4*>(a.q8 + (static_cast<int64_t>(g) * a.n_pad + row0 + r) * D + 16 * c);
+        }
         const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
         uint32_t o[8];
 #pragma unroll
@@ -509,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const bool ap = (am >> bl[i]) & 1u;
-            const float len = ap ? static_cast<float>(min(kBR, a.N - (blk0 + bl[i]) * kBR)) : 0.f;
+            const float len = ap ? static_cast<float>(min(BR, a.N - (blk0 + bl[i]) * BR)) : 0.f;
             pa[i] = ap ? __fmul_rn(exp2f(__fmul_rn(__fsub_rn(xa[i], mn_a), Ae_a)), len) : 0.f;
             pb[i] = ap ? __fmul_rn(exp2f(__fmul_rn(__fsub_rn(xb[i], mn_b), Ae_b)), len) : 0.f;
             ls_a += pa[i];
@@ -537,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t zero[4 * NCH];
 #pragma unroll
         for (int i = 0; i < 4 * NCH; ++i) zero[i] = 0u;
-        tmem_st_16x256b_x4(sb, zero);
+        store_p<NCH>(sb, zero);
         warp_arrive(&sm.f_free[ring], lane);
       } else {
         float x[NCH][16];
@@ -559,8 +583,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         warp_arrive(&sm.f_free[ring], lane);
-        const int valid = a.N - step_index(st) * kBR;
-        if (valid < kBR) {
+        const int valid = a.N - step_index(st) * BR;
+        if (valid < BR) {
 #pragma unroll
           for (int ch = 0; ch < NCH; ++ch)
 #pragma unroll
@@ -610,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             packed[4 * ch + 3] = exp4(x[ch][10], x[ch][11], x[ch][14], x[ch][15], Ae_b, Be_b);
           }
         }
-        tmem_st_16x256b_x4(sb, packed);
+        store_p<NCH>(sb, packed);
         m_a = mn_a;
         m_b = mn_b;
       }
@@ -628,14 +652,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 248;\n" ::: "memory");
     // ------------------------------------------------------------ correction
-    // Thread = query row r = 32 (w%4) + lane (TMEM lane r), O[128] in
+    // Thread = query row r = 32 (w%4) + lane (TMEM lane r), O[D] in
     // registers; T read with the 32x32b shape, 64 columns per load batch.
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const uint32_t lb = tbase + (static_cast<uint32_t>(wq * 32) << 16);
-    float o[kD];
+    float o[D];
 #pragma unroll
-    for (int c = 0; c < kD; ++c) o[c] = 0.f;
+    for (int c = 0; c < D; ++c) o[c] = 0.f;
     float l = 0.f;
     bool ok = true;
     for (int i = 0; i < nst; ++i) {
@@ -665,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float4* f4 = reinterpret_cast<const float4*>(sm.cm[ring][0]);
       const float4* g4 = reinterpret_cast<const float4*>(sm.cm[ring][1]);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int half = 0; half < D / 64; ++half) {
         if (half == 1) {
           tmem_ld32(lb + tcol + 64, xa);
           tmem_ld32(lb + tcol + 96, xb);
@@ -709,12 +733,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok && !*abort) {
       constexpr int ES = (ODT == VCATTN_DTYPE_F32) ? 4 : 2;
-      constexpr int RS = kD * ES + 16;
-      static_assert(kBM * RS <= static_cast<int>(sizeof(SpSmem::q) + sizeof(SpSmem::k) + sizeof(SpSmem::v)),
+      constexpr int RS = D * ES + 16;
+      using SM = SpSmem<BR, D>;
+      static_assert(kBM * RS <= static_cast<int>(sizeof(SM::q) + sizeof(SM::k) + sizeof(SM::v)),
                     "output staging must fit in the operand buffers");
       uint8_t* stage = sm.q + wq * 32 * RS;
 #pragma unroll
-      for (int c0 = 0; c0 < kD; c0 += 16 / ES) {
+      for (int c0 = 0; c0 < D; c0 += 16 / ES) {
         uint4 w;
 #pragma unroll
         for (int e = 0; e < 16 / ES; e += 2)
@@ -722,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint4*>(stage + lane * RS + c0 * ES) = w;
       }
       __syncwarp();
-      constexpr int CPR = kD * ES / 16;
+      constexpr int CPR = D * ES / 16;
       const int bq = g / a.H, hq = g % a.H;
       uint8_t* out = static_cast<uint8_t*>(a.out) + (bq * a.osb + hq * a.osh) * ES;
       for (int idx = lane; idx < 32 * CPR; idx += 32) {
@@ -756,34 +781,36 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows) {
+// (rows, D) E4M3 codes; D = 128: 128-byte swizzle, D = 64: 64-byte swizzle.
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows, int D) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[2] = {128, rows};
-  cuuint64_t strides[1] = {128};
-  cuuint32_t box[2] = {128, box_rows};
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), rows};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(D), box_rows};
   cuuint32_t es[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_INTERLEAVE_NONE, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool EC, int ODT>
+template <int BR, int D, bool EC, int ODT>
 cudaError_t launch_sp(const AttnParams& p, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   const uint64_t rows = static_cast<uint64_t>(p.B) * p.H * p.n_pad;
-  if (!make_map(&mq, p.q8, rows, kBM) || !make_map(&mk, p.k8, rows, kBR) || !make_map(&mv, p.v8, rows, kBR))
+  if (!make_map(&mq, p.q8, rows, kBM, D) || !make_map(&mk, p.k8, rows, BR, D) || !make_map(&mv, p.v8, rows, BR, D))
     return cudaErrorInvalidValue;
   SpArgs a{};
+  a.q8 = p.q8;
   a.q_scale = p.q_scale; a.k_scale = p.k_scale; a.v_scale = p.v_scale; a.mu = p.mu;
   a.ap_tiles = p.ap_tiles; a.keep = p.keep;
-  a.H = p.H; a.N = p.N; a.n_pad = p.n_pad; a.nb = p.n_pad / kBR; a.nqb = p.n_pad / kQBlock;
+  a.H = p.H; a.N = p.N; a.n_pad = p.n_pad; a.nb = p.n_pad / BR; a.nqb = p.n_pad / kQBlock;
   a.ngroups = (a.nb + kGroup - 1) / kGroup;
   a.sm_scale = p.sm_scale;
   a.c120 = static_cast<float>(64.0 + 56.0 + p.beta);
   a.out = p.out; a.osb = p.osb; a.osh = p.osh; a.osn = p.osn;
-  const size_t smem = sizeof(SpSmem) + 1024;
-  auto k = attn_tc_sparse_kernel<EC, ODT>;
+  const size_t smem = sizeof(SpSmem<BR, D>) + 1024;
+  auto k = attn_tc_sparse_kernel<BR, D, EC, ODT>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const dim3 grid((p.n_pad + kBM - 1) / kBM, p.B * p.H);
@@ -798,24 +825,32 @@ cudaError_t launch_sp(const AttnParams& p, cudaStream_t st) {
   return e;
 }
 
+template <int BR, int D>
+cudaError_t launch_sp_shape(const AttnParams& p, cudaStream_t st) {
+  const bool ec = (p.flags & VCATTN_EXPCAST) != 0;
+  switch (p.out_dtype) {
+    case VCATTN_DTYPE_BF16:
+      return ec ? launch_sp<BR, D, true, VCATTN_DTYPE_BF16>(p, st) : launch_sp<BR, D, false, VCATTN_DTYPE_BF16>(p, st);
+    case VCATTN_DTYPE_F16:
+      return ec ? launch_sp<BR, D, true, VCATTN_DTYPE_F16>(p, st) : launch_sp<BR, D, false, VCATTN_DTYPE_F16>(p, st);
+    default:
+      return ec ? launch_sp<BR, D, true, VCATTN_DTYPE_F32>(p, st) : launch_sp<BR, D, false, VCATTN_DTYPE_F32>(p, st);
+  }
+}
+
 }  // namespace
 
 bool attn_sparse_tc_supported(const AttnParams& p) {
-  return p.D == kD && p.block_rows == kBR && p.q_block == kQBlock && p.group == kGroup &&
-         p.n_pad / kBR + (p.n_pad / kBR + kGroup - 1) / kGroup <= kMaxSteps;
+  const bool br_ok = p.block_rows == 128 || p.block_rows == 64;
+  return (p.D == 128 || p.D == 64) && br_ok && p.q_block == kQBlock && p.group == kGroup &&
+         p.n_pad % p.block_rows == 0 &&
+         p.n_pad / p.block_rows + (p.n_pad / p.block_rows + kGroup - 1) / kGroup <= kMaxSteps;
 }
 
 cudaError_t launch_attn_sparse_tc(const AttnParams& p, cudaStream_t st) {
   if (!attn_sparse_tc_supported(p)) return cudaErrorNotSupported;
-  const bool ec = (p.flags & VCATTN_EXPCAST) != 0;
-  switch (p.out_dtype) {
-    case VCATTN_DTYPE_BF16:
-      return ec ? launch_sp<true, VCATTN_DTYPE_BF16>(p, st) : launch_sp<false, VCATTN_DTYPE_BF16>(p, st);
-    case VCATTN_DTYPE_F16:
-      return ec ? launch_sp<true, VCATTN_DTYPE_F16>(p, st) : launch_sp<false, VCATTN_DTYPE_F16>(p, st);
-    default:
-      return ec ? launch_sp<true, VCATTN_DTYPE_F32>(p, st) : launch_sp<false, VCATTN_DTYPE_F32>(p, st);
-  }
+  if (p.block_rows == 128) return p.D == 128 ? launch_sp_shape<128, 128>(p, st) : launch_sp_shape<128, 64>(p, st);
+  return p.D == 128 ? launch_sp_shape<64, 128>(p, st) : launch_sp_shape<64, 64>(p, st);
 }
 
 const char* attn_sparse_tc_diag() { return g_sp_diag; }

@@ -305,10 +305,12 @@ int vcattn_route_tiles(const float* k_mean, const float* v_mean, int G, int n_pa
                        uint8_t* tiles, void* stream) {
   g_last_error.clear();
   VC_CHECK(k_mean && v_mean && tiles, "vcattn_route_tiles: null pointer");
-  VC_CHECK(D == 128 && block_rows == 128, "vcattn_route_tiles: needs D = 128 and block_rows = 128");
+  VC_CHECK((D == 128 || D == 64) && (block_rows == 128 || block_rows == 64),
+           "vcattn_route_tiles: needs D and block_rows in {64, 128}");
   VC_CHECK(G > 0 && n_pad > 0 && n_pad % block_rows == 0, "vcattn_route_tiles: bad shape");
   VC_CHECK(aligned16(tiles), "vcattn_route_tiles: tiles must be 16-byte aligned");
-  return cuda_status(launch_route_tiles(k_mean, v_mean, G, n_pad / block_rows, tiles, static_cast<cudaStream_t>(stream)),
+  return cuda_status(launch_route_tiles(k_mean, v_mean, G, n_pad / block_rows, D, tiles,
+                                        static_cast<cudaStream_t>(stream)),
                      "vcattn_route_tiles");
 }
 
@@ -499,7 +501,8 @@ int vcattn_attn_fp8_sparse_tc(const uint8_t* q8, const float* q_scale, const uin
   p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
   p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
   VC_CHECK(attn_sparse_tc_supported(p),
-           "vcattn_attn_fp8_sparse_tc: needs D = 128, block_rows = 128, q_block = 64, group = 16 and N <= 131072");
+           "vcattn_attn_fp8_sparse_tc: needs D and block_rows in {64, 128}, q_block = 64, group = 16 and at most "
+           "1024 KV blocks (N <= 131072 at block_rows 128, 65536 at 64)");
   const cudaError_t e = launch_attn_sparse_tc(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess)
     return fail(VCATTN_ERR_CUDA,

@@ -77,7 +77,7 @@ size_t kmeans_workspace_bytes(int G, int N, int D, int k, int nkeys);
 cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t st);
 cudaError_t launch_prepare_nvfp4(const NvfpParams& p, cudaStream_t st);
 cudaError_t launch_route_mask(const RouteParams& p, cudaStream_t st);
-cudaError_t launch_route_tiles(const float* k_mean, const float* v_mean, int G, int nb, uint8_t* tiles,
+cudaError_t launch_route_tiles(const float* k_mean, const float* v_mean, int G, int nb, int D, uint8_t* tiles,
                                cudaStream_t st);
 cudaError_t launch_kmeans(const KMeansParams& p, cudaStream_t st);
 // Tensor-core nearest-centroid assignment (kmeans_tc.cu): labels identical to

@@ -703,7 +703,7 @@ __host__ __device__ constexpr int tile_sw128(int r, int c) {
 
 __global__ void __launch_bounds__(256) route_tiles_kernel(const float* __restrict__ k_mean,
                                                           const float* __restrict__ v_mean, int nb, int ngroups,
-                                                          uint8_t* __restrict__ tiles) {
+                                                          int D, uint8_t* __restrict__ tiles) {
   const int grp = blockIdx.x, g = blockIdx.y;
   const int g0 = grp * 16;
   uint8_t* t = tiles + (static_cast<int64_t>(g) * ngroups + grp) * 8192;
@@ -713,8 +713,8 @@ __global__ void __launch_bounds__(256) route_tiles_kernel(const float* __restric
     const int ch = 2 * pair;                       // channel of the low half
     const int blk = g0 + (which == 0 ? r : route_tile_block(r));
     float v0 = 0.f, v1 = 0.f;
-    if (blk < nb) {
-      const float* src = (which == 0 ? k_mean : v_mean) + (static_cast<int64_t>(g) * nb + blk) * 128 + ch;
+    if (blk < nb && ch < D) {   // head dim 64: channels 64-127 of the tile stay zero
+      const float* src = (which == 0 ? k_mean : v_mean) + (static_cast<int64_t>(g) * nb + blk) * D + ch;
       v0 = src[0];
       v1 = src[1];
     }
@@ -725,11 +725,11 @@ __global__ void __launch_bounds__(256) route_tiles_kernel(const float* __restric
   }
 }
 
-cudaError_t launch_route_tiles(const float* k_mean, const float* v_mean, int G, int nb, uint8_t* tiles,
+cudaError_t launch_route_tiles(const float* k_mean, const float* v_mean, int G, int nb, int D, uint8_t* tiles,
                                cudaStream_t st) {
   const int ngroups = (nb + 15) / 16;
   if (G <= 0 || ngroups <= 0) return cudaSuccess;
-  route_tiles_kernel<<<dim3(ngroups, G), 256, 0, st>>>(k_mean, v_mean, nb, ngroups, tiles);
+  route_tiles_kernel<<<dim3(ngroups, G), 256, 0, st>>>(k_mean, v_mean, nb, ngroups, D, tiles);
   return cudaGetLastError();
 }
 

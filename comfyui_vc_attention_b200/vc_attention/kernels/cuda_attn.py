@@ -216,7 +216,7 @@ def prepare(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, perm: Optional[to
         nqb = n_pad // q_block
         keep, thresh = route_mask(route, g, n, n_pad, d, block_rows, tau, local_blocks, sink_blocks,
                                   sc, dev, q)
-        if d == 128 and block_rows == 128:
+        if d in (64, 128) and block_rows in (64, 128):
             ap_tiles = torch.empty((g, -(-nb // 16), 8192), dtype=u8, device=dev)
             N.check("vcattn_route_tiles", lib.vcattn_route_tiles(
                 k_mean.data_ptr(), v_mean.data_ptr(), g, n_pad, d, block_rows, ap_tiles.data_ptr(), _stream(q)))
@@ -418,7 +418,7 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
         if kernel == "tc":
             if p.v is None or not p.v_mma_order or p.ap_tiles is None:
                 raise ValueError("the tcgen05 sparse kernel reads V codes in its key order and the proxy "
-                                 "tiles (want_v=True, v_mma_order=True, D = block_rows = 128)")
+                                 "tiles (want_v=True, v_mma_order=True, D and block_rows in {64, 128})")
             N.check("vcattn_attn_fp8_sparse_tc", lib.vcattn_attn_fp8_sparse_tc(
                 q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
                 p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), p.ap_tiles.data_ptr(),
@@ -458,9 +458,11 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
 
 def sparse_tc_applies(d: int, block_rows: int, q_block: int, group: int, n: int) -> bool:
     """Whether the tcgen05 sparse kernel takes this shape (two 64-row routing
-    blocks per CTA, 128-key tiles, groups of 16, at most 1024 KV tiles)."""
+    blocks per CTA, head dim and value block of 64 or 128, groups of 16, at
+    most 1024 KV tiles)."""
     nb = -(-n // block_rows)
-    return d == 128 and block_rows == 128 and q_block == 64 and group == 16 and nb + -(-nb // 16) <= 1088
+    return (d in (64, 128) and block_rows in (64, 128) and q_block == 64 and group == 16
+            and nb + -(-nb // 16) <= 1088)
 
 
 def attention_status(reset: bool = True):

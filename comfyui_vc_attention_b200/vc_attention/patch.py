@@ -172,8 +172,8 @@ class VCAttentionRuntime:
         from .kernels.cuda_attn import TritonConfig, sparse_tc_applies, vc_attention_triton
         sparse, tau = self.sparsity(n)
         if sparse and not sparse_tc_applies(d, cfg.block_rows, cfg.block_m, 16, n):
-            # the tcgen05 sparse kernel takes head dim 128, 128-row value
-            # blocks and 64-row query blocks; other shapes run the exact
+            # the tcgen05 sparse kernel takes head dims and value blocks of
+            # 64 or 128 with 64-row query blocks; other shapes run the exact
             # dense tcgen05 kernel, which is faster than the register-MMA
             # sparse kernel (10.9 ms vs 6.1 ms at the configs[2] size)
             sparse = False

@@ -282,7 +282,8 @@ VCATTN_API int vcattn_attn_fp8_sparse(const uint8_t* q8, const float* q_scale, c
  * operands): per (head, group of 16 KV blocks) one 8192-byte tile holding
  * bf16(k_mean) and bf16(v_mean) of the group in the kernel's 128-byte
  * swizzled shared-memory layout.  tiles: G * ceil(NB/16) * 8192 bytes.
- * Needs D = 128 and block_rows = 128. */
+ * D and block_rows in {64, 128}; with D = 64 channels 64-127 of each half are
+ * zero. */
 VCATTN_API int vcattn_route_tiles(const float* k_mean, const float* v_mean, int G, int n_pad, int D,
                        int block_rows, uint8_t* tiles, void* stream);
 
@@ -291,9 +292,9 @@ VCATTN_API int vcattn_route_tiles(const float* k_mean, const float* v_mean, int 
  * (G,NP,D) in the tcgen05 key order (prepare flag VCATTN_V_MMA_ORDER)
  * instead of the block-transposed v8t, and the proxy operands as the tiles
  * of vcattn_route_tiles instead of fp32 k_mean / v_mean.  One CTA runs two
- * routing query blocks: needs D = 128, block_rows = 128, q_block = 64,
- * group = 16 and n_pad / 128 <= 1024.  Bounded waits report through
- * vcattn_attn_status as 200 + site. */
+ * routing query blocks: needs D and block_rows in {64, 128}, q_block = 64,
+ * group = 16 and at most 1024 KV blocks (n_pad / block_rows).  Bounded waits
+ * report through vcattn_attn_status as 200 + site. */
 VCATTN_API int vcattn_attn_fp8_sparse_tc(const uint8_t* q8, const float* q_scale, const uint8_t* k8,
                               const float* k_scale, const uint8_t* v8, const float* v_scale,
                               const float* mu, const uint8_t* ap_tiles,

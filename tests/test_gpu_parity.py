@@ -399,15 +399,16 @@ def test_route_mask_bit_exact(dev, tau, local, sink):
     assert 0.0 < keep.mean() < 1.0, "routing must be non-trivial on the spatial inputs"
 
 
-def _sparse_gpu(q, k, v, perm, dev, tau, local=1, sink=0, expcast=False, out_dtype=torch.float32, kernel="mma"):
+def _sparse_gpu(q, k, v, perm, dev, tau, local=1, sink=0, expcast=False, out_dtype=torch.float32, kernel="mma",
+                br=128):
     from comfyui_vc_attention_b200.vc_attention.kernels.cuda_attn import (TritonConfig, attention_prepared,
                                                                            attention_status)
     b, h, n, d = q.shape
     tc = kernel == "tc"
-    p = _prep_gpu(q, k, v, perm, 128, dev, sparse=True, tau=tau, q_block=64, want_v_t=not tc, want_v=tc,
+    p = _prep_gpu(q, k, v, perm, br, dev, sparse=True, tau=tau, q_block=64, want_v_t=not tc, want_v=tc,
                   local_blocks=local, sink_blocks=sink)
     out = torch.empty((b, h, n, d), dtype=out_dtype, device=dev)
-    cfg = TritonConfig(block_m=64, block_n=128, sparse=True, tau=tau, local_blocks=local, sink_blocks=sink,
+    cfg = TritonConfig(block_m=64, block_n=br, sparse=True, tau=tau, local_blocks=local, sink_blocks=sink,
                        enable_expcast=expcast)
     attention_prepared(p, n, out, d ** -0.5, cfg, kernel=kernel)
     torch.cuda.synchronize()
@@ -503,6 +504,49 @@ def test_sparse_ragged_and_multi_group(dev, kernel):
     assert np.array_equal(keep, keep_o)
     ref = O.attention_sparse_codes(prep, st, keep, n, 128, 64, 128 ** -0.5, group=16)
     assert O.rel_l2(got, ref) <= REL_L2_CODES
+
+
+_SPARSE_SHAPES = [(1024, 64, 128, 1.3), (1024, 128, 64, 1.3), (1000, 64, 64, 0.8), (2048, 64, 128, 0.8),
+                  (2500, 128, 64, 0.8)]
+
+
+def _sparse_shape_case(n, br, d):
+    grid = {1024: (4, 16, 16), 2048: (8, 16, 16)}.get(n)
+    q, k, v = make_qkv(1, 2, n, d, seed=n + d + br, spatial=grid)
+    perm = np.stack([np.random.default_rng(70 + i).permutation(n) for i in range(2)]).astype(np.int32)
+    return q, k, v, perm
+
+
+@pytest.mark.parametrize("n,br,d,tau", _SPARSE_SHAPES)
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
+def test_sparse_shapes(dev, n, br, d, tau, kernel):
+    """Value blocks of 64 keys and head dim 64 (one and two 16-block groups,
+    ragged N) on both sparse kernels: the GPU routing mask equals the
+    oracle's, and the output matches the oracle driven by that mask."""
+    h = 2
+    q, k, v, perm = _sparse_shape_case(n, br, d)
+    got, p = _sparse_gpu(q, k, v, perm, dev, tau=tau, kernel=kernel, br=br)
+    qg, kg, vg = (a.reshape(h, n, d) for a in (q, k, v))
+    prep = O.prepare(qg, kg, vg, perm, block_rows=br)
+    sc = d ** -0.5
+    st = O.route_stats(prep, br, 64, tau, sc)
+    keep_o, _ = O.route_mask(prep, st, n, br, 64, sc, local_blocks=1)
+    keep = p.keep.cpu().numpy().astype(bool)
+    assert np.array_equal(keep, keep_o)
+    assert 0.0 < keep.mean() < 1.0
+    ref = O.attention_sparse_codes(prep, st, keep, n, br, 64, sc, group=16)
+    assert O.rel_l2(got, ref) <= REL_L2_CODES
+
+
+@pytest.mark.parametrize("n,br,d", [(1024, 64, 128), (1024, 128, 64), (1000, 64, 64)])
+def test_sparse_tc_keep_all_equals_dense_shapes(dev, n, br, d):
+    """Every block kept: the tcgen05 sparse kernel at 64-key value blocks and
+    head dim 64 equals the dense tcgen05 kernel of the same shape bit for bit."""
+    q, k, v, perm = _sparse_shape_case(n, br, d)
+    sparse, p = _sparse_gpu(q, k, v, perm, dev, tau=-1000.0, kernel="tc", br=br)
+    assert p.keep.bool().all()
+    dense = _attn_gpu(q, k, v, perm, br, dev, kernel="tc")
+    assert np.array_equal(sparse, dense)
 
 
 # ------------------------------------------------------------ NVFP4 Q / K ----
