@@ -496,6 +496,8 @@ def main() -> int:
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent full-size replicas per rank instead of the sharded split")
     ap.add_argument("--no-psnr", action="store_true")
+    ap.add_argument("--kv-split", type=int, default=1,
+                    help="dense kernel KV split: 1 = none, 0 = the last partial wave (auto), k = k pieces")
     ap.add_argument("--eager", action="store_true", help="N > 1: launch every round eagerly (no CUDA graph)")
     ap.add_argument("--serial-rounds", action="store_true",
                     help="N > 1: rounds in order on one stream (default: two alternating streams)")
@@ -544,7 +546,7 @@ def main() -> int:
     kmeans_ms = e0.elapsed_time(e1)
     perm = res.perm
     cfg = TritonConfig(block_n=w["block_rows"], enable_expcast=w["expcast"], sparse=w["sparse"],
-                       tau=w.get("tau", 1.3), qk_fp4=w.get("qk_fp4", False))
+                       tau=w.get("tau", 1.3), qk_fp4=w.get("qk_fp4", False), kv_split=args.kv_split)
     scale = D ** -0.5
     out = torch.empty_like(q)
     # tcgen05 kernels read V in their key order; the register-MMA sparse
@@ -680,7 +682,7 @@ def main() -> int:
         "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 (fp32 accumulate)",
         "data": "synthetic (seeded configs[1] distributions, generated on device)",
         "config": {"workload": w["desc"], "B": B, "H": H, "N": NT, "D": D, "block_rows": w["block_rows"],
-                   "kmeans_k": res.k, "expcast": w["expcast"], "sparse": w["sparse"],
+                   "kmeans_k": res.k, "expcast": w["expcast"], "sparse": w["sparse"], "kv_split": args.kv_split,
                    "parallelism": (f"(batch, head) units x{world} ranks, independent replicas, no collective"
                                    if world > 1 else "one GPU"),
                    "l2": "inputs larger than L2 (Q/K/V 235 MB each)",

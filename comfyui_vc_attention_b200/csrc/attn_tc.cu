@@ -34,6 +34,7 @@
 // head dim 128 and the 64-byte swizzle for head dim 64.
 // Every wait is bounded.
 #include <cuda.h>
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 
@@ -93,6 +94,12 @@ struct TcSmem {
   uint32_t tmem_base;
   int abort;
   int kvn;     // keys taking part in this CTA's head
+  int g;       // head (b * H + h)
+  int row0;    // first query row
+  int slot;    // KV piece of a split query tile (partial output slot), or -1
+  int j0;      // first KV tile of this CTA (0 unless it runs one piece of a split query tile)
+  int ntl;     // KV tiles this CTA visits
+  int kv0;     // kvn - j0 * BR: keys of this CTA's tile range from its first tile on
   int nload;   // KV tiles the producer loads (fewer only under vcattn_inject_stall)
 };
 
@@ -108,6 +115,17 @@ struct TcArgs {
   int64_t osb, osh, osn;
   const int32_t* kv_len;   // (B,) keys taking part per batch entry, or null (all N)
   int stall_tile;          // tests: the producer stops before this KV tile (-1: never)
+  // Grid: CTA t < n_main runs query tile t of the flattened (head, query
+  // tile) order whole; CTA n_main + u runs KV piece u % pieces of query tile
+  // n_main + u / pieces and writes its unnormalised partial to part_o
+  // ([u][D][128]), part_l and part_m ([u][128]: row sum and log2-domain max).
+  int qt;                  // query tiles per head
+  int n_main;
+  int pieces;              // >= 1
+  int tp;                  // KV tiles per piece
+  float* part_o;
+  float* part_l;
+  float* part_m;
 };
 
 // ECM: 0 = E4M3 of exp2, 1 = one-FMA ExpCast, 2 = ExpCast in the reference's
@@ -132,17 +150,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   DevStatus* status = &g_attn_tc_status;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = blockIdx.y;
-  const int row0 = blockIdx.x * kBM;
   const int nb = a.nb;
 
   if (tid == 0) {
+    // (head, query tile) of this CTA, kept in shared memory (read where used,
+    // so that no role holds them in registers through its loop)
+    const int cta = static_cast<int>(blockIdx.x);
+    const int slot = cta < a.n_main ? -1 : cta - a.n_main;
+    const int tq = slot < 0 ? cta : a.n_main + slot / a.pieces;
+    const int g = tq / a.qt;
+    sm.g = g;
+    sm.row0 = (tq - g * a.qt) * kBM;
+    sm.slot = slot;
     // Keys at (permuted) positions >= kvn take no part (reference.py
     // valid_len, padding sorted to the tail by grouping.py:181-183); only the
     // tiles holding keys below kvn are visited.
     sm.kvn = a.kv_len ? min(a.N, max(1, a.kv_len[g / a.H])) : a.N;
     const int tiles = (sm.kvn + BR - 1) / BR;
-    sm.nload = a.stall_tile >= 0 ? min(tiles, a.stall_tile) : tiles;
+    int j0 = 0, nt = tiles;
+    if (slot >= 0) {
+      j0 = (slot % a.pieces) * a.tp;
+      nt = max(0, min(a.tp, tiles - j0));
+    }
+    sm.j0 = j0;
+    sm.kv0 = sm.kvn - j0 * BR;
+    sm.ntl = nt;
+    sm.nload = a.stall_tile >= 0 ? min(nt, a.stall_tile) : nt;
 
     sm.abort = 0;
     mbar_init(&sm.q_full, 1);
@@ -176,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tbase = sm.tmem_base;
   volatile int* abort = &sm.abort;
-#define VC_TILES_VISITED ((sm.kvn + BR - 1) / BR)
+#define VC_TILES_VISITED (sm.ntl)
 
   if (warp < 4) {
   // Register budget per warpgroup (launched at 168 x 384 = 64512):
@@ -190,7 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
       mbar_expect_tx(&sm.q_full, kBM * kD);
-      tma_load_2d(sm.q, &tm_q, 0, g * a.n_pad + row0, &sm.q_full);
+      const int g = sm.g, j0 = sm.j0;
+      tma_load_2d(sm.q, &tm_q, 0, g * a.n_pad + sm.row0, &sm.q_full);
       const uint32_t tile_bytes = 2u * BR * kD + BR * 4u + 2u * kD * 4u;
       // (under vcattn_inject_stall the copies of tile nload on never come,
       // and the waits on them time out)
@@ -198,11 +232,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = j % kStages;
         if (j >= kStages && !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, status, 1)) break;
         mbar_expect_tx(&sm.kv_full[s], tile_bytes);
-        const int krow = g * a.n_pad + j * BR;
+        const int krow = g * a.n_pad + (j0 + j) * BR;
         tma_load_2d(sm.k[s], &tm_k, 0, krow, &sm.kv_full[s]);
         tma_load_2d(sm.v[s], &tm_v, 0, krow, &sm.kv_full[s]);
         bulk_load(sm.ks[s], a.k_scale + static_cast<int64_t>(krow), BR * 4, &sm.kv_full[s]);
-        const int64_t vo = (static_cast<int64_t>(g) * nb + j) * kD;
+        const int64_t vo = (static_cast<int64_t>(g) * nb + j0 + j) * kD;
         bulk_load(sm.vs[s], a.v_scale + vo, kD * 4, &sm.kv_full[s]);
         bulk_load(sm.mu[s], a.mu + vo, kD * 4, &sm.kv_full[s]);
         issued = j + 1;
@@ -296,7 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // P for keys 4c..4c+3 in column c (key order: V is read in token order).
     const int t = (warp & 3) * 32 + lane;
     const uint32_t lane_base = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const int64_t qrow = static_cast<int64_t>(g) * a.n_pad + row0 + t;
+    const int row0 = sm.row0;
+    const int64_t qrow = static_cast<int64_t>(sm.g) * a.n_pad + row0 + t;
     const float qs = (row0 + t < a.n_pad) ? a.q_scale[qrow] : 0.f;
     const float qsm = __fmul_rn(qs, a.sm_scale);
     // ExpCast: c = A * (x - m) + c120 with A = 8 log2e qs sm; evaluated as
@@ -338,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mul2(x[4 * q + 2], x[4 * q + 3], kv.z, kv.w);
         }
       }
-      const int valid = sm.kvn - j * BR;                 // keys >= valid are padding or masked
+      const int valid = sm.kv0 - j * BR;                 // keys >= valid are padding or masked
       if (valid < BR) {
 #pragma unroll
         for (int c = 0; c < BR; ++c)
@@ -409,6 +444,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       warp_arrive(&sm.a_full[ring], lane);
       m = mn;
     }
+    // split piece: its row max in the log2 domain, for the combine
+    if (sm.slot >= 0) a.part_m[sm.slot * kBM + t] = __fmul_rn(m, Ae);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 248;\n" ::: "memory");
     // ------------------------------------------------------------ correction
@@ -474,7 +511,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       warp_arrive(&sm.f_free[ring], lane);
       l = __fadd_rn(__fmul_rn(l, al), rr);
     }
-    if (ok && !*abort) {
+    const int slot = sm.slot;
+    if (ok && !*abort && slot >= 0) {
+      // split piece: unnormalised O (channel-major, coalesced over rows) and l
+      float* po = a.part_o + static_cast<int64_t>(slot) * kD * kBM + r;
+#pragma unroll
+      for (int c = 0; c < kD; ++c) po[c * kBM] = o[c];
+      a.part_l[slot * kBM + r] = l;
+    } else if (ok && !*abort) {
       // Stage this warp's 32 rows (padded stride), then write them out as
       // whole 16-byte row chunks.
       constexpr int ES = (ODT == VCATTN_DTYPE_F32) ? 4 : 2;
@@ -493,6 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       constexpr int CPR = kD * ES / 16;   // 16-byte chunks per row
+      const int g = sm.g, row0 = sm.row0;
       const int bq = g / a.H, hq = g % a.H;
       uint8_t* out = static_cast<uint8_t*>(a.out) + (bq * a.osb + hq * a.osh) * ES;
       for (int idx = lane; idx < 32 * CPR; idx += 32) {
@@ -508,6 +553,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tbase, 512);
 }
 #undef VC_TILES_VISITED
+
+constexpr int kMaxPieces = 32;
+
+// The split query tiles: out = sum_p w_p O_p / sum_p w_p l_p with
+// w_p = exp2(m_p - max_p m_p) (m_p in the log2 domain), one thread per row.
+template <int D, int ODT>
+__global__ void __launch_bounds__(kBM) attn_tc_combine_kernel(const TcArgs a) {
+  const int e = blockIdx.x, r = threadIdx.x;
+  const int tq = a.n_main + e;
+  const int g = tq / a.qt;
+  const int row = (tq - g * a.qt) * kBM + r;
+  if (row >= a.N) return;
+  const int u0 = e * a.pieces;
+  float mx = -INFINITY;
+  for (int q = 0; q < a.pieces; ++q) mx = fmaxf(mx, a.part_m[(u0 + q) * kBM + r]);
+  float w[kMaxPieces];
+  float den = 0.f;
+#pragma unroll
+  for (int q = 0; q < kMaxPieces; ++q) {
+    w[q] = q < a.pieces ? exp2f(__fsub_rn(a.part_m[(u0 + q) * kBM + r], mx)) : 0.f;
+    if (q < a.pieces) den = __fmaf_rn(w[q], a.part_l[(u0 + q) * kBM + r], den);
+  }
+  constexpr int ES = (ODT == VCATTN_DTYPE_F32) ? 4 : 2;
+  const int bq = g / a.H, hq = g % a.H;
+  uint8_t* out = static_cast<uint8_t*>(a.out) + ((bq * a.osb + hq * a.osh) + static_cast<int64_t>(row) * a.osn) * ES;
+  const float* po = a.part_o + static_cast<int64_t>(u0) * D * kBM + r;
+  for (int c = 0; c < D; c += 2) {
+    float n0 = 0.f, n1 = 0.f;
+#pragma unroll
+    for (int q = 0; q < kMaxPieces; ++q) {
+      if (q < a.pieces) {
+        n0 = __fmaf_rn(w[q], po[(static_cast<int64_t>(q) * D + c) * kBM], n0);
+        n1 = __fmaf_rn(w[q], po[(static_cast<int64_t>(q) * D + c + 1) * kBM], n1);
+      }
+    }
+    stage2<ODT>(out + c * ES, __fdiv_rn(n0, den), __fdiv_rn(n1, den));
+  }
+}
 
 // ---- host side ---------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -541,6 +624,50 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
+  return n > 0 ? n : 148;
+}
+
+// Which query tiles run split over their KV tiles (see TcArgs).  Auto: when
+// the CTAs end in a partial wave holding at most half of the SMs, its query
+// tiles run in about SMs / (tiles in that wave) pieces each, so the last wave
+// takes a fraction of a CTA's time instead of a whole one.
+struct SplitPlan {
+  int qt, n_main, pieces, tp, nsplit;
+};
+
+SplitPlan plan_split(const AttnParams& p) {
+  SplitPlan s{};
+  s.qt = (p.n_pad + kBM - 1) / kBM;
+  const int ctas = p.B * p.H * s.qt;
+  const int tiles = (p.N + p.block_rows - 1) / p.block_rows;
+  s.n_main = ctas;
+  s.pieces = 1;
+  s.tp = tiles;
+  s.nsplit = 0;
+  if (p.kv_len != nullptr || g_stall_tile >= 0 || p.kv_split == 1 || p.part == nullptr || tiles < 2) return s;
+  int r = ctas, want = p.kv_split;
+  if (p.kv_split <= 0) {
+    const int nsm = sm_count();
+    r = ctas % nsm;
+    if (ctas <= nsm || r == 0 || r > nsm / 2) return s;
+    want = nsm / r;
+  }
+  want = std::min(want, std::min(tiles, kMaxPieces));
+  if (want < 2) return s;
+  const int tp = (tiles + want - 1) / want;
+  const int pieces = (tiles + tp - 1) / tp;
+  if (pieces < 2) return s;
+  s.n_main = ctas - r;
+  s.pieces = pieces;
+  s.tp = tp;
+  s.nsplit = r * pieces;
+  return s;
+}
+
 template <int BR, int D, int EC, int ODT>
 cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
@@ -556,13 +683,28 @@ cudaError_t launch_tc(const AttnParams& p, cudaStream_t st) {
   a.out = p.out; a.osb = p.osb; a.osh = p.osh; a.osn = p.osn;
   a.kv_len = p.kv_len;
   a.stall_tile = g_stall_tile;
+  const SplitPlan sp = plan_split(p);
+  a.qt = sp.qt;
+  a.n_main = sp.n_main;
+  a.pieces = sp.pieces;
+  a.tp = sp.tp;
+  if (sp.nsplit > 0) {
+    float* part = static_cast<float*>(p.part);
+    a.part_o = part;
+    a.part_l = part + static_cast<size_t>(sp.nsplit) * D * kBM;
+    a.part_m = a.part_l + static_cast<size_t>(sp.nsplit) * kBM;
+  }
   const size_t smem = sizeof(TcSmem<BR, D>) + 1024;
   auto k = attn_tc_kernel<BR, D, EC, ODT>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const dim3 grid((p.n_pad + kBM - 1) / kBM, p.B * p.H);
-  k<<<grid, kThreads, smem, st>>>(mq, mk, mv, a);
+  const unsigned ctas = static_cast<unsigned>(sp.n_main + sp.nsplit);
+  k<<<ctas, kThreads, smem, st>>>(mq, mk, mv, a);
   e = cudaGetLastError();
+  if (e == cudaSuccess && sp.nsplit > 0) {
+    attn_tc_combine_kernel<D, ODT><<<sp.nsplit / sp.pieces, kBM, 0, st>>>(a);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) {
     cudaFuncAttributes fa{};
     cudaFuncGetAttributes(&fa, k);
@@ -604,6 +746,13 @@ cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t st) {
 const char* attn_tc_diag() { return g_tc_diag; }
 
 void set_attn_tc_stall(int tile) { g_stall_tile = tile; }
+
+size_t attn_tc_split_bytes(const AttnParams& p) {
+  AttnParams q = p;
+  q.part = reinterpret_cast<void*>(16);   // plan as if a workspace were given
+  const SplitPlan sp = plan_split(q);
+  return static_cast<size_t>(sp.nsplit) * kBM * (p.D + 2) * sizeof(float);
+}
 
 cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset) {
   tc::DevStatus s{};

@@ -352,6 +352,47 @@ int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k8, 
   return VCATTN_OK;
 }
 
+size_t vcattn_attn_split_workspace_bytes(int B, int H, int N, int n_pad, int D, int block_rows, int kv_split) {
+  if (B <= 0 || H <= 0 || N <= 0 || n_pad < N || (D != 64 && D != 128) || (block_rows != 64 && block_rows != 128))
+    return 0;
+  AttnParams p{};
+  p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows; p.kv_split = kv_split;
+  return attn_tc_split_bytes(p);
+}
+
+int vcattn_attn_fp8_split(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
+                          const uint8_t* v8, const float* v_scale, const float* mu, int B, int H, int N, int n_pad,
+                          int D, int block_rows, float sm_scale, int flags, double expcast_beta, void* out,
+                          int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn, int kv_split,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (injected("vcattn_attn_fp8_split")) return fail(VCATTN_ERR_INJECTED, "vcattn_attn_fp8_split: injected fault");
+  const int rc = attn_common_checks("vcattn_attn_fp8_split", q8, q_scale, k8, k_scale, v8, v_scale, mu, B, H, N,
+                                    n_pad, D, block_rows, out, out_dtype);
+  if (rc != VCATTN_OK) return rc;
+  VC_CHECK(aligned16(out) && (out_sn % 8) == 0 && (out_sh % 8) == 0 && (out_sb % 8) == 0,
+           "vcattn_attn_fp8_split: out must be 16-byte aligned with 8-element multiple strides");
+  VC_CHECK(kv_split >= 0, "vcattn_attn_fp8_split: kv_split must be >= 0");
+  AttnParams p{};
+  p.q8 = q8; p.k8 = k8; p.v8 = v8; p.q_scale = q_scale; p.k_scale = k_scale; p.v_scale = v_scale; p.mu = mu;
+  p.B = B; p.H = H; p.N = N; p.n_pad = n_pad; p.D = D; p.block_rows = block_rows;
+  p.sm_scale = sm_scale; p.beta = expcast_beta; p.flags = flags;
+  p.out = out; p.out_dtype = out_dtype; p.osb = out_sb; p.osh = out_sh; p.osn = out_sn;
+  p.kv_split = kv_split;
+  const size_t need = attn_tc_split_bytes(p);
+  if (need > 0) {
+    VC_CHECK(workspace != nullptr && workspace_bytes >= need && aligned16(workspace),
+             "vcattn_attn_fp8_split: workspace missing, unaligned or smaller than "
+             "vcattn_attn_split_workspace_bytes()");
+    p.part = workspace;
+  }
+  const cudaError_t e = launch_attn_tc(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(VCATTN_ERR_CUDA,
+                std::string("vcattn_attn_fp8_split: ") + cudaGetErrorString(e) + " [" + attn_tc_diag() + "]");
+  return VCATTN_OK;
+}
+
 int vcattn_attn_fp8_masked(const uint8_t* q8, const float* q_scale, const uint8_t* k8, const float* k_scale,
                            const uint8_t* v8, const float* v_scale, const float* mu, const int32_t* kv_len, int B,
                            int H, int N, int n_pad, int D, int block_rows, float sm_scale, int flags,

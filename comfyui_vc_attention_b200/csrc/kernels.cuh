@@ -69,6 +69,11 @@ struct AttnParams {
   int out_dtype;
   int64_t osb, osh, osn;
   const int32_t* kv_len;   // (B,) keys taking part per batch entry (dense tcgen05 kernel), or nullptr
+  // dense tcgen05 kernel, KV split of query tiles: 0 = the last partial wave
+  // of CTAs (auto), 1 = none, k >= 2 = every query tile in k pieces; the
+  // partials go to `part` (attn_tc_split_bytes bytes)
+  int kv_split;
+  void* part;
 };
 
 size_t prepare_workspace_bytes(int G, int N, int D);
@@ -97,6 +102,7 @@ cudaError_t attn_tc_status(int* code, int* where, int* block, bool reset);
 const char* attn_tc_diag();
 // Bounded-wait test hook of the dense tcgen05 kernel (vcattn_inject_stall).
 void set_attn_tc_stall(int tile);
+size_t attn_tc_split_bytes(const AttnParams& p);
 cudaError_t launch_attn_sparse_mma(const AttnParams& p, cudaStream_t st);
 bool attn_sparse_tc_supported(const AttnParams& p);
 cudaError_t launch_attn_sparse_tc(const AttnParams& p, cudaStream_t st);

@@ -92,6 +92,11 @@ _SIGNATURES = {
     "vcattn_attn_fp8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_double,
                                 c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p]),
+    "vcattn_attn_split_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int, c_int]),
+    "vcattn_attn_fp8_split": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_double,
+                                      c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_void_p, c_size_t,
+                                      c_void_p]),
     "vcattn_attn_fp8_masked": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                        c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_int,
                                        c_double, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p]),

@@ -19,7 +19,7 @@ Per call (all on the current CUDA stream, no host synchronisation):
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 from typing import NamedTuple, Optional
 
 import torch
@@ -46,6 +46,12 @@ class TritonConfig:
     expcast_exact  (this build) with enable_expcast, the dense tcgen05 kernel
                 evaluates ExpCast in expcast.py's operation order instead of
                 the one-FMA form (slower; for parity runs).
+    kv_split    (this build) dense tcgen05 kernel: 1 = no split (default),
+                0 = split the query tiles of a last partial wave of CTAs over
+                their KV tiles when that wave would fill at most half of the
+                SMs, k >= 2 = every query tile in k KV pieces
+                (vcattn_attn_fp8_split; split tiles round P relative to each
+                piece's own max).
     """
     block_m: int = 64
     block_n: int = 128
@@ -61,6 +67,7 @@ class TritonConfig:
     sink_blocks: int = 0
     group: int = 16
     expcast_exact: bool = False
+    kv_split: int = 1
 
 
 class Prepared(NamedTuple):
@@ -371,13 +378,14 @@ def _attention_into(q, k, v, perm, cfg, scale, out, kv_len=None):
 
 def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
                        cfg: TritonConfig, kernel: str = "auto",
-                       kv_len: Optional[torch.Tensor] = None) -> torch.Tensor:
+                       kv_len: Optional[torch.Tensor] = None, kv_split: Optional[int] = None) -> torch.Tensor:
     """Run the attention kernel on prepared operands, writing into ``out``.
 
     kernel: "tc" (tcgen05, needs ``p.v``), "mma" (register MMA,
     needs ``p.v_t``) or "auto" (tcgen05 whenever it applies), for the dense
     and the sparse path alike.  ``kv_len`` ((B,) int32 on the device) runs
     the key-padding masked dense tcgen05 kernel (vcattn_attn_fp8_masked).
+    ``kv_split`` overrides ``cfg.kv_split`` for the dense tcgen05 kernel.
     """
     lib = N.lib()
     b, h, n_pad, d = (p.q if p.q is not None else p.v).shape
@@ -440,11 +448,21 @@ def attention_prepared(p: Prepared, n: int, out: torch.Tensor, scale: float,
     if kernel == "tc":
         if p.v is None or p.v_mma_order:
             raise ValueError("the dense tcgen05 kernel reads V codes in token order (want_v=True, v_mma_order=False)")
-        N.check("vcattn_attn_fp8", lib.vcattn_attn_fp8(
-            q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
-            p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), b, h, n, n_pad, d,
-            p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
-            out.stride(0), out.stride(1), out.stride(2), st))
+        split = cfg.kv_split if kv_split is None else int(kv_split)
+        ws_bytes = lib.vcattn_attn_split_workspace_bytes(b, h, n, n_pad, d, p.block_rows, split)
+        if ws_bytes == 0:
+            N.check("vcattn_attn_fp8", lib.vcattn_attn_fp8(
+                q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
+                p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), b, h, n, n_pad, d,
+                p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
+                out.stride(0), out.stride(1), out.stride(2), st))
+        else:
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=out.device)
+            N.check("vcattn_attn_fp8_split", lib.vcattn_attn_fp8_split(
+                q8.data_ptr(), p.q_scale.data_ptr(), k8.data_ptr(), p.k_scale.data_ptr(),
+                p.v.view(torch.uint8).data_ptr(), p.v_scale.data_ptr(), p.mu.data_ptr(), b, h, n, n_pad, d,
+                p.block_rows, float(scale), flags, float(cfg.expcast_beta), out.data_ptr(), odt,
+                out.stride(0), out.stride(1), out.stride(2), split, ws.data_ptr(), ws_bytes, st))
     else:
         if p.v_t is None:
             raise ValueError("the register-MMA kernel needs the block-transposed V codes (want_v_t=True)")
@@ -537,6 +555,9 @@ def vc_attention_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if out.shape != q.shape or out.dtype != q.dtype or out.is_cuda or not out.is_contiguous():
         raise ValueError("out must be a contiguous host tensor of q's shape and dtype")
     c = chunk_heads or max(1, -(-g // 14))   # ~14 chunks: the copies dominate, keep the pipe full
+    # chunks overlap one another, so no chunk's last wave is the call's tail:
+    # no KV split (the output equals per-unit device calls bit for bit)
+    cfg = replace(cfg, kv_split=1)
     if scale is None:
         scale = d ** -0.5
     src = [t.reshape(g, n, d) for t in (q, k, v)]

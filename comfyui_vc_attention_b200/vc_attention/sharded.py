@@ -167,8 +167,10 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                     _compute_units(q, k, v, perm, lo, hi, compute, slab[: hi - lo], cfg, scale)
                 else:
                     from .kernels.cuda_attn import _call_config, attention_prepared
+                    # rounds overlap one another: no KV split of a round's last
+                    # wave (each unit equals its single-GPU call bit for bit)
                     attention_prepared(preps(i), n, slab[: hi - lo].unsqueeze(0), scale if scale else d ** -0.5,
-                                       _call_config(cfg, d))
+                                       _call_config(cfg, d), kv_split=1)
                 mine.append(slab[: hi - lo])
             if gather:
                 # every rank issues every round, in the same order, with equal

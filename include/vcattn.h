@@ -231,6 +231,29 @@ VCATTN_API int vcattn_attn_fp8(const uint8_t* q8, const float* q_scale, const ui
                     void* out, int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn,
                     void* stream);
 
+/* ---- the same with query tiles split over their KV tiles (no counterpart in
+ * the reference).  A split query tile runs as several CTAs, each over a
+ * contiguous range of its KV tiles with its own running max, and a second
+ * kernel combines the partials (O = sum w_p O_p / sum w_p l_p, w_p =
+ * exp2(m_p - max m)).  kv_split 0 (auto): only when the CTAs would end in a
+ * partial wave holding at most half of the SMs are that wave's query tiles
+ * split, so the last wave takes a fraction of a CTA's time; 1: no split
+ * (identical to vcattn_attn_fp8); k >= 2: every query tile in k pieces (at
+ * most 32).  Split tiles round their P bytes relative to each piece's own
+ * maximum, so their output differs from the unsplit kernel's at the level of
+ * the FP8 rounding; unsplit tiles are bit-identical to vcattn_attn_fp8.
+ * workspace: at least vcattn_attn_split_workspace_bytes() bytes, 16-byte
+ * aligned (may be null when that is 0); the plan depends on the current
+ * device's SM count. */
+VCATTN_API size_t vcattn_attn_split_workspace_bytes(int B, int H, int N, int n_pad, int D,
+                                                    int block_rows, int kv_split);
+VCATTN_API int vcattn_attn_fp8_split(const uint8_t* q8, const float* q_scale, const uint8_t* k8,
+                          const float* k_scale, const uint8_t* v8, const float* v_scale,
+                          const float* mu, int B, int H, int N, int n_pad, int D,
+                          int block_rows, float sm_scale, int flags, double expcast_beta,
+                          void* out, int out_dtype, int64_t out_sb, int64_t out_sh, int64_t out_sn,
+                          int kv_split, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- masked (key-padding) dense FP8 attention: reference.py:162-294 with
  * valid_len (keys at positions >= valid_len masked out), per batch entry.
  * The reference applies valid_len to the permuted key order, after

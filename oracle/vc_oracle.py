@@ -622,7 +622,8 @@ def _row_starts(n: int, block_m: int, row_blocks: Optional[Sequence[int]]):
 def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_m: int,
                     sm_scale: float, expcast: bool = False, beta: float = -0.35,
                     row_blocks: Optional[Sequence[int]] = None,
-                    kv_len: Optional[Sequence[int]] = None) -> np.ndarray:
+                    kv_len: Optional[Sequence[int]] = None,
+                    kv_piece_tiles: Optional[int] = None) -> np.ndarray:
     """The fused kernel's arithmetic in code units (triton_attn.py:203-322):
     s = dot(q8,k8) * (qs*ks) * sm_scale ; P as E4M3 (exp2*448 cast or ExpCast);
     r = sum(P)/448 ; acc = alpha*acc + (P@V8)*vs/448 + r*mu*vs ; O = acc/l.
@@ -631,6 +632,11 @@ def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_
     ``kv_len`` (G,): per head, only keys below it take part (key padding,
     reference.py valid_len); KV tiles entirely past it are not visited, which
     leaves every value as if they had been visited with all keys masked.
+    ``kv_piece_tiles`` (this build's split of the KV axis, no counterpart in
+    the reference): the KV tiles run in pieces of that many tiles, each piece
+    from a fresh running max, sum and accumulator (its P bytes relative to its
+    own max), and the pieces combine as O = sum_p w_p acc_p / sum_p w_p l_p
+    with w_p = exp2((m_p - max_p m_p) log2e).
     """
     q8 = e4m3_decode(prep["q"])
     k8 = e4m3_decode(prep["k"])
@@ -643,17 +649,32 @@ def attention_codes(prep: Dict[str, np.ndarray], n: int, block_rows: int, block_
         for _, sm in _row_starts(n, block_m, row_blocks):
             em = min(n, sm + block_m)
             rows = em - sm
-            m_i = np.full(rows, -np.inf, np.float32)
-            l_i = np.zeros(rows, np.float32)
-            acc = np.zeros((rows, d), np.float32)
             kv = n if kv_len is None else max(1, min(n, int(kv_len[gi])))
-            for j in range(-(-kv // block_rows)):
-                js, je = j * block_rows, (j + 1) * block_rows
-                m_i, l_i, acc = _exact_tile(
-                    q8[gi, sm:em], qs[gi, sm:em], k8[gi, js:je], ks[gi, js:je], v8[gi, js:je],
-                    vs[gi, j], mu[gi, j], np.arange(js, je) < kv, sm_scale, m_i, l_i, acc,
-                    expcast, beta)
-            out[gi, sm:em] = acc / l_i[:, None]
+            tiles = -(-kv // block_rows)
+            step = tiles if kv_piece_tiles is None else int(kv_piece_tiles)
+            parts = []
+            for j0 in range(0, tiles, step):
+                m_i = np.full(rows, -np.inf, np.float32)
+                l_i = np.zeros(rows, np.float32)
+                acc = np.zeros((rows, d), np.float32)
+                for j in range(j0, min(tiles, j0 + step)):
+                    js, je = j * block_rows, (j + 1) * block_rows
+                    m_i, l_i, acc = _exact_tile(
+                        q8[gi, sm:em], qs[gi, sm:em], k8[gi, js:je], ks[gi, js:je], v8[gi, js:je],
+                        vs[gi, j], mu[gi, j], np.arange(js, je) < kv, sm_scale, m_i, l_i, acc,
+                        expcast, beta)
+                parts.append((m_i, l_i, acc))
+            if len(parts) == 1:
+                out[gi, sm:em] = acc / l_i[:, None]
+                continue
+            mx = np.max(np.stack([pm for pm, _, _ in parts]), axis=0)
+            num = np.zeros((rows, d), np.float64)
+            den = np.zeros(rows, np.float64)
+            for pm, pl, pa in parts:
+                w = np.exp2((pm.astype(np.float64) - mx) * LOG2E)
+                num += w[:, None] * pa
+                den += w * pl
+            out[gi, sm:em] = (num / den[:, None]).astype(np.float32)
     return out
 
 

@@ -758,7 +758,8 @@ def test_full_size_sparse_keep_all_equals_dense(dev):
     del ps
     pd = prepare(qt, kt, vt, pt, block_rows=128, want_v=True)
     o_d = torch.empty_like(o_s)
-    attention_prepared(pd, FULL_N, o_d, sc, TritonConfig(block_n=128, enable_expcast=True), kernel="tc")
+    attention_prepared(pd, FULL_N, o_d, sc, TritonConfig(block_n=128, enable_expcast=True), kernel="tc",
+                       kv_split=1)
     torch.cuda.synchronize()
     assert attention_status() == (0, 0, 0)
     assert torch.equal(o_s, o_d)
