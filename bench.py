@@ -77,6 +77,12 @@ WORKLOADS = {
     "c2l": dict(desc="configs[2] at N=65536: block-sparse FP8 VC-Attention, tau=1.3, B1 H56 N65536 D128 on a "
                      "64x32x32 grid, ExpCast on, V-Smooth k=512", B=1, H=56, N=65536, D=128, expcast=True,
                 sparse=True, k=512, block_rows=128, spatial=(64, 32, 32), tau=1.3),
+    "c2b64": dict(desc="configs[2] with 64-key value blocks: block-sparse FP8 VC-Attention, tau=1.3, B1 H56 "
+                       "N16384 D128 on a 16x32x32 grid, block_rows 64, ExpCast on, V-Smooth k=64", B=1, H=56,
+                  N=16384, D=128, expcast=True, sparse=True, k=64, block_rows=64, spatial=(16, 32, 32), tau=1.3),
+    "c2d64": dict(desc="configs[2] with head dim 64 at the same width: block-sparse FP8 VC-Attention, tau=1.3, "
+                       "B1 H112 N16384 D64 on a 16x32x32 grid, ExpCast on, V-Smooth k=64", B=1, H=112, N=16384,
+                  D=64, expcast=True, sparse=True, k=64, block_rows=128, spatial=(16, 32, 32), tau=1.3),
     "c2": dict(desc="configs[2]: block-sparse FP8 VC-Attention, tau=1.3, B1 H56 N16384 D128 on a 16x32x32 "
                     "grid, ExpCast on, V-Smooth k=64", B=1, H=56, N=16384, D=128, expcast=True, sparse=True,
                k=64, block_rows=128, spatial=(16, 32, 32), tau=1.3),
