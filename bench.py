@@ -502,6 +502,9 @@ def main() -> int:
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent full-size replicas per rank instead of the sharded split")
     ap.add_argument("--no-psnr", action="store_true")
+    ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "mma"],
+                    help="attention kernel of the timed device step: tcgen05, the register-MMA comparison "
+                         "kernel, or auto (tcgen05 wherever it applies)")
     ap.add_argument("--kv-split", type=int, default=1,
                     help="dense kernel KV split: 1 = none, 0 = the last partial wave (auto), k = k pieces")
     ap.add_argument("--eager", action="store_true", help="N > 1: launch every round eagerly (no CUDA graph)")
@@ -558,7 +561,7 @@ def main() -> int:
     # tcgen05 kernels read V in their key order; the register-MMA sparse
     # kernel (other shapes) reads the block-transposed copy.
     sparse_tc = cfg.sparse and sparse_tc_applies(D, w["block_rows"], cfg.block_m, cfg.group, NT)
-    want_v = (not cfg.sparse) or sparse_tc
+    want_v = ((not cfg.sparse) or sparse_tc) and args.kernel != "mma"
 
     def step(evs=None):
         if evs is not None:
@@ -569,7 +572,7 @@ def main() -> int:
                     sink_blocks=cfg.sink_blocks, qk_fp4=cfg.qk_fp4, fp8_qk=not cfg.qk_fp4)
         if evs is not None:
             evs[1].record()
-        attention_prepared(p, NT, out, scale, cfg)
+        attention_prepared(p, NT, out, scale, cfg, kernel=args.kernel)
         if evs is not None:
             evs[2].record()
         return p
@@ -689,6 +692,7 @@ def main() -> int:
         "data": "synthetic (seeded configs[1] distributions, generated on device)",
         "config": {"workload": w["desc"], "B": B, "H": H, "N": NT, "D": D, "block_rows": w["block_rows"],
                    "kmeans_k": res.k, "expcast": w["expcast"], "sparse": w["sparse"], "kv_split": args.kv_split,
+                   "kernel": args.kernel,
                    "parallelism": (f"(batch, head) units x{world} ranks, independent replicas, no collective"
                                    if world > 1 else "one GPU"),
                    "l2": "inputs larger than L2 (Q/K/V 235 MB each)",
@@ -698,9 +702,10 @@ def main() -> int:
         "ms_prepare": prep_ms, "ms_attention": attn_ms, "kmeans_ms": kmeans_ms, "psnr_db": psnr,
         "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": fp8_peak, "unit": "TFLOP/s",
                      "frac": attn_tflops / fp8_peak, "traffic": traffic,
-                     "kernel": ("attn_tc_sparse_kernel (tcgen05, tau-routed)" if sparse_tc
+                     "kernel": ("attn_tc_sparse_kernel (tcgen05, tau-routed)" if sparse_tc and want_v
                                 else "attn_sparse_kernel (mma.sync, tau-routed)" if w["sparse"]
                                 else "attn_tc_kernel<NVFP4 QK> (tcgen05 mxf4nvf4 + f8f6f4)" if w.get("qk_fp4")
+                                else "attn_mma_kernel (mma.sync comparison kernel)" if args.kernel == "mma"
                                 else "attn_tc_kernel (tcgen05)"),
                      "flops": ("executed (kept tiles + proxy)" if w["sparse"] else "dense"),
                      "peak_note": f"dense FP8 = 2 x {peak_kind} bf16 burst ({peaks.get('bf16_tflops')} TF/s)"},
