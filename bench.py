@@ -23,7 +23,10 @@ the workload (weak scaling, no collective).
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle
 restatement of vc_attention_reference, oracle/) on the host cores on a
-bounded sample of the same workload, extrapolated by rows and heads.
+bounded sample of the same workload (one head x a block of query rows per
+step, timed as it runs), and reports beside it the committed timing of the
+reference's own code against that restatement on the same inputs
+(oracle/reference_cpu_calibration.json).
 """
 
 from __future__ import annotations
@@ -247,29 +250,49 @@ def cpu_sample(w, q_rows, seed=0):
     return dt, dt * scale * 1e3
 
 
+def reference_calibration():
+    """oracle/reference_cpu_calibration.json: the reference's own CPU code
+    timed against this port on the same one-head inputs (made where the
+    reference is importable by oracle/calibrate_reference.py), or None."""
+    try:
+        with open(os.path.join(ROOT, "oracle", "reference_cpu_calibration.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
 def run_reference_arm(args, w, rank):
+    """The reference's CPU algorithm on the host cores: each step is one head x
+    cpu_rows query rows x all N keys of the workload (prepare of that head
+    included), timed as it runs; ``value`` is that sample's attention FLOPs
+    over its time, the same rate a whole call would run at (every head and
+    query row block costs the same)."""
     if rank != 0:
         return 0
     cores = os.cpu_count() or 1
     q_rows = args.cpu_rows
     for _ in range(args.warmup):
         cpu_sample(w, q_rows)
-    times = []
+    secs, extrap = [], []
     for i in range(args.steps):
-        _, ms = cpu_sample(w, q_rows, seed=i)
-        times.append(ms)
-    ms = statistics.mean(times)
-    val = flops_per_call(w) / (ms / 1e3) / 1e12
+        dt, ms = cpu_sample(w, q_rows, seed=i)
+        secs.append(dt)
+        extrap.append(ms)
+    dt = statistics.mean(secs)
+    ms_call = statistics.mean(extrap)
+    val = 4.0 * q_rows * float(w["N"]) * w["D"] / dt / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 (fp32 accumulate, CPU emulation)",
         "data": "synthetic (seeded configs[1] distributions)",
         "config": {"workload": w["desc"], "q_rows_sampled": q_rows, "heads_sampled": 1},
+        "ms_per_call_extrapolated": ms_call,
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"oracle vc_attention_reference, 1 head x {q_rows} query rows x "
-                                   f"{w['N']} keys per step, extrapolated x{w['B'] * w['H']} heads x "
-                                   f"{w['N'] // q_rows} row blocks"},
+                                   f"{w['N']} keys per step (a full call is {w['B'] * w['H']} heads x "
+                                   f"{w['N'] // q_rows} such blocks: {ms_call / 1e3:.0f} s)",
+                         "reference_calibration": reference_calibration()},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -723,7 +746,8 @@ def main() -> int:
             "value": fl / (ms_cpu / 1e3) / 1e12, "unit": UNIT, "cores": os.cpu_count() or 1,
             "kind": "port", "ms_per_call_extrapolated": ms_cpu, "sample_seconds": dt,
             "sample": f"oracle vc_attention_reference, 1 head x {args.cpu_rows} query rows x {NT} keys, "
-                      f"extrapolated x{G} heads x {NT // args.cpu_rows} row blocks"}
+                      f"extrapolated x{G} heads x {NT // args.cpu_rows} row blocks",
+            "reference_calibration": reference_calibration()}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
