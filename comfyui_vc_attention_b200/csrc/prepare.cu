@@ -112,8 +112,18 @@ __global__ void kmean_final_kernel(const double* __restrict__ partial, int nchun
                                    float* __restrict__ kmean) {
   const int g = blockIdx.x, d = threadIdx.x;
   if (d >= D) return;
+  // chunks in order, eight loads in flight at a time
+  const double* pp = partial + static_cast<int64_t>(g) * nchunks * D + d;
   double tot = 0.0;
-  for (int c = 0; c < nchunks; ++c) tot += partial[(static_cast<int64_t>(g) * nchunks + c) * D + d];
+  int c = 0;
+  for (; c + 8 <= nchunks; c += 8) {
+    double x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] = pp[static_cast<int64_t>(c + u) * D];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) tot += x[u];
+  }
+  for (; c < nchunks; ++c) tot += pp[static_cast<int64_t>(c) * D];
   kmean[g * D + d] = __fdiv_rn(__double2float_rn(tot), static_cast<float>(N));
 }
 
@@ -231,6 +241,281 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(QKArgs a) {
                                 static_cast<float>(a.rows));
     if (want_qbar) a.blk_qbar[o] = __double2float_rn(reduce_lanes<D>(red_q, nwarps, d));
   }
+}
+
+// ---------------------------------------------------------------------------
+// Head dim 128 with four lanes per row.  Lane 4 s + c of a warp owns channels
+// 32 c .. 32 c + 31 of the warp's row s (eight rows per warp at a time), so
+// the butterfly strides 1 .. 16 run inside the lane and only strides 32 and
+// 64 cross lanes (partners lane ^ 1 and lane ^ 2): 8 warp shuffles per row
+// instead of 25, the row maximum reduces over four lanes, and the E4M3 row
+// scale and its reciprocal are divided out by four lanes instead of 32.  The
+// butterfly pairs, their order and every rounding are those of fwht128_warp
+// (hadamard.py:37-65), so the bytes are identical.
+// ---------------------------------------------------------------------------
+
+// 32 consecutive input elements (16-byte aligned) -> float.
+template <int DT>
+__device__ __forceinline__ void load32(const void* base, int64_t off, float v[32]) {
+  if constexpr (DT == VCATTN_DTYPE_F32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + off);
+    float4 x[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) x[q] = p[q];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      v[4 * q] = x[q].x; v[4 * q + 1] = x[q].y; v[4 * q + 2] = x[q].z; v[4 * q + 3] = x[q].w;
+    }
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + off);
+    uint4 x[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) x[q] = p[q];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w[4] = {x[q].x, x[q].y, x[q].z, x[q].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if constexpr (DT == VCATTN_DTYPE_BF16) {
+          v[8 * q + 2 * e] = __uint_as_float(w[e] << 16);
+          v[8 * q + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+          v[8 * q + 2 * e] = f.x;
+          v[8 * q + 2 * e + 1] = f.y;
+        }
+      }
+    }
+  }
+}
+
+// Walsh-Hadamard transform of a 128-wide row over the four lanes that hold
+// it (32 consecutive elements each), then the IEEE division by
+// fp32(sqrt(128)) (Markstein's correction on the values where it equals the
+// division, as in fwht128_warp; the choice of path is per lane, which gives
+// the same quotients).
+__device__ __forceinline__ void fwht128_quad(float v[32], int lane) {
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if ((i & h) == 0) {
+        const float x = v[i], y = v[i + h];
+        v[i] = __fadd_rn(x, y);
+        v[i + h] = __fsub_rn(x, y);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 1; m <= 2; m <<= 1) {
+    // lower lane: v + p, upper lane: p - v, as one fma with a +-1 multiplier
+    const float sg = (lane & m) ? -1.0f : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float p = __shfl_xor_sync(0xffffffffu, v[i], m);
+      v[i] = __fmaf_rn(sg, v[i], p);
+    }
+  }
+  const float r = 11.313708498984761f;
+  const float y = 0.0883883461356163f;
+  float lo = fabsf(v[0]), hi = fabsf(v[0]);
+#pragma unroll
+  for (int i = 1; i < 31; i += 2) {
+    lo = fmin3(lo, fabsf(v[i]), fabsf(v[i + 1]));
+    hi = fmax3(hi, fabsf(v[i]), fabsf(v[i + 1]));
+  }
+  lo = fminf(lo, fabsf(v[31]));
+  hi = fmaxf(hi, fabsf(v[31]));
+  if (!(lo >= 0x1p-100f && hi <= 0x1p+100f)) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __fdiv_rn(v[i], r);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float q0 = __fmul_rn(v[i], y);
+      v[i] = __fmaf_rn(__fmaf_rn(-q0, r, v[i]), y, q0);
+    }
+  }
+}
+
+// Q / K rows (D = 128): the work of quant_rows_kernel in the four-lane
+// layout.  A CTA still covers `rows` consecutive output rows; it takes them
+// 64 at a time (eight warps x eight rows).  With STATS the rotated rows (and
+// for Q the dequantised fp32(q8 * fp32(qs * sm))) of each 64-row pass go
+// through shared memory, where one thread per channel adds them in float64.
+template <int DT, bool STATS>
+__global__ void __launch_bounds__(256, 3) quant_rows4_kernel(QKArgs a) {
+  constexpr int D = 128;
+  constexpr int kPad = D + 4;
+  const int g = blockIdx.y;
+  const int b = g / a.H, h = g % a.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slot = lane >> 2, c = lane & 3;
+  const int r0 = blockIdx.x * a.rows;
+  const bool want_mean = STATS && a.blk_mean != nullptr;
+  const bool want_qbar = STATS && a.blk_qbar != nullptr;
+  extern __shared__ float stat_sm[];   // STATS: [64][kPad] rows, then [64][kPad] q-bar terms
+  __shared__ float km_sm[D];
+  __shared__ double half_sm[2][D];
+  double msum = 0.0, qsum = 0.0;       // thread d < 128: channel d of the CTA's block
+  if (a.kmean != nullptr && threadIdx.x < D) km_sm[threadIdx.x] = a.kmean[g * D + threadIdx.x];
+  __syncthreads();
+  for (int p0 = 0; p0 < a.rows; p0 += 64) {
+    const int rl = p0 + warp * 8 + slot;
+    const int t = r0 + rl;
+    const bool mine = rl < a.rows && t < a.n_pad;
+    const bool real = mine && t < a.N;
+    float v[32];
+    if (real) {
+      const int src = source_row(a.perm, a.perm_rows, g, a.N, t);
+      load32<DT>(a.x.data, b * a.x.sb + h * a.x.sh + static_cast<int64_t>(src) * a.x.sn + 32 * c, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    }
+    if (a.flags & VCATTN_HADAMARD) fwht128_quad(v, lane);
+    if (real && a.kmean != nullptr) {
+      const float4* km = reinterpret_cast<const float4*>(km_sm + 32 * c);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 m = km[q];
+        v[4 * q] = __fsub_rn(v[4 * q], m.x);
+        v[4 * q + 1] = __fsub_rn(v[4 * q + 1], m.y);
+        v[4 * q + 2] = __fsub_rn(v[4 * q + 2], m.z);
+        v[4 * q + 3] = __fsub_rn(v[4 * q + 3], m.w);
+      }
+    }
+    if (!real) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    }
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) am = fmax3(am, fabsf(v[i]), fabsf(v[i + 1]));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    uint32_t pk[8];
+    float sc = 0.f;
+    if (real) {
+      sc = e4m3_row_scale(am);
+      const DivBy div(sc);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        pk[q] = e4m3x4(div(v[4 * q]), div(v[4 * q + 1]), div(v[4 * q + 2]), div(v[4 * q + 3]));
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) pk[q] = 0u;
+    }
+    if (mine) {
+      uint4* dst = reinterpret_cast<uint4*>(a.codes + (static_cast<int64_t>(g) * a.n_pad + t) * D + 32 * c);
+      dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      if (c == 0) a.scale[static_cast<int64_t>(g) * a.n_pad + t] = sc;
+    }
+    if constexpr (STATS) {
+      if (want_mean || want_qbar) {
+        float* row_m = stat_sm + (warp * 8 + slot) * kPad + 32 * c;
+        float* row_q = row_m + 64 * kPad;
+        if (want_mean) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(row_m + 4 * q) =
+                mine ? make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (want_qbar) {
+          const float w = __fmul_rn(sc, a.sm_scale);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (real)
+              f = make_float4(__fmul_rn(e4m3_to_float(pk[q] & 0xff), w), __fmul_rn(e4m3_to_float((pk[q] >> 8) & 0xff), w),
+                              __fmul_rn(e4m3_to_float((pk[q] >> 16) & 0xff), w),
+                              __fmul_rn(e4m3_to_float(pk[q] >> 24), w));
+            *reinterpret_cast<float4*>(row_q + 4 * q) = f;
+          }
+        }
+        __syncthreads();
+        // all 256 threads: channel d = tid % 128, rows 32 (tid / 128) .. + 31
+        // with four accumulators, then the two halves
+        const int d = threadIdx.x & (D - 1), hr = (threadIdx.x >> 7) * 32;
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          if (which == 0 ? !want_mean : !want_qbar) continue;
+          const float* col = stat_sm + (which * 64 + hr) * kPad + d;
+          double s4[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+          for (int r = 0; r < 32; r += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) s4[u] += static_cast<double>(col[(r + u) * kPad]);
+          }
+          half_sm[threadIdx.x >> 7][d] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+          __syncthreads();
+          if (threadIdx.x < D) {
+            const double part = half_sm[0][d] + half_sm[1][d];
+            if (which == 0) msum += part; else qsum += part;
+          }
+          __syncthreads();
+        }
+      }
+    }
+  }
+  if constexpr (STATS) {
+    if (threadIdx.x < D && (want_mean || want_qbar)) {
+      const int64_t o = (static_cast<int64_t>(g) * gridDim.x + blockIdx.x) * D + threadIdx.x;
+      if (want_mean) a.blk_mean[o] = __fdiv_rn(__double2float_rn(msum), static_cast<float>(a.rows));
+      if (want_qbar) a.blk_qbar[o] = __double2float_rn(qsum);
+    }
+  }
+}
+constexpr size_t kStatSmem4 = 2 * 64 * (128 + 4) * sizeof(float);
+
+// K token mean (D = 128) in the four-lane layout: 256 rows per CTA in four
+// passes of 64.  Each pass's rotated rows go through shared memory, where all
+// 256 threads add them in float64: thread i takes channel i % 128 of rows
+// 32 (i / 128) .. + 31 with four accumulators, kept across the passes; the
+// two halves are added at the end.
+template <int DT>
+__global__ void __launch_bounds__(256, 3) kmean_partial4_kernel(vcattn_bhnd k, int H, int N, int flags,
+                                                                 double* __restrict__ partial) {
+  constexpr int D = 128;
+  constexpr int kPad = D + 4;
+  __shared__ float rows_sm[64 * kPad];
+  __shared__ double half_sm[2][D];
+  const int g = blockIdx.y, chunk = blockIdx.x;
+  const int b = g / H, h = g % H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slot = lane >> 2, c = lane & 3;
+  const int d = threadIdx.x & (D - 1), hr = (threadIdx.x >> 7) * 32;
+  const int t0 = chunk * kChunkRows;
+  double s4[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int p0 = 0; p0 < kChunkRows; p0 += 64) {
+    const int t = t0 + p0 + warp * 8 + slot;
+    float v[32];
+    if (t < N) {
+      load32<DT>(k.data, b * k.sb + h * k.sh + static_cast<int64_t>(t) * k.sn + 32 * c, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    }
+    if (flags & VCATTN_HADAMARD) fwht128_quad(v, lane);
+    float* row = rows_sm + (warp * 8 + slot) * kPad + 32 * c;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4*>(row + 4 * q) =
+          t < N ? make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncthreads();
+    const float* col = rows_sm + hr * kPad + d;
+#pragma unroll
+    for (int r = 0; r < 32; r += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s4[u] += static_cast<double>(col[(r + u) * kPad]);
+    }
+    __syncthreads();
+  }
+  half_sm[threadIdx.x >> 7][d] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+  __syncthreads();
+  if (threadIdx.x < D)
+    partial[(static_cast<int64_t>(g) * gridDim.x + chunk) * D + d] = half_sm[0][d] + half_sm[1][d];
 }
 
 // ---------------------------------------------------------------------------
@@ -617,6 +902,24 @@ size_t prepare_workspace_bytes(int G, int N, int D) {
          2 * static_cast<size_t>(G) * sizeof(unsigned) + 256;
 }
 
+// The Q / K row pass: the four-lane kernel for D = 128, the warp-per-row
+// kernel for D = 64.
+template <int DT, int D>
+static void launch_rows(const QKArgs& a, dim3 grid, bool stats, cudaStream_t st) {
+  if constexpr (D == 128) {
+    if (stats) {
+      cudaFuncSetAttribute(quant_rows4_kernel<DT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kStatSmem4));
+      quant_rows4_kernel<DT, true><<<grid, 256, kStatSmem4, st>>>(a);
+    } else {
+      quant_rows4_kernel<DT, false><<<grid, 256, 0, st>>>(a);
+    }
+  } else {
+    if (stats) quant_rows_kernel<DT, D, true><<<grid, 256, 0, st>>>(a);
+    else quant_rows_kernel<DT, D, false><<<grid, 256, 0, st>>>(a);
+  }
+}
+
 template <int DT, int D>
 static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
   const int G = p.B * p.H;
@@ -626,7 +929,8 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
     const int nchunks = (p.N + kChunkRows - 1) / kChunkRows;
     double* partial = reinterpret_cast<double*>(p.workspace);
     kmean = reinterpret_cast<float*>(partial + static_cast<size_t>(G) * nchunks * D);
-    kmean_partial_kernel<DT, D><<<dim3(nchunks, G), 256, 0, st>>>(*p.k, p.H, p.N, p.flags, partial);
+    if constexpr (D == 128) kmean_partial4_kernel<DT><<<dim3(nchunks, G), 256, 0, st>>>(*p.k, p.H, p.N, p.flags, partial);
+    else kmean_partial_kernel<DT, D><<<dim3(nchunks, G), 256, 0, st>>>(*p.k, p.H, p.N, p.flags, partial);
     kmean_final_kernel<D><<<G, D, 0, st>>>(partial, nchunks, p.N, kmean);
   }
   const bool route = p.route != nullptr;
@@ -641,8 +945,7 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
     a.blk_qbar = route ? p.route->q_bar : nullptr;
     a.sm_scale = route ? p.route->sm_scale : 0.f;
     const int grid_x = (p.n_pad + a.rows - 1) / a.rows;
-    if (route) quant_rows_kernel<DT, D, true><<<dim3(grid_x, G), 256, 0, st>>>(a);
-    else quant_rows_kernel<DT, D, false><<<dim3(grid_x, G), 256, 0, st>>>(a);
+    launch_rows<DT, D>(a, dim3(grid_x, G), route, st);
   }
   // K rows (gathered by perm)
   if (p.k8 != nullptr) {
@@ -653,8 +956,7 @@ static cudaError_t prepare_impl(const PrepareParams& p, cudaStream_t st) {
     a.rows = p.block_rows;
     a.blk_mean = route ? p.route->k_mean : nullptr;
     a.blk_qbar = nullptr;
-    if (route) quant_rows_kernel<DT, D, true><<<dim3(nb, G), 256, 0, st>>>(a);
-    else quant_rows_kernel<DT, D, false><<<dim3(nb, G), 256, 0, st>>>(a);
+    launch_rows<DT, D>(a, dim3(nb, G), route, st);
   }
   // V blocks
   {

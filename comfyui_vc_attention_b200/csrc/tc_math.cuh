@@ -42,11 +42,6 @@ __device__ __forceinline__ void add2(float& a, float& b, float x, float y) {
       : "+f"(a), "+f"(b)
       : "f"(x), "f"(y));
 }
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
 __device__ __forceinline__ float fma_sat(float a, float b, float c) {
   float d;
   asm("fma.rn.sat.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
