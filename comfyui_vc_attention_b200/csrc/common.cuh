@@ -81,6 +81,14 @@ __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
   return static_cast<uint32_t>(e4m3x2(a, b)) | (static_cast<uint32_t>(e4m3x2(c, d)) << 16);
 }
 
+// Four E4M3 codes of a word (byte i = element i) -> their exact values.
+__device__ __forceinline__ float4 e4m3x4_to_float4(uint32_t w) {
+  const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w & 0xffffu), __NV_E4M3);
+  const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w >> 16), __NV_E4M3);
+  return make_float4(__half2float(__half(__half_raw{lo.x})), __half2float(__half(__half_raw{lo.y})),
+                     __half2float(__half(__half_raw{hi.x})), __half2float(__half(__half_raw{hi.y})));
+}
+
 // E4M3 byte -> float (exact).
 __device__ __forceinline__ float e4m3_to_float(uint32_t code) {
   const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(code & 0xff), __NV_E4M3);

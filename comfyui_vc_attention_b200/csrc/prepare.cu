@@ -427,10 +427,10 @@ __global__ void __launch_bounds__(256, 3) quant_rows4_kernel(QKArgs a) {
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (real)
-              f = make_float4(__fmul_rn(e4m3_to_float(pk[q] & 0xff), w), __fmul_rn(e4m3_to_float((pk[q] >> 8) & 0xff), w),
-                              __fmul_rn(e4m3_to_float((pk[q] >> 16) & 0xff), w),
-                              __fmul_rn(e4m3_to_float(pk[q] >> 24), w));
+            if (real) {
+              const float4 q8 = e4m3x4_to_float4(pk[q]);
+              f = make_float4(__fmul_rn(q8.x, w), __fmul_rn(q8.y, w), __fmul_rn(q8.z, w), __fmul_rn(q8.w, w));
+            }
             *reinterpret_cast<float4*>(row_q + 4 * q) = f;
           }
         }
