@@ -360,7 +360,7 @@ def run_sharded(args, w, rank, world, local) -> int:
 
     def step(gather=True):
         return vc_attention_sharded(q, k, v, perm, cfg, scale, gather=gather, chunk=chunk,
-                                    overlap_rounds=not args.serial_rounds)
+                                    overlap_rounds=not args.serial_rounds, transport=args.gather)
 
     for _ in range(max(3, args.warmup)):
         out = step()
@@ -482,8 +482,12 @@ def run_sharded(args, w, rank, world, local) -> int:
                        "units_per_rank": n_mine,
                        "parallelism": (f"(batch, head) units over {world} ranks (strong scaling), dealt in "
                                        f"{rounds} rounds of {chunk} per rank, prepared once per rank; each "
-                                       f"round's NCCL all-gather of the bf16 output (high-priority stream: "
-                                       f"{not args.nccl_normal_priority}) overlaps the next round's attention "
+                                       + (f"round's bf16 output slice pushed to every peer's symmetric-memory "
+                                          f"buffer by copy-engine copies (no SMs), one NCCL all-reduce at the end"
+                                          if args.gather == "peer" else
+                                          f"round's NCCL all-gather of the bf16 output (high-priority stream: "
+                                          f"{not args.nccl_normal_priority})")
+                                       + f"; overlaps the next round's attention "
                                        f"(rounds on two streams: {not args.serial_rounds})"
                                        if world > 1 else "one GPU"),
                        "l2": "inputs larger than L2"},
@@ -534,6 +538,9 @@ def main() -> int:
     ap.add_argument("--serial-rounds", action="store_true",
                     help="N > 1: rounds in order on one stream (default: two alternating streams)")
     ap.add_argument("--nccl-normal-priority", action="store_true", help="N > 1: NCCL on a normal-priority stream")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: output all-gather by copy-engine pushes into the peers' symmetric-memory "
+                         "buffers (peer) or by one NCCL all-gather per round (nccl)")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, PSNR or CPU baseline): the command profiled by ncu")
     args = ap.parse_args()

@@ -23,6 +23,16 @@ Two layouts:
   attention leaves idle or as attention CTAs retire: a high-priority NCCL
   stream makes the waiting NCCL CTAs take those SMs first.
 
+With ``transport="peer"`` (CUDA, chunked layout) the gather uses no SMs:
+the full output lives in symmetric memory (every rank maps every other
+rank's buffer), each round's attention writes straight into the rank's own
+slice of it, and a copy stream pushes that slice into every peer's buffer
+with device-to-device copies, which the copy engines carry over NVLink while
+the next rounds compute.  One small NCCL all-reduce after the pushes tells
+every rank that all slices have arrived.  The returned tensor is then that
+persistent buffer (one per shape and group), which the next call of the same
+shape overwrites.
+
 Padding units (past U) are never computed; their output rows are zeros in
 the padded buffer and are never returned.
 """
@@ -78,6 +88,40 @@ def _round_streams(dev: torch.device):
     return _ROUND_STREAMS[key]
 
 
+_COPY_STREAMS = {}
+_PEER_BUFFERS = {}
+
+
+def _copy_stream(dev: torch.device):
+    """The stream that pushes a rank's round slices to its peers."""
+    key = dev.index
+    if key not in _COPY_STREAMS:
+        _COPY_STREAMS[key] = torch.cuda.Stream(dev)
+    return _COPY_STREAMS[key]
+
+
+def _peer_output(shape, dtype, device, group):
+    """(this rank's buffer, every rank's buffer as mapped here) of one output
+    shape in symmetric memory, made once per (shape, dtype, device, group) by a
+    rendezvous of all ranks of the group."""
+    import os
+
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm
+    # plain peer mappings only: the pushes are copy-engine copies, and a
+    # buffer bound to an NVLink multicast object is not needed (nor wanted
+    # when a rank can end while its peers still hold the mapping)
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+    pg = group if group is not None else dist.group.WORLD
+    key = (tuple(shape), dtype, device.index, pg.group_name)
+    if key not in _PEER_BUFFERS:
+        buf = symm.empty(*shape, dtype=dtype, device=device)
+        hdl = symm.rendezvous(buf, pg)
+        views = [buf if r == hdl.rank else hdl.get_buffer(r, tuple(shape), dtype) for r in range(hdl.world_size)]
+        _PEER_BUFFERS[key] = (buf, views, hdl)
+    return _PEER_BUFFERS[key][:2]
+
+
 def _compute_units(q, k, v, perm, lo, hi, compute, dst, cfg=None, scale=None):
     """Attention of units [lo, hi), written to ``dst`` (hi - lo, N, D): by
     ``compute`` when given (tests), else by the CUDA kernels straight into
@@ -100,7 +144,8 @@ def _compute_units(q, k, v, perm, lo, hi, compute, dst, cfg=None, scale=None):
 def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                          perm: Optional[torch.Tensor] = None, cfg=None, scale: Optional[float] = None,
                          group=None, gather: bool = True, chunk: Optional[int] = None,
-                         compute: Optional[Callable] = None, overlap_rounds: bool = True) -> torch.Tensor:
+                         compute: Optional[Callable] = None, overlap_rounds: bool = True,
+                         transport: str = "nccl") -> torch.Tensor:
     """VC-Attention over this rank's (b, h) units, optionally all-gathered.
 
     q, k, v: (B, H, N, D), the same full tensors on every rank (views are
@@ -120,6 +165,10 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     retire, which is prompt when the process group's NCCL stream has high
     priority (``ProcessGroupNCCL.Options.is_high_priority_stream``).  Without
     it the rounds run in order on the caller's stream.
+    ``transport``: "nccl" (an all-gather per round) or "peer" (CUDA tensors
+    and the chunked layout with ``gather``: copy-engine pushes into the
+    peers' symmetric-memory buffers, see the module notes; the result is a
+    persistent buffer that the next call of the same shape overwrites).
     """
     import torch.distributed as dist
 
@@ -145,7 +194,14 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         return full[:units].reshape(b, h, n, d)
 
     rounds = -(-units // (world * chunk))
-    full = torch.empty((rounds * world * chunk, n, d), dtype=q.dtype, device=q.device) if gather else None
+    if transport not in ("nccl", "peer"):
+        raise ValueError(f"transport must be 'nccl' or 'peer', got {transport!r}")
+    peer = transport == "peer" and gather and q.is_cuda and compute is None
+    if peer:
+        full, views = _peer_output((rounds * world * chunk, n, d), q.dtype, q.device, group)
+        cstream = _copy_stream(q.device)
+    else:
+        full = torch.empty((rounds * world * chunk, n, d), dtype=q.dtype, device=q.device) if gather else None
     mine = []
     works = []
     cur = torch.cuda.current_stream(q.device) if q.is_cuda else None
@@ -160,7 +216,10 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         hi = min(units, lo + chunk)
         ctx = torch.cuda.stream(streams[i % 2]) if streams is not None else _nullctx()
         with ctx:
-            slab = torch.empty((chunk, n, d), dtype=q.dtype, device=q.device)
+            if peer:
+                slab = full[base + rank * chunk: base + (rank + 1) * chunk]
+            else:
+                slab = torch.empty((chunk, n, d), dtype=q.dtype, device=q.device)
             slab[max(0, hi - lo):].zero_()
             if hi > lo:
                 if preps is None:
@@ -172,16 +231,34 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                     attention_prepared(preps(i), n, slab[: hi - lo].unsqueeze(0), scale if scale else d ** -0.5,
                                        _call_config(cfg, d), kv_split=1)
                 mine.append(slab[: hi - lo])
-            if gather:
+            if peer:
+                done = torch.cuda.Event()
+                done.record()
+            elif gather:
                 # every rank issues every round, in the same order, with equal
                 # slabs; NCCL orders the transfer after this round's compute
                 works.append((dist.all_gather_into_tensor(full[base: base + world * chunk], slab, group=group,
                                                           async_op=True), slab))
+        if peer:
+            # push this round's slice into every peer's buffer (contiguous
+            # device-to-device copies: copy engines over NVLink, no SMs)
+            cstream.wait_event(done)
+            with torch.cuda.stream(cstream):
+                lo_r, hi_r = base + rank * chunk, base + (rank + 1) * chunk
+                for r in range(world):
+                    if r != rank:
+                        views[r][lo_r:hi_r].copy_(slab)
     for w, _ in works:
         w.wait()
     if streams is not None:
         for st in streams:
             cur.wait_stream(st)
+    if peer:
+        # every rank's pushes are done once every rank has reached this
+        # all-reduce (each enters it after its own copy stream drained)
+        cur.wait_stream(cstream)
+        flag = torch.zeros(1, dtype=torch.float32, device=q.device)
+        dist.all_reduce(flag, group=group)
     if not gather:
         return torch.cat(mine, 0) if mine else torch.zeros((0, n, d), dtype=q.dtype, device=q.device)
     return full[:units].reshape(b, h, n, d)

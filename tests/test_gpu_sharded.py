@@ -1,5 +1,7 @@
 """Multi-GPU (batch, head) sharding on real GPUs: the all-gathered output of
-vc_attention_sharded equals single-GPU calls of every unit, bit for bit.
+vc_attention_sharded equals single-GPU calls of every unit, bit for bit, with
+the NCCL all-gathers and with the copy-engine pushes into symmetric memory
+(twice in a row: the second call reuses the persistent buffer).
 
 Runs as two spawned ranks over NCCL when two GPUs are visible; skipped
 otherwise (the host-side partition logic is covered on CPU by
@@ -48,8 +50,9 @@ def _rank_main(rank, world, port, result_dir):
         perm = torch.stack([torch.from_numpy(np.random.default_rng(50 + i).permutation(n)) for i in range(g)])
         perm = perm.to(torch.int32).to(dev)
         cfg = TritonConfig(block_n=128, enable_expcast=True)
-        for chunk in (None, 3):
-            full = vc_attention_sharded(q, k, v, perm, cfg, d ** -0.5, gather=True, chunk=chunk)
+        for chunk, transport in ((None, "nccl"), (3, "nccl"), (3, "peer"), (3, "peer")):
+            full = vc_attention_sharded(q, k, v, perm, cfg, d ** -0.5, gather=True, chunk=chunk,
+                                        transport=transport)
             torch.cuda.synchronize()
             for u in range(g):
                 ref = vc_attention_cuda(q.reshape(g, n, d)[u:u + 1].unsqueeze(0),
@@ -58,7 +61,7 @@ def _rank_main(rank, world, port, result_dir):
                                         d ** -0.5)
                 if not torch.equal(ref.reshape(n, d), full.reshape(g, n, d)[u]):
                     ok = False
-                    msg += f"chunk={chunk} unit {u} differs; "
+                    msg += f"chunk={chunk} {transport} unit {u} differs; "
         if attention_status() != (0, 0, 0):
             ok = False
             msg += "device status set; "
