@@ -172,6 +172,8 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     """
     import torch.distributed as dist
 
+    if transport not in ("nccl", "peer"):
+        raise ValueError(f"transport must be 'nccl' or 'peer', got {transport!r}")
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     b, h, n, d = q.shape
@@ -194,8 +196,6 @@ def vc_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         return full[:units].reshape(b, h, n, d)
 
     rounds = -(-units // (world * chunk))
-    if transport not in ("nccl", "peer"):
-        raise ValueError(f"transport must be 'nccl' or 'peer', got {transport!r}")
     peer = transport == "peer" and gather and q.is_cuda and compute is None
     if peer:
         full, views = _peer_output((rounds * world * chunk, n, d), q.dtype, q.device, group)

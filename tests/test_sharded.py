@@ -50,7 +50,7 @@ def _stand_in(ql, kl, vl, pl):
     return out
 
 
-def _worker(rank, world, port, b, h, n, d, with_perm, ret, chunk=None):
+def _worker(rank, world, port, b, h, n, d, with_perm, ret, chunk=None, transport="nccl"):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -61,11 +61,12 @@ def _worker(rank, world, port, b, h, n, d, with_perm, ret, chunk=None):
         k = torch.randn(b, h, n, d, generator=g)
         v = torch.randn(b, h, n, d, generator=g)
         perm = torch.stack([torch.randperm(n, generator=g) for _ in range(b * h)]).int() if with_perm else None
-        full = vc_attention_sharded(q, k, v, perm, compute=_stand_in, chunk=chunk)
+        full = vc_attention_sharded(q, k, v, perm, compute=_stand_in, chunk=chunk, transport=transport)
         ref = _stand_in(q.reshape(1, b * h, n, d), k.reshape(1, b * h, n, d), v.reshape(1, b * h, n, d),
                         perm).reshape(b, h, n, d)
         ok = torch.equal(full, ref)
-        part = vc_attention_sharded(q, k, v, perm, compute=_stand_in, gather=False, chunk=chunk)
+        part = vc_attention_sharded(q, k, v, perm, compute=_stand_in, gather=False, chunk=chunk,
+                                    transport=transport)
         flat = ref.reshape(b * h, n, d)
         mine = [flat[lo:hi] for lo, hi in rank_units(b * h, world, rank, chunk)]
         want = torch.cat(mine, 0) if mine else flat[:0]
@@ -83,14 +84,18 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("b,h,with_perm,chunk", [(2, 3, True, None), (1, 5, False, None), (2, 4, True, None),
-                                                 (2, 3, True, 1), (1, 5, False, 2), (2, 4, True, 3)])
-def test_sharded_gather_matches_unsharded(b, h, with_perm, chunk):
+@pytest.mark.parametrize("b,h,with_perm,chunk,transport", [
+    (2, 3, True, None, "nccl"), (1, 5, False, None, "nccl"), (2, 4, True, None, "nccl"),
+    (2, 3, True, 1, "nccl"), (1, 5, False, 2, "nccl"), (2, 4, True, 3, "nccl"),
+    # the copy-engine transport needs CUDA tensors: host tensors (and the
+    # test stand-in) take the collective all-gather with the same layout
+    (2, 4, True, 3, "peer")])
+def test_sharded_gather_matches_unsharded(b, h, with_perm, chunk, transport):
     world = 2
     ctx = mp.get_context("spawn")
     ret = ctx.Array("i", [0] * world)
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, b, h, 16, 8, with_perm, ret, chunk))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, b, h, 16, 8, with_perm, ret, chunk, transport))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -98,3 +103,12 @@ def test_sharded_gather_matches_unsharded(b, h, with_perm, chunk):
         p.join(timeout=120)
         assert p.exitcode == 0
     assert list(ret) == [1] * world
+
+
+def test_unknown_transport_is_refused():
+    q = torch.zeros(1, 2, 4, 8)
+    with pytest.raises(ValueError, match="transport"):
+        # checked before anything runs, with or without a process group
+        import torch.distributed as dist
+        assert not dist.is_initialized()
+        vc_attention_sharded(q, q, q, None, compute=_stand_in, chunk=1, transport="ring")
