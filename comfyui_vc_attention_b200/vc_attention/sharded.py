@@ -30,8 +30,8 @@ slice of it, and a copy stream pushes that slice into every peer's buffer
 with device-to-device copies, which the copy engines carry over NVLink while
 the next rounds compute.  One small NCCL all-reduce after the pushes tells
 every rank that all slices have arrived.  The returned tensor is then that
-persistent buffer (one per shape and group), which the next call of the same
-shape overwrites.
+persistent buffer (one per shape, dtype, device and group, held until the
+process exits), which the next call of the same shape overwrites.
 
 Padding units (past U) are never computed; their output rows are zeros in
 the padded buffer and are never returned.
