@@ -358,9 +358,26 @@ def run_sharded(args, w, rank, world, local) -> int:
                        tau=w.get("tau", 1.3), qk_fp4=w.get("qk_fp4", False))
     scale = D ** -0.5
 
+    transport, transport_note = args.gather, None
+    if world > 1 and transport == "peer":
+        # the symmetric-memory rendezvous happens on the first call; if it
+        # raises on any rank, every rank takes the NCCL gathers instead
+        ok = 1.0
+        try:
+            vc_attention_sharded(q, k, v, perm, cfg, scale, gather=True, chunk=chunk,
+                                 overlap_rounds=not args.serial_rounds, transport="peer")
+            torch.cuda.synchronize()
+        except Exception as e:  # reported in the JSON line
+            ok, transport_note = 0.0, f"peer transport unavailable ({type(e).__name__}: {str(e)[:160]})"
+        flag = torch.tensor([ok], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if float(flag.item()) < 1.0:
+            transport = "nccl"
+            transport_note = transport_note or "peer transport failed on another rank"
+
     def step(gather=True):
         return vc_attention_sharded(q, k, v, perm, cfg, scale, gather=gather, chunk=chunk,
-                                    overlap_rounds=not args.serial_rounds, transport=args.gather)
+                                    overlap_rounds=not args.serial_rounds, transport=transport)
 
     for _ in range(max(3, args.warmup)):
         out = step()
@@ -484,7 +501,7 @@ def run_sharded(args, w, rank, world, local) -> int:
                                        f"{rounds} rounds of {chunk} per rank, prepared once per rank; each "
                                        + (f"round's bf16 output slice pushed to every peer's symmetric-memory "
                                           f"buffer by copy-engine copies (no SMs), one NCCL all-reduce at the end"
-                                          if args.gather == "peer" else
+                                          if transport == "peer" else
                                           f"round's NCCL all-gather of the bf16 output (high-priority stream: "
                                           f"{not args.nccl_normal_priority})")
                                        + f"; overlaps the next round's attention "
@@ -492,6 +509,7 @@ def run_sharded(args, w, rank, world, local) -> int:
                                        if world > 1 else "one GPU"),
                        "l2": "inputs larger than L2"},
             "ms_compute": ms_compute, "ms_gather_exposed": max(0.0, ms - ms_compute), "kmeans_ms": kmeans_ms,
+            "gather_transport": transport if world > 1 else None, "gather_transport_note": transport_note,
             "host_enqueue_ms": host_ms, "cuda_graph": bool(graphs),
             "psnr_db": psnr,
             "sharded_equals_single_gpu": {"units_checked": check_units, "mismatches": mismatches,
